@@ -1,0 +1,264 @@
+/*
+ * tendo_b200.h — C ABI of libtendo_b200.so, the B200 (sm_100a) kernels for
+ * tendo's int8-quantized Llama inference path.
+ *
+ * Conventions (those of tendo's popcorn binding, cuda/popcorn.go:21-37):
+ *  - every entry point returns a tb_status_t, TB_SUCCESS == 0;
+ *  - tb_get_error_string(status) names a status; after TB_ERROR_CUDA,
+ *    tb_get_last_cuda_error_string() holds the CUDA error text;
+ *  - all tensor arguments are device pointers to contiguous row-major
+ *    arrays, unless a parameter says "host";
+ *  - kernels run on the stream passed in (NULL = legacy default stream) and
+ *    on the device that is current on the calling thread;
+ *  - the op entry points allocate nothing: output and workspace buffers come
+ *    from the caller, who owns every buffer.
+ * Only the tb_model_* engine allocates, once, at creation.
+ */
+#ifndef TENDO_B200_H
+#define TENDO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(TB_BUILDING_LIBRARY)
+#define TB_API __attribute__((visibility("default")))
+#else
+#define TB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tb_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  TB_SUCCESS = 0,
+  TB_ERROR_INVALID_ARGUMENT = 1, /* bad size, null pointer, misaligned buffer */
+  TB_ERROR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+  TB_ERROR_NOT_SUPPORTED = 3,    /* valid request this build does not handle */
+  TB_ERROR_OUT_OF_MEMORY = 4,    /* engine allocation failed */
+  TB_ERROR_TIMEOUT = 5,          /* a bounded device-side wait gave up */
+  TB_ERROR_INJECTED = 6          /* host-side fault injection (TENDO_B200_INJECT) */
+} tb_status_t;
+
+/* popcornGetErrorString (cuda/popcorn.go:25). */
+TB_API const char* tb_get_error_string(tb_status_t status);
+/* popcornGetLastCudaErrorString (cuda/popcorn.go:28); per calling thread. */
+TB_API const char* tb_get_last_cuda_error_string(void);
+/* Library version, major * 10000 + minor * 100 + patch. */
+TB_API int tb_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Quantization (nn/quantize.go)
+ * ------------------------------------------------------------------------- */
+
+/* Symmetric absmax int8 quantization of w[N, K] (fp32): replaces the host
+ * loops of nn.Quantize -> quantizePerChannel (nn/quantize.go:42-124) and
+ * quantizePerGroup (nn/quantize.go:126-187).  group_size 0 = per output
+ * channel (scale[N]); otherwise scale[N, K / group_size].  q and scale are
+ * bit-identical to the reference: scale = maxAbs / 127 (1 when 0),
+ * q = clamp(round_half_away(w / scale), -128, 127). */
+TB_API tb_status_t tb_quantize_i8_f32(int8_t* q, float* scale, const float* w, int64_t N, int64_t K,
+                               int64_t group_size, tb_stream_t stream);
+
+/* Packs the reference's float32-coded q values ("stored as float32 but values
+ * are int8 range", nn/quantize.go:68) into int8.  Values must be integers in
+ * [-128, 127]; anything else sets *bad_count (device int32, may be NULL). */
+TB_API tb_status_t tb_pack_q_f32_to_i8(int8_t* q, const float* q_f32, int64_t n, int32_t* bad_count,
+                                tb_stream_t stream);
+
+/* QuantizedTensor.Dequantize (nn/quantize.go:191-229): w = q * scale. */
+TB_API tb_status_t tb_dequantize_i8_f32(float* w, const int8_t* q, const float* scale, int64_t N, int64_t K,
+                                 int64_t group_size, tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Quantized Linear (nn/quantize.go:251-312)
+ * ------------------------------------------------------------------------- */
+
+/* out[M, N] = x[M, K] @ dequantize(q[N, K], scale)^T, fp32 in and out.
+ * Replaces popcornDequantizeMatmul_i8f32 (cuda/popcorn.go:1306-1315, per
+ * channel) and popcornDequantizeMatmulGrouped_i8f32 (cuda/popcorn.go:1353-1363,
+ * group_size > 0), reached from cuda.Backend.DequantizeMatmul
+ * (cuda/backend.go:676-721).  M <= 32 runs the fused-dequant int8 GEMV;
+ * larger M runs the tensor-core GEMM (int8 tiles widened to bf16 in shared
+ * memory, fp32 accumulation), x carried as a bf16 hi + lo pair so the result
+ * stays within 1e-3 of the fp32 path. */
+TB_API tb_status_t tb_dequant_matmul_i8f32(float* out, const float* x, const int8_t* q, const float* scale,
+                                    int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                    tb_stream_t stream);
+
+/* Precision modes of the tensor-core GEMM (M > 32). */
+typedef enum {
+  TB_GEMM_BF16X2 = 0, /* x = hi + lo bf16 pair, two MMAs: ~fp32 accuracy (default) */
+  TB_GEMM_BF16 = 1,   /* x rounded once to bf16, one MMA: 1e-2 class accuracy */
+  TB_GEMM_SIMT = 2    /* fp32 CUDA-core tiles (no tensor cores) */
+} tb_gemm_mode_t;
+
+/* tb_dequant_matmul_i8f32 with the GEMM mode chosen by the caller (used for
+ * M > 32; M <= 32 always takes the GEMV). */
+TB_API tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, const int8_t* q, const float* scale,
+                                         int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                         tb_gemm_mode_t mode, tb_stream_t stream);
+
+/* out[M, N] = a[M, K] @ b[N, K]^T in fp32: the fp32 lm_head projection
+ * (models/llama/quantized.go:164-172, cuBLAS SGEMM in cuda/ops.go:182-330). */
+TB_API tb_status_t tb_matmul_nt_f32(float* out, const float* a, const float* b, int64_t M, int64_t N, int64_t K,
+                             tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Norm, activation, elementwise (cpu/backend.go; cuda/popcorn.go; cuDNN)
+ * ------------------------------------------------------------------------- */
+
+/* popcornRMSNorm_f32 (cuda/popcorn.go:615-623): out = x / sqrt(mean(x^2) + eps)
+ * * weight over the last norm_size elements of n rows; weight may be NULL.
+ * residual != NULL fuses the residual add first: x = in + residual, and x is
+ * also written to residual_out (may alias residual). */
+TB_API tb_status_t tb_rmsnorm_f32(float* out, const float* in, const float* weight, int64_t n, int64_t norm_size,
+                           float eps, tb_stream_t stream);
+TB_API tb_status_t tb_add_rmsnorm_f32(float* out, float* residual_out, const float* in, const float* residual,
+                               const float* weight, int64_t n, int64_t norm_size, float eps,
+                               tb_stream_t stream);
+
+/* SiLU (cuDNN swish, cuda/ops.go:14-86; cpu/backend.go:193-198). */
+TB_API tb_status_t tb_silu_f32(float* out, const float* in, int64_t n, tb_stream_t stream);
+/* SwiGLU glue: out = silu(gate) * up (models/llama/quantized.go:392-404). */
+TB_API tb_status_t tb_silu_mul_f32(float* out, const float* gate, const float* up, int64_t n, tb_stream_t stream);
+/* Residual Add (models/llama/quantized.go:199, :219; cudnnOpTensor). */
+TB_API tb_status_t tb_add_f32(float* out, const float* a, const float* b, int64_t n, tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * RoPE and attention (nn/rope.go; models/llama/quantized.go:229-382)
+ * ------------------------------------------------------------------------- */
+
+/* NewRoPE tables (nn/rope.go:22-52), computed on the HOST into host arrays
+ * cos_t/sin_t [max_seq, dim / 2] with fp64 pow/cos/sin as the reference does. */
+TB_API tb_status_t tb_rope_tables_host(float* cos_t, float* sin_t, int dim, int max_seq, float base);
+
+/* RoPE.Apply / rotateHalf (nn/rope.go:102-197) on x[B, Hx, S, D] (contiguous),
+ * positions pos_offset .. pos_offset + S - 1; out may alias x. */
+TB_API tb_status_t tb_rope_apply_f32(float* out, const float* x, const float* cos_t, const float* sin_t, int64_t B,
+                              int64_t Hx, int64_t S, int64_t D, int64_t pos_offset, int64_t max_seq,
+                              tb_stream_t stream);
+
+/* KV-cache append (the Cat along dim 2 of models/llama/quantized.go:282-299,
+ * popcornCat_f32 cuda/popcorn.go:1077-1085) done in place, with RoPE fused on
+ * k.  k, v: [B, S, Hkv, D] projections (the layout the Linear writes);
+ * kcache, vcache: [B, Hkv, max_seq, D]; positions pos .. pos + S - 1. */
+TB_API tb_status_t tb_kv_append_rope_f32(float* kcache, float* vcache, const float* k, const float* v,
+                                  const float* cos_t, const float* sin_t, int64_t B, int64_t Hkv, int64_t S,
+                                  int64_t D, int64_t pos, int64_t max_seq, tb_stream_t stream);
+
+/* Scaled-dot-product attention over the cache: scores = (q . k) * scale,
+ * causal mask keeps key j for query i when j <= i + (Sk - Sq), softmax over
+ * keys, then P . V (models/llama/quantized.go:319-372, forward.go:345-417).
+ * q: [B, Sq, H, D] (post-RoPE, the projection layout), caches
+ * [B, Hkv, max_seq, D] holding Sk valid positions; GQA maps query head h to
+ * kv head h / (H / Hkv).  out: [B, Sq, H, D].  Sq == 1 runs the split-K
+ * decode kernel, which needs `workspace` of tb_attention_workspace_size()
+ * bytes (device memory owned by the caller; its contents need not be zero).
+ * Calls that share a workspace must not overlap on the GPU. */
+TB_API size_t tb_attention_workspace_size(int64_t B, int64_t H, int64_t Sq, int64_t D, int64_t max_seq);
+TB_API tb_status_t tb_attention_f32(float* out, const float* q, const float* kcache, const float* vcache, int64_t B,
+                             int64_t H, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int64_t max_seq,
+                             float scale, void* workspace, size_t workspace_bytes, tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Embedding and sampling
+ * ------------------------------------------------------------------------- */
+
+/* popcornEmbedding_f32 (cuda/popcorn.go:980-988): out[i, :] = table[ids[i], :].
+ * Out-of-range ids produce zero rows and set *bad_count (device int32, may be
+ * NULL) — the Go CPU path panics there. */
+TB_API tb_status_t tb_embedding_f32(float* out, const float* table, const int64_t* ids, int64_t n, int64_t vocab,
+                             int64_t dim, int32_t* bad_count, tb_stream_t stream);
+
+/* popcornArgMax_f32 (cuda/popcorn.go:458-464) with models.Greedy's tie rule
+ * (models/sampling.go:73-83, first index of the maximum): out_idx[r] for each
+ * of `rows` rows of length n. */
+TB_API tb_status_t tb_argmax_f32(int64_t* out_idx, const float* x, int64_t rows, int64_t n, tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Synthetic workload generator (include/tendo_synth.h), on the device
+ * ------------------------------------------------------------------------- */
+
+/* w[N, K] with w[n, k] = N(0, std) draw n*K + k of (seed, stream), fp32. */
+TB_API tb_status_t tb_synth_normal_f32(float* w, int64_t N, int64_t K, uint64_t seed, uint64_t stream_id, double std_,
+                                tb_stream_t stream);
+/* Generates and quantizes per channel in one pass (no fp32 copy kept):
+ * the device form of nn.Quantize applied to tb_synth_normal_f32's matrix. */
+TB_API tb_status_t tb_synth_quantized_i8(int8_t* q, float* scale, int64_t N, int64_t K, uint64_t seed,
+                                  uint64_t stream_id, double std_, tb_stream_t stream);
+/* Host: n uniform token ids in [0, vocab) of (seed, TS_STREAM_PROMPT). */
+TB_API tb_status_t tb_synth_tokens_host(int64_t* ids, int64_t n, int64_t vocab, uint64_t seed);
+
+/* ---------------------------------------------------------------------------
+ * Model engine: QuantizedModel (models/llama/quantized.go:13-477)
+ * ------------------------------------------------------------------------- */
+
+typedef struct {
+  int32_t vocab, dim, layers, heads, kv_heads, hidden, max_seq;
+  float rope_base, eps;
+  int32_t max_batch; /* sequences decoded in lockstep */
+} tb_model_config;
+
+typedef struct tb_model tb_model;
+
+/* Allocates weights, KV cache and work buffers on `device`. */
+TB_API tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device);
+TB_API tb_status_t tb_model_destroy(tb_model* m);
+/* Synthetic weights: N(0, 0.02) from (seed, stream = layer * 8 + matrix),
+ * quantized per channel on the device; gains 1.0; embedding and lm_head fp32. */
+TB_API tb_status_t tb_model_init_synthetic(tb_model* m, uint64_t seed);
+/* Loads one quantized Linear (mat 0..6 = q, k, v, o, gate, up, down) from
+ * HOST arrays q[N, K] int8 and scale[N]; which = 0 embedding [V, d],
+ * 1 lm_head [V, d], 2 final norm [d], 3 attn norm of `layer`, 4 mlp norm. */
+TB_API tb_status_t tb_model_set_linear(tb_model* m, int layer, int mat, const int8_t* q_host, const float* scale_host);
+TB_API tb_status_t tb_model_set_tensor(tb_model* m, int which, int layer, const float* host);
+/* Copies a tensor set by tb_model_set_tensor back to a host array. */
+TB_API tb_status_t tb_model_get_tensor(tb_model* m, int which, int layer, float* host);
+/* Copies one quantized Linear back to host arrays. */
+TB_API tb_status_t tb_model_get_linear(tb_model* m, int layer, int mat, int8_t* q_host, float* scale_host);
+/* Empties the KV cache (position 0). */
+TB_API tb_status_t tb_model_reset(tb_model* m);
+TB_API int64_t tb_model_position(const tb_model* m);
+
+/* QuantizedModel.Forward (models/llama/quantized.go:125-178) over tokens
+ * [B, S] (HOST int64) appended at the current position.  last_logits_host
+ * [B, vocab] (may be NULL) receives the last position's logits and
+ * next_host[B] (may be NULL) their greedy argmax. */
+TB_API tb_status_t tb_model_forward(tb_model* m, const int64_t* tokens_host, int64_t B, int64_t S,
+                             float* last_logits_host, int64_t* next_host);
+
+/* GenerateGreedy (models/llama/generate.go:99-150): reset, prefill with
+ * prompt[B, S] (HOST), then n_new greedy tokens into out_tokens_host[B, n_new].
+ * Each decode step is one CUDA-graph launch that reads the token and position
+ * from device memory, so only the token ids cross back to the host. */
+TB_API tb_status_t tb_model_generate_greedy(tb_model* m, const int64_t* prompt_host, int64_t B, int64_t S,
+                                     int64_t n_new, int64_t* out_tokens_host);
+
+/* Device-resident decode: runs n_steps greedy steps from the current
+ * position, feeding each argmax back as the next token, and keeps the tokens
+ * on the device (fetch them with tb_model_tokens).  `start_tokens_host` [B]
+ * (may be NULL = continue from the last token).  Asynchronous on the engine
+ * stream; tb_model_sync waits. */
+TB_API tb_status_t tb_model_decode(tb_model* m, const int64_t* start_tokens_host, int64_t n_steps);
+TB_API tb_status_t tb_model_tokens(tb_model* m, int64_t* out_host, int64_t count);
+TB_API tb_status_t tb_model_set_position(tb_model* m, int64_t pos);
+TB_API tb_status_t tb_model_sync(tb_model* m);
+/* The engine's CUDA stream (for events). */
+TB_API tb_stream_t tb_model_stream(tb_model* m);
+/* Launches one kernel of the fused decode step for `layer` on the engine
+ * stream, without graph or programmatic launch, for timing it alone: kind
+ * 0 = RMSNorm+QKV+RoPE+append GEMV, 1 = split-K attention + combine,
+ * 2 = O GEMV + residual, 3 = RMSNorm+gate/up+SwiGLU GEMV, 4 = down GEMV +
+ * residual, 5 = final RMSNorm + lm_head GEMV + argmax.  Reads and writes
+ * the engine's own buffers at the current position. */
+TB_API tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer);
+/* Kernel launches one decode step issues. */
+TB_API int64_t tb_model_launches_per_step(const tb_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TENDO_B200_H */

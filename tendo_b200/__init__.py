@@ -1,0 +1,506 @@
+"""tendo_b200 — B200 (sm_100a) kernels for tendo's int8-quantized Llama path.
+
+The product is the C ABI of ``libtendo_b200.so`` (include/tendo_b200.h).  This
+module binds it with ctypes for Python callers and tests.  It mirrors the
+tendo operator names of the path — ``DequantizeMatmul``, ``Quantize``,
+``RMSNorm``, ``SiLU``, ``Add``, ``Embedding``, ``RoPE``, attention — and the
+``QuantizedModel`` engine.  PyTorch is used only for device memory and
+streams: every op runs a kernel of this library, and there is no CPU or
+PyTorch fallback; a missing library raises at import time.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtendo_b200.so")
+
+TB_SUCCESS = 0
+TB_ERROR_INVALID_ARGUMENT = 1
+TB_ERROR_CUDA = 2
+TB_ERROR_NOT_SUPPORTED = 3
+TB_ERROR_OUT_OF_MEMORY = 4
+TB_ERROR_TIMEOUT = 5
+TB_ERROR_INJECTED = 6
+
+TB_GEMM_BF16X2 = 0
+TB_GEMM_BF16 = 1
+TB_GEMM_SIMT = 2
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_f32 = ctypes.c_float
+_st = ctypes.c_int
+
+# (name, restype, argtypes) of every exported entry point of include/tendo_b200.h
+SIGNATURES = [
+    ("tb_get_error_string", ctypes.c_char_p, [_st]),
+    ("tb_get_last_cuda_error_string", ctypes.c_char_p, []),
+    ("tb_version", ctypes.c_int, []),
+    ("tb_quantize_i8_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("tb_pack_q_f32_to_i8", _st, [_vp, _vp, _i64, _vp, _vp]),
+    ("tb_dequantize_i8_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("tb_dequant_matmul_i8f32", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    ("tb_dequant_matmul_i8f32_mode", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _st, _vp]),
+    ("tb_matmul_nt_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("tb_rmsnorm_f32", _st, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    ("tb_add_rmsnorm_f32", _st, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    ("tb_silu_f32", _st, [_vp, _vp, _i64, _vp]),
+    ("tb_silu_mul_f32", _st, [_vp, _vp, _vp, _i64, _vp]),
+    ("tb_add_f32", _st, [_vp, _vp, _vp, _i64, _vp]),
+    ("tb_rope_tables_host", _st, [_vp, _vp, ctypes.c_int, ctypes.c_int, _f32]),
+    ("tb_rope_apply_f32", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    ("tb_kv_append_rope_f32", _st, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    ("tb_attention_workspace_size", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
+    ("tb_attention_f32", _st,
+     [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, ctypes.c_size_t, _vp]),
+    ("tb_embedding_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    ("tb_argmax_f32", _st, [_vp, _vp, _i64, _i64, _vp]),
+    ("tb_synth_normal_f32", _st, [_vp, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, _vp]),
+    ("tb_synth_quantized_i8", _st,
+     [_vp, _vp, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, _vp]),
+    ("tb_synth_tokens_host", _st, [_vp, _i64, _i64, ctypes.c_uint64]),
+    ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
+    ("tb_model_destroy", _st, [_vp]),
+    ("tb_model_init_synthetic", _st, [_vp, ctypes.c_uint64]),
+    ("tb_model_set_linear", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    ("tb_model_set_tensor", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("tb_model_get_linear", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    ("tb_model_get_tensor", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("tb_model_bench_kernel", _st, [_vp, ctypes.c_int, ctypes.c_int]),
+    ("tb_model_reset", _st, [_vp]),
+    ("tb_model_position", _i64, [_vp]),
+    ("tb_model_forward", _st, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    ("tb_model_generate_greedy", _st, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    ("tb_model_decode", _st, [_vp, _vp, _i64]),
+    ("tb_model_tokens", _st, [_vp, _vp, _i64]),
+    ("tb_model_set_position", _st, [_vp, _i64]),
+    ("tb_model_sync", _st, [_vp]),
+    ("tb_model_stream", _vp, [_vp]),
+    ("tb_model_launches_per_step", _i64, [_vp]),
+]
+
+
+class TendoB200Error(RuntimeError):
+    """Mirror of tendo's cuda.CUDAError{Code, Message} (cuda/types.go:7-15)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"tendo_b200: {message} (status {code})")
+        self.code = code
+        self.message = message
+
+
+class ShapeError(ValueError):
+    """Mirror of tendo.ShapeError (ops.go:232-248)."""
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m tendo_b200.build` (there is no fallback path)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, res, args in SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def check(status: int) -> None:
+    if status != TB_SUCCESS:
+        msg = lib.tb_get_error_string(status).decode()
+        if status == TB_ERROR_CUDA:
+            detail = lib.tb_get_last_cuda_error_string().decode()
+            if detail:
+                msg = f"{msg}: {detail}"
+        raise TendoB200Error(status, msg)
+
+
+# ---------------------------------------------------------------------------
+# torch plumbing
+# ---------------------------------------------------------------------------
+def _torch():
+    import torch
+
+    return torch
+
+
+def _ptr(t) -> int:
+    return t.data_ptr() if t is not None else None
+
+
+def _stream(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ShapeError("tendo_b200 ops take CUDA tensors (DeviceError in tendo terms)")
+        if t is not None and not t.is_contiguous():
+            raise ShapeError("tendo_b200 ops take contiguous tensors")
+
+
+@dataclass
+class QuantizedTensor:
+    """nn.QuantizedTensor (nn/quantize.go:22-37) with int8 storage."""
+
+    data: object  # torch.int8 [N, K]
+    scale: object  # torch.float32 [N] or [N, K / group]
+    shape: tuple
+    group_size: int = 0
+
+
+class Backend:
+    """The ops of tendo's quantized Llama path on this library's kernels.
+
+    Method names and argument meaning follow tendo's Backend interfaces
+    (api.go:81-318, nn/quantize.go:251-258, models/llama/forward.go:13-27);
+    each call returns a new tensor, as every tendo op does.
+    """
+
+    def __init__(self, device: int = 0):
+        self.device = device
+
+    # nn/quantize.go:42-187
+    def Quantize(self, weight, group_size: int = 0) -> QuantizedTensor:
+        torch = _torch()
+        _need_cuda(weight)
+        if weight.dim() != 2:
+            raise ShapeError(f"nn.Quantize: weight must be 2D, got {weight.dim()}D")
+        N, K = weight.shape
+        if group_size and K % group_size:
+            raise ShapeError(f"nn.Quantize: in_features {K} not divisible by group_size {group_size}")
+        q = torch.empty((N, K), dtype=torch.int8, device=weight.device)
+        s = torch.empty((N, K // group_size) if group_size else (N,), dtype=torch.float32, device=weight.device)
+        check(lib.tb_quantize_i8_f32(_ptr(q), _ptr(s), _ptr(weight), N, K, group_size, _stream()))
+        return QuantizedTensor(q, s, (N, K), group_size)
+
+    # nn/quantize.go:191-229
+    def Dequantize(self, qt: QuantizedTensor):
+        torch = _torch()
+        N, K = qt.shape
+        w = torch.empty((N, K), dtype=torch.float32, device=qt.data.device)
+        check(lib.tb_dequantize_i8_f32(_ptr(w), _ptr(qt.data), _ptr(qt.scale), N, K, qt.group_size, _stream()))
+        return w
+
+    def PackQ(self, q_f32):
+        """float32-coded q (nn/quantize.go:68) -> int8; raises on non-integer values."""
+        torch = _torch()
+        _need_cuda(q_f32)
+        q = torch.empty(q_f32.shape, dtype=torch.int8, device=q_f32.device)
+        bad = torch.zeros(1, dtype=torch.int32, device=q_f32.device)
+        check(lib.tb_pack_q_f32_to_i8(_ptr(q), _ptr(q_f32), q_f32.numel(), _ptr(bad), _stream()))
+        if int(bad.item()):
+            raise ShapeError(f"{int(bad.item())} q values are not integers in [-128, 127]")
+        return q
+
+    # nn.QuantizedLinearBackend.DequantizeMatmul (nn/quantize.go:251-258; cuda/backend.go:676-721)
+    def DequantizeMatmul(self, x, qweight, scale, group_size: int = 0, mode: int = TB_GEMM_BF16X2):
+        torch = _torch()
+        _need_cuda(x, qweight, scale)
+        K = x.shape[-1]
+        N = qweight.shape[0]
+        if qweight.dim() != 2 or qweight.shape[1] != K:
+            raise ShapeError(f"dequantize matmul: x [..., {K}] vs qweight {tuple(qweight.shape)}")
+        if qweight.dtype != torch.int8:
+            qweight = self.PackQ(qweight.contiguous())
+        M = x.numel() // K if K else 0
+        out = torch.empty((*x.shape[:-1], N), dtype=torch.float32, device=x.device)
+        check(lib.tb_dequant_matmul_i8f32_mode(_ptr(out), _ptr(x), _ptr(qweight), _ptr(scale), M, N, K, group_size,
+                                               mode, _stream()))
+        return out
+
+    def MatMulNT(self, a, b):
+        """a @ b^T in fp32 (the lm_head projection)."""
+        torch = _torch()
+        _need_cuda(a, b)
+        M, K = a.shape
+        N = b.shape[0]
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+        check(lib.tb_matmul_nt_f32(_ptr(out), _ptr(a), _ptr(b), M, N, K, _stream()))
+        return out
+
+    # NormOps.RMSNorm (api.go; cpu/backend.go:606-652)
+    def RMSNorm(self, x, normalized_shape, weight, eps: float):
+        torch = _torch()
+        _need_cuda(x, weight)
+        ns = 1
+        for d in normalized_shape:
+            ns *= d
+        out = torch.empty_like(x)
+        check(lib.tb_rmsnorm_f32(_ptr(out), _ptr(x), _ptr(weight), x.numel() // ns, ns, eps, _stream()))
+        return out
+
+    def AddRMSNorm(self, x, residual, weight, eps: float):
+        """(residual + x, RMSNorm(residual + x) * weight) in one pass."""
+        torch = _torch()
+        _need_cuda(x, residual, weight)
+        d = x.shape[-1]
+        out = torch.empty_like(x)
+        res = torch.empty_like(x)
+        check(lib.tb_add_rmsnorm_f32(_ptr(out), _ptr(res), _ptr(x), _ptr(residual), _ptr(weight), x.numel() // d, d,
+                                     eps, _stream()))
+        return res, out
+
+    def SiLU(self, x):
+        torch = _torch()
+        _need_cuda(x)
+        out = torch.empty_like(x)
+        check(lib.tb_silu_f32(_ptr(out), _ptr(x), x.numel(), _stream()))
+        return out
+
+    def SiLUMul(self, gate, up):
+        torch = _torch()
+        _need_cuda(gate, up)
+        out = torch.empty_like(gate)
+        check(lib.tb_silu_mul_f32(_ptr(out), _ptr(gate), _ptr(up), gate.numel(), _stream()))
+        return out
+
+    def Add(self, a, b):
+        torch = _torch()
+        _need_cuda(a, b)
+        if a.shape != b.shape:
+            raise ShapeError(f"add: shapes {tuple(a.shape)} and {tuple(b.shape)}")
+        out = torch.empty_like(a)
+        check(lib.tb_add_f32(_ptr(out), _ptr(a), _ptr(b), a.numel(), _stream()))
+        return out
+
+    # EmbeddingOps.Embedding (cpu/backend.go:1289-1339)
+    def Embedding(self, weight, indices):
+        torch = _torch()
+        _need_cuda(weight, indices)
+        V, d = weight.shape
+        out = torch.empty((*indices.shape, d), dtype=torch.float32, device=weight.device)
+        bad = torch.zeros(1, dtype=torch.int32, device=weight.device)
+        check(lib.tb_embedding_f32(_ptr(out), _ptr(weight), _ptr(indices), indices.numel(), V, d, _ptr(bad),
+                                   _stream()))
+        if int(bad.item()):
+            raise ShapeError(f"embedding: {int(bad.item())} ids outside [0, {V})")
+        return out
+
+    def ArgMax(self, x):
+        torch = _torch()
+        _need_cuda(x)
+        n = x.shape[-1]
+        out = torch.empty(x.shape[:-1], dtype=torch.int64, device=x.device)
+        check(lib.tb_argmax_f32(_ptr(out), _ptr(x), x.numel() // n, n, _stream()))
+        return out
+
+    # nn.NewRoPE / RoPE.Apply (nn/rope.go:22-197)
+    @staticmethod
+    def RoPETables(dim: int, max_seq: int, base: float):
+        import numpy as np
+
+        c = np.empty((max_seq, dim // 2), np.float32)
+        s = np.empty((max_seq, dim // 2), np.float32)
+        check(lib.tb_rope_tables_host(c.ctypes.data, s.ctypes.data, dim, max_seq, base))
+        return c, s
+
+    def RoPEApply(self, x, cos_t, sin_t, pos_offset: int):
+        """x [B, H, S, D] -> rotated copy at positions pos_offset.. (RoPE.Apply)."""
+        torch = _torch()
+        _need_cuda(x, cos_t, sin_t)
+        B, H, S, D = x.shape
+        out = torch.empty_like(x)
+        check(lib.tb_rope_apply_f32(_ptr(out), _ptr(x), _ptr(cos_t), _ptr(sin_t), B, H, S, D, pos_offset,
+                                    cos_t.shape[0], _stream()))
+        return out
+
+    def KVAppendRoPE(self, kcache, vcache, k, v, cos_t, sin_t, pos: int):
+        """Cat([cache, new], 2) done in place: k, v [B, S, Hkv, D]; caches [B, Hkv, max_seq, D]."""
+        _need_cuda(kcache, vcache, k, v, cos_t, sin_t)
+        B, S, Hkv, D = k.shape
+        check(lib.tb_kv_append_rope_f32(_ptr(kcache), _ptr(vcache), _ptr(k), _ptr(v), _ptr(cos_t), _ptr(sin_t), B,
+                                        Hkv, S, D, pos, kcache.shape[2], _stream()))
+
+    def Attention(self, q, kcache, vcache, sk: int, scale: float | None = None):
+        """q [B, Sq, H, D] over the first sk cached positions -> [B, Sq, H, D]."""
+        torch = _torch()
+        _need_cuda(q, kcache, vcache)
+        B, Sq, H, D = q.shape
+        Hkv, max_seq = kcache.shape[1], kcache.shape[2]
+        if scale is None:
+            import math
+
+            scale = float(ctypes.c_float(1.0 / ctypes.c_float(math.sqrt(D)).value).value)
+        out = torch.empty_like(q)
+        ws_bytes = lib.tb_attention_workspace_size(B, H, Sq, D, max_seq)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+        check(lib.tb_attention_f32(_ptr(out), _ptr(q), _ptr(kcache), _ptr(vcache), B, H, Hkv, Sq, sk, D, max_seq,
+                                   scale, _ptr(ws), ws_bytes, _stream()))
+        return out
+
+    # synthetic workload generator
+    def SynthNormal(self, N: int, K: int, seed: int, stream_id: int, std: float):
+        torch = _torch()
+        w = torch.empty((N, K), dtype=torch.float32, device=f"cuda:{self.device}")
+        check(lib.tb_synth_normal_f32(_ptr(w), N, K, seed, stream_id, std, _stream()))
+        return w
+
+    def SynthQuantized(self, N: int, K: int, seed: int, stream_id: int, std: float = 0.02):
+        torch = _torch()
+        q = torch.empty((N, K), dtype=torch.int8, device=f"cuda:{self.device}")
+        s = torch.empty((N,), dtype=torch.float32, device=f"cuda:{self.device}")
+        check(lib.tb_synth_quantized_i8(_ptr(q), _ptr(s), N, K, seed, stream_id, std, _stream()))
+        return q, s
+
+
+def synth_tokens(n: int, vocab: int, seed: int):
+    """Uniform prompt ids in [0, vocab) of the (seed, prompt) stream (host only)."""
+    import numpy as np
+
+    ids = np.empty(n, np.int64)
+    check(lib.tb_synth_tokens_host(ids.ctypes.data, n, vocab, seed))
+    return ids
+
+
+# Stream ids of the synthetic generator (include/tendo_synth.h).
+STREAM_EMBED = 0x7FFF0001
+STREAM_LMHEAD = 0x7FFF0002
+STREAM_PROMPT = 0x7FFF0003
+STREAM_X = 0x7FFF0004
+STREAM_W = 0x7FFF0005
+MATS_PER_LAYER = 8
+
+
+class ModelConfig(ctypes.Structure):
+    """tb_model_config: llama.Config (models/llama/config.go:5-21) plus the lockstep batch."""
+
+    _fields_ = [
+        ("vocab", ctypes.c_int32),
+        ("dim", ctypes.c_int32),
+        ("layers", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("max_seq", ctypes.c_int32),
+        ("rope_base", ctypes.c_float),
+        ("eps", ctypes.c_float),
+        ("max_batch", ctypes.c_int32),
+    ]
+
+
+class QuantizedModel:
+    """QuantizedModel (models/llama/quantized.go) on one GPU, B sequences in lockstep."""
+
+    def __init__(self, cfg: dict, batch: int = 1, device: int = 0):
+        self.cfg = dict(cfg)
+        self.B = batch
+        self.device = device
+        c = ModelConfig(cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"],
+                        cfg["max_seq"], cfg["rope_base"], cfg["eps"], batch)
+        h = ctypes.c_void_p()
+        check(lib.tb_model_create(ctypes.byref(h), ctypes.byref(c), device))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib.tb_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_synthetic(self, seed: int = 0):
+        check(lib.tb_model_init_synthetic(self.h, seed))
+
+    def set_linear(self, layer: int, mat: int, q, scale):
+        import numpy as np
+
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        scale = np.ascontiguousarray(scale, dtype=np.float32)
+        check(lib.tb_model_set_linear(self.h, layer, mat, q.ctypes.data, scale.ctypes.data))
+
+    def get_linear(self, layer: int, mat: int, shape):
+        import numpy as np
+
+        q = np.empty(shape, np.int8)
+        s = np.empty(shape[0], np.float32)
+        check(lib.tb_model_get_linear(self.h, layer, mat, q.ctypes.data, s.ctypes.data))
+        return q, s
+
+    def set_tensor(self, which: int, layer: int, host):
+        import numpy as np
+
+        a = np.ascontiguousarray(host, dtype=np.float32)
+        check(lib.tb_model_set_tensor(self.h, which, layer, a.ctypes.data))
+
+    def get_tensor(self, which: int, layer: int, shape):
+        import numpy as np
+
+        a = np.empty(shape, np.float32)
+        check(lib.tb_model_get_tensor(self.h, which, layer, a.ctypes.data))
+        return a
+
+    def bench_kernel(self, kind: int, layer: int):
+        check(lib.tb_model_bench_kernel(self.h, kind, layer))
+
+    def reset(self):
+        check(lib.tb_model_reset(self.h))
+
+    @property
+    def position(self) -> int:
+        return int(lib.tb_model_position(self.h))
+
+    def set_position(self, pos: int):
+        check(lib.tb_model_set_position(self.h, pos))
+
+    def forward(self, tokens, want_logits: bool = True):
+        """Forward of tokens [B, S] (host ints) at the current position: (last_logits [B, V], next [B])."""
+        import numpy as np
+
+        t = np.ascontiguousarray(tokens, dtype=np.int64).reshape(self.B, -1)
+        logits = np.empty((self.B, self.cfg["vocab"]), np.float32) if want_logits else None
+        nxt = np.empty(self.B, np.int64)
+        check(lib.tb_model_forward(self.h, t.ctypes.data, self.B, t.shape[1],
+                                   logits.ctypes.data if logits is not None else None, nxt.ctypes.data))
+        return logits, nxt
+
+    def generate_greedy(self, prompt, n_new: int):
+        import numpy as np
+
+        p = np.ascontiguousarray(prompt, dtype=np.int64).reshape(self.B, -1)
+        out = np.empty((self.B, n_new), np.int64)
+        check(lib.tb_model_generate_greedy(self.h, p.ctypes.data, self.B, p.shape[1], n_new, out.ctypes.data))
+        return out
+
+    def decode(self, n_steps: int, start_tokens=None):
+        import numpy as np
+
+        st = None
+        if start_tokens is not None:
+            st = np.ascontiguousarray(start_tokens, dtype=np.int64).reshape(self.B)
+        check(lib.tb_model_decode(self.h, st.ctypes.data if st is not None else None, n_steps))
+
+    def tokens(self, count: int):
+        import numpy as np
+
+        out = np.empty((count, self.B), np.int64)
+        check(lib.tb_model_tokens(self.h, out.ctypes.data, count))
+        return out
+
+    def sync(self):
+        check(lib.tb_model_sync(self.h))
+
+    @property
+    def stream_handle(self) -> int:
+        return lib.tb_model_stream(self.h) or 0
+
+    @property
+    def launches_per_step(self) -> int:
+        return int(lib.tb_model_launches_per_step(self.h))
+
+
+MAT_NAMES = ("q", "k", "v", "o", "gate", "up", "down")

@@ -1,0 +1,368 @@
+// attention.cu — KV-cache attention for the quantized Llama path
+// (models/llama/quantized.go:319-372): scores = (q . k) * (1/sqrt(D)),
+// causal mask j <= i + (Sk - Sq) (models/llama/forward.go:372-417), softmax
+// over keys, P . V; GQA reads kv head h / (H / Hkv) directly
+// (models/llama/forward.go:345-370) instead of materialising the repeat.
+//
+// Decode (Sq = 1) is HBM-bound on the fp32 cache: split-K over positions,
+// one CTA per (split, kv head, sequence) serving all H / Hkv query heads of
+// that kv head (each K/V row is read once), online softmax per warp, then a
+// combine kernel merges the splits.  Prefill is a tiled (flash-style) fp32
+// kernel with the online softmax, so no [S, S] score matrix is stored.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tb {
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<2> {
+  using T = float2;
+};
+template <>
+struct VecT<4> {
+  using T = float4;
+};
+
+template <int VEC>
+__device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
+  if constexpr (VEC == 4) {
+    float4 t = *reinterpret_cast<const float4*>(p);
+    r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+  } else {
+    float2 t = *reinterpret_cast<const float2*>(p);
+    r[0] = t.x; r[1] = t.y;
+  }
+}
+
+// grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv head.
+template <int VEC, int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArgs a) {
+  constexpr int D = VEC * 32;
+  __shared__ float sm_o[kAttnWarps][G][D];
+  __shared__ float sm_ml[kAttnWarps][G][2];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t sk = a.pos ? (*a.pos + 1) : a.sk;
+  const int64_t chunk = (sk + a.nsplit - 1) / a.nsplit;
+  const int64_t start = (int64_t)split * chunk;
+  const int64_t end = min(start + chunk, sk);
+
+  float qr[G][VEC];
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) load_vec<VEC>(qr[gi], a.q + ((size_t)b * a.H + kvh * G + gi) * D + lane * VEC);
+
+  float mx[G], l[G], o[G][VEC];
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+    mx[gi] = -INFINITY;
+    l[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; e++) o[gi][e] = 0.f;
+  }
+  const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  constexpr int U = 4;  // positions in flight per warp
+  for (int64_t j0 = start + warp; j0 < end; j0 += kAttnWarps * U) {
+    float kr[U][VEC], vr[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int64_t j = j0 + (int64_t)u * kAttnWarps;
+      if (j < end) {
+        load_vec<VEC>(kr[u], kb + j * D + lane * VEC);
+        load_vec<VEC>(vr[u], vb + j * D + lane * VEC);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int64_t j = j0 + (int64_t)u * kAttnWarps;
+      if (j >= end) break;
+#pragma unroll
+      for (int gi = 0; gi < G; gi++) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; e++) d = fmaf(qr[gi][e], kr[u][e], d);
+        d = warp_sum(d);
+        const float s = d * a.scale;
+        const float mn = fmaxf(mx[gi], s);
+        const float corr = expf(mx[gi] - mn);
+        const float p = expf(s - mn);
+        l[gi] = l[gi] * corr + p;
+#pragma unroll
+        for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e] * corr);
+        mx[gi] = mn;
+      }
+    }
+  }
+  // merge the warps of this CTA
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+#pragma unroll
+    for (int e = 0; e < VEC; e++) sm_o[warp][gi][lane * VEC + e] = o[gi][e];
+    if (lane == 0) {
+      sm_ml[warp][gi][0] = mx[gi];
+      sm_ml[warp][gi][1] = l[gi];
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < G * D; t += kAttnThreads) {
+    const int gi = t / D, e = t - gi * D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) m = fmaxf(m, sm_ml[w][gi][0]);
+    float L = 0.f, O = 0.f;
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; w++) {
+        const float c = expf(sm_ml[w][gi][0] - m);
+        L = fmaf(sm_ml[w][gi][1], c, L);
+        O = fmaf(sm_o[w][gi][e], c, O);
+      }
+    }
+    float* part = a.partial + (((size_t)b * a.H + kvh * G + gi) * a.nsplit + split) * (D + 2);
+    part[e] = O;
+    if (e == 0) {
+      part[D] = m;
+      part[D + 1] = L;
+    }
+  }
+}
+
+// grid (H, B), D threads: out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+__global__ void attn_combine_kernel(float* out, const float* partial, int H, int D, int nsplit) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  pdl_wait();
+  pdl_launch_dependents();
+  const float* p = partial + ((size_t)b * H + h) * nsplit * (D + 2);
+  float m = -INFINITY;
+  for (int s = 0; s < nsplit; s++) m = fmaxf(m, p[(size_t)s * (D + 2) + D]);
+  for (int e = threadIdx.x; e < D; e += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < nsplit; s++) {
+      const float* ps = p + (size_t)s * (D + 2);
+      const float ms = ps[D];
+      if (ms == -INFINITY) continue;
+      const float c = expf(ms - m);
+      L = fmaf(ps[D + 1], c, L);
+      O = fmaf(ps[e], c, O);
+    }
+    out[((size_t)b * H + h) * D + e] = O / L;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill: grid (ceil(Sq / BQ), H, B), 256 threads; q/out [B, Sq, H, D].
+// ---------------------------------------------------------------------------
+constexpr int BQ = 32, BK = 16, KU = BK / 8, kPfThreads = 256;
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, const float* __restrict__ q,
+                                                                   const float* __restrict__ kc,
+                                                                   const float* __restrict__ vc, int H, int Hkv,
+                                                                   int Sq, int64_t Sk, int max_seq, float scale) {
+  __shared__ float Qs[BQ][D + 1];
+  __shared__ float Ks[BK][D + 1];
+  __shared__ float Vs[BK][D];
+  __shared__ float Ps[BQ][BK];
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (H / Hkv);
+  const int t = threadIdx.x;
+  const int qi = t >> 3, sub = t & 7;
+  const int64_t offset = Sk - Sq;
+  const int q0 = qt * BQ;
+  for (int i = t; i < BQ * D; i += kPfThreads) {
+    const int r = i / D, e = i - r * D;
+    const int qq = q0 + r;
+    Qs[r][e] = qq < Sq ? q[(((size_t)b * Sq + qq) * H + h) * D + e] : 0.f;
+  }
+  const float* kb = kc + ((size_t)b * Hkv + kvh) * max_seq * D;
+  const float* vb = vc + ((size_t)b * Hkv + kvh) * max_seq * D;
+  constexpr int OV = D / 8;
+  float o[OV];
+#pragma unroll
+  for (int v = 0; v < OV; v++) o[v] = 0.f;
+  float mrow = -INFINITY, lrow = 0.f;
+  const int64_t qpos = q0 + qi;
+  const int64_t last_key = min((int64_t)(q0 + BQ - 1) + offset, Sk - 1);
+  for (int64_t k0 = 0; k0 <= last_key; k0 += BK) {
+    __syncthreads();
+    for (int i = t; i < BK * D; i += kPfThreads) {
+      const int r = i / D, e = i - r * D;
+      const int64_t kk = k0 + r;
+      const bool ok = kk < Sk;
+      Ks[r][e] = ok ? kb[kk * D + e] : 0.f;
+      Vs[r][e] = ok ? vb[kk * D + e] : 0.f;
+    }
+    __syncthreads();
+    float s[KU];
+#pragma unroll
+    for (int u = 0; u < KU; u++) {
+      const int kj = sub + 8 * u;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int e = 0; e < D; e++) acc = fmaf(Qs[qi][e], Ks[kj][e], acc);
+      const int64_t kpos = k0 + kj;
+      const bool valid = kpos < Sk && kpos <= qpos + offset && qpos < Sq;
+      s[u] = valid ? acc * scale : -INFINITY;
+    }
+    float tm = s[0];
+#pragma unroll
+    for (int u = 1; u < KU; u++) tm = fmaxf(tm, s[u]);
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 1));
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 2));
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+    const float mn = fmaxf(mrow, tm);
+    float ps = 0.f;
+#pragma unroll
+    for (int u = 0; u < KU; u++) {
+      const float p = mn == -INFINITY ? 0.f : expf(s[u] - mn);
+      Ps[qi][sub + 8 * u] = p;
+      ps += p;
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    const float corr = (mrow == -INFINITY) ? 0.f : expf(mrow - mn);
+    lrow = lrow * corr + ps;
+    mrow = mn;
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < OV; v++) o[v] *= corr;
+#pragma unroll 4
+    for (int kj = 0; kj < BK; kj++) {
+      const float p = Ps[qi][kj];
+#pragma unroll
+      for (int v = 0; v < OV; v++) o[v] = fmaf(p, Vs[kj][sub + 8 * v], o[v]);
+    }
+  }
+  if (qpos < Sq) {
+    float* dst = out + (((size_t)b * Sq + qpos) * H + h) * D;
+    const float inv = 1.0f / lrow;
+#pragma unroll
+    for (int v = 0; v < OV; v++) dst[sub + 8 * v] = o[v] * inv;
+  }
+}
+
+template <int VEC, int G>
+tb_status_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G>, a);
+  if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
+  cfg.gridDim = dim3(a.H, a.B);
+  cfg.blockDim = dim3(a.D);
+  e = cudaLaunchKernelEx(&cfg, attn_combine_kernel, a.out, (const float*)a.partial, a.H, a.D, a.nsplit);
+  if (e != cudaSuccess) return cuda_fail(e, "attn_combine_kernel");
+  return TB_SUCCESS;
+}
+
+template <int VEC>
+tb_status_t launch_decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  switch (a.H / a.Hkv) {
+    case 1: return launch_decode<VEC, 1>(a, st, pdl);
+    case 2: return launch_decode<VEC, 2>(a, st, pdl);
+    case 4: return launch_decode<VEC, 4>(a, st, pdl);
+    case 8: return launch_decode<VEC, 8>(a, st, pdl);
+    default: return TB_ERROR_NOT_SUPPORTED;
+  }
+}
+
+}  // namespace
+
+int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq) {
+  (void)H;
+  // About two waves of CTAs over the SMs, never a split shorter than 16 keys.
+  int64_t want = (2LL * sm_count() + (int64_t)B * Hkv - 1) / ((int64_t)B * Hkv);
+  int64_t cap = (max_seq + 15) / 16;
+  if (want > cap) want = cap;
+  if (want > 64) want = 64;
+  return (int)(want < 1 ? 1 : want);
+}
+
+size_t attn_decode_workspace(int B, int H, int D, int nsplit) {
+  return (size_t)B * H * nsplit * (D + 2) * sizeof(float);
+}
+
+tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  TB_REQUIRE(a.Hkv > 0 && a.H % a.Hkv == 0);
+  if (a.D == 128) return launch_decode_g<4>(a, st, pdl);
+  if (a.D == 64) return launch_decode_g<2>(a, st, pdl);
+  return TB_ERROR_NOT_SUPPORTED;
+}
+
+tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const float* vcache, int B, int H,
+                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st) {
+  TB_REQUIRE(Hkv > 0 && H % Hkv == 0 && Sq >= 1 && Sk >= Sq);
+  dim3 grid((Sq + BQ - 1) / BQ, H, B);
+  if (D == 128) {
+    attn_prefill_kernel<128><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
+  } else if (D == 64) {
+    attn_prefill_kernel<64><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
+  } else {
+    return TB_ERROR_NOT_SUPPORTED;
+  }
+  return check_launch("attn_prefill_kernel");
+}
+
+}  // namespace tb
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" size_t tb_attention_workspace_size(int64_t B, int64_t H, int64_t Sq, int64_t D, int64_t max_seq) {
+  if (B <= 0 || H <= 0 || D <= 0 || Sq != 1) return 0;
+  const int ns = tb::attn_decode_splits((int)B, (int)H, 1, max_seq);
+  // sized for the largest split count any Hkv can pick (Hkv = 1 maximises it)
+  return tb::attn_decode_workspace((int)B, (int)H, (int)D, ns);
+}
+
+extern "C" tb_status_t tb_attention_f32(float* out, const float* q, const float* kcache, const float* vcache,
+                                        int64_t B, int64_t H, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                                        int64_t max_seq, float scale, void* workspace, size_t workspace_bytes,
+                                        tb_stream_t stream) {
+  TB_INJECT("tb_attention_f32");
+  TB_REQUIRE(B >= 0 && H > 0 && Hkv > 0 && H % Hkv == 0 && Sq >= 0 && D > 0);
+  TB_REQUIRE(Sk >= Sq && Sk <= max_seq);
+  if (B == 0 || Sq == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && q && kcache && vcache);
+  TB_REQUIRE(Sk >= 1);
+  TB_REQUIRE(tb::aligned(q, 16) && tb::aligned(kcache, 16) && tb::aligned(vcache, 16));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (Sq == 1) {
+    tb::AttnDecodeArgs a{};
+    a.q = q;
+    a.kcache = kcache;
+    a.vcache = vcache;
+    a.out = out;
+    a.pos = nullptr;
+    a.sk = Sk;
+    a.B = (int)B;
+    a.H = (int)H;
+    a.Hkv = (int)Hkv;
+    a.D = (int)D;
+    a.max_seq = (int)max_seq;
+    a.scale = scale;
+    a.nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, max_seq);
+    TB_REQUIRE(workspace && workspace_bytes >= tb::attn_decode_workspace(a.B, a.H, a.D, a.nsplit));
+    a.partial = (float*)workspace;
+    return tb::attn_decode(a, st, false);
+  }
+  return tb::attn_prefill(out, q, kcache, vcache, (int)B, (int)H, (int)Hkv, (int)Sq, Sk, (int)D, (int)max_seq, scale,
+                          st);
+}

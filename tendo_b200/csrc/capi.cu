@@ -1,0 +1,109 @@
+// capi.cu — status strings, error capture, host-side fault injection and the
+// DequantizeMatmul / MatMul dispatch of the C ABI.
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tb {
+
+namespace {
+thread_local std::string g_last_cuda_error;
+}
+
+tb_status_t cuda_fail(cudaError_t e, const char* where) {
+  g_last_cuda_error = std::string(where) + ": " + cudaGetErrorName(e) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) return TB_ERROR_OUT_OF_MEMORY;
+  return TB_ERROR_CUDA;
+}
+
+tb_status_t check_launch(const char* where) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, where);
+  return TB_SUCCESS;
+}
+
+bool injected(const char* name) {
+  const char* env = getenv("TENDO_B200_INJECT");
+  if (!env || !*env) return false;
+  const size_t n = strlen(name);
+  for (const char* p = env; *p;) {
+    const char* comma = strchr(p, ',');
+    const size_t len = comma ? (size_t)(comma - p) : strlen(p);
+    if (len == n && strncmp(p, name, n) == 0) return true;
+    if (len == 3 && strncmp(p, "all", 3) == 0) return true;
+    if (!comma) break;
+    p = comma + 1;
+  }
+  return false;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace tb
+
+extern "C" const char* tb_get_error_string(tb_status_t status) {
+  switch (status) {
+    case TB_SUCCESS: return "success";
+    case TB_ERROR_INVALID_ARGUMENT: return "invalid argument";
+    case TB_ERROR_CUDA: return "CUDA error";
+    case TB_ERROR_NOT_SUPPORTED: return "not supported";
+    case TB_ERROR_OUT_OF_MEMORY: return "out of memory";
+    case TB_ERROR_TIMEOUT: return "device-side wait timed out";
+    case TB_ERROR_INJECTED: return "injected failure";
+  }
+  return "unknown status";
+}
+
+extern "C" const char* tb_get_last_cuda_error_string(void) { return tb::g_last_cuda_error.c_str(); }
+
+extern "C" int tb_version(void) { return 100; }
+
+extern "C" tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, const int8_t* q, const float* scale,
+                                                    int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                                    tb_gemm_mode_t mode, tb_stream_t stream) {
+  TB_INJECT("tb_dequant_matmul_i8f32");
+  TB_REQUIRE(M >= 0 && N >= 0 && K > 0 && group_size >= 0);
+  TB_REQUIRE(group_size == 0 || K % group_size == 0);
+  TB_REQUIRE(M <= 0x7fffffff && N <= 0x7fffffff && K <= 0x7fffffff);
+  TB_REQUIRE(mode == TB_GEMM_BF16X2 || mode == TB_GEMM_BF16 || mode == TB_GEMM_SIMT);
+  if (M == 0 || N == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && x && q && scale);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M <= 32) {
+    if (group_size == 0 && tb::gemv_fast_ok(x, q, K))
+      return tb::gemv_plain(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, nullptr, 0.f, st, false);
+    return tb::gemv_generic(out, x, q, scale, (int)M, (int)N, (int)K, group_size > 0 ? (int)group_size : (int)K, st);
+  }
+  return tb::gemm_i8(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, (int)group_size, mode, st);
+}
+
+extern "C" tb_status_t tb_dequant_matmul_i8f32(float* out, const float* x, const int8_t* q, const float* scale,
+                                               int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                               tb_stream_t stream) {
+  return tb_dequant_matmul_i8f32_mode(out, x, q, scale, M, N, K, group_size, TB_GEMM_BF16X2, stream);
+}
+
+extern "C" tb_status_t tb_matmul_nt_f32(float* out, const float* a, const float* b, int64_t M, int64_t N, int64_t K,
+                                        tb_stream_t stream) {
+  TB_INJECT("tb_matmul_nt_f32");
+  TB_REQUIRE(M >= 0 && N >= 0 && K > 0);
+  TB_REQUIRE(M <= 0x7fffffff && N <= 0x7fffffff && K <= 0x7fffffff);
+  if (M == 0 || N == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && a && b);
+  return tb::gemm_f32_nt(out, a, b, (int)M, (int)N, (int)K, (cudaStream_t)stream);
+}

@@ -1,0 +1,658 @@
+// engine.cu — the host side of the path in C++: tendo's QuantizedModel
+// (models/llama/quantized.go:13-477) over the kernels of this library.
+//
+// Layout in HBM (one engine per GPU):
+//   wqkv  [L][(H + 2 Hkv) D][d] int8   — q, k, v rows concatenated per layer
+//   sqkv  [L][(H + 2 Hkv) D]    fp32   — their per-channel scales
+//   wo    [L][d][H D], wgate/wup [L][F][d], wdown [L][d][F] int8 (+ scales)
+//   embed, lm_head [V][d] fp32 (the reference keeps both fp32)
+//   kc, vc [L][B][Hkv][max_seq][D] fp32 (the reference's cache layout,
+//          preallocated; the Cat append becomes an in-place write)
+//
+// Prefill (and any batch too wide for the fused decode kernels) runs layer
+// by layer: RMSNorm, the GEMM projections, RoPE + cache append, tiled causal
+// attention, residual adds.  Decode runs one CUDA graph per step: embedding,
+// then per layer [fused RMSNorm+QKV+RoPE+append GEMV] -> [split-K attention
+// + combine] -> [O GEMV + residual] -> [fused RMSNorm+gate/up+SwiGLU GEMV]
+// -> [down GEMV + residual], then the fused final-norm lm_head GEMV with
+// greedy argmax, and a tail kernel that feeds the token back and advances
+// the position — both live in device memory, so the same graph replays for
+// every step with programmatic dependent launch between the kernels.
+#include <math.h>
+#include <string.h>
+
+#include <vector>
+
+#include "../../include/tendo_synth.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "kernels.h"
+
+struct tb_model {
+  tb_model_config c{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int64_t d = 0, H = 0, Hkv = 0, D = 0, F = 0, V = 0, L = 0, Ms = 0, B = 0, NQKV = 0;
+  int8_t *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *sgate = nullptr, *sup = nullptr, *sdown = nullptr;
+  float *attn_norm = nullptr, *mlp_norm = nullptr, *final_norm = nullptr;
+  float *embed = nullptr, *lm_head = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+  float *kc = nullptr, *vc = nullptr;
+  float *h = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *u = nullptr;
+  float *qbuf = nullptr, *partial = nullptr, *logits = nullptr, *last = nullptr;
+  unsigned long long* keys = nullptr;
+  int64_t *tokens = nullptr, *ids = nullptr, *history = nullptr, *pos = nullptr, *step = nullptr;
+  int32_t* bad = nullptr;
+  int64_t host_pos = 0, host_step = 0, hist_cap = 0, chunk_s = 0, rows_max = 0;
+  int nsplit = 1;
+  bool fused = false;
+  bool pdl = true;
+  cudaGraphExec_t graph = nullptr;
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+using tb::ceil_div;
+
+template <typename T>
+tb_status_t dalloc(tb_model* m, T** p, size_t count) {
+  void* v = nullptr;
+  cudaError_t e = cudaMalloc(&v, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+  if (e != cudaSuccess) return tb::cuda_fail(e, "cudaMalloc");
+  m->allocs.push_back(v);
+  *p = (T*)v;
+  return TB_SUCCESS;
+}
+
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+size_t lin_rows(const tb_model* m, int mat) {
+  const int64_t hq = m->H * m->D, hkv = m->Hkv * m->D;
+  const int64_t r[7] = {hq, hkv, hkv, m->d, m->F, m->F, m->d};
+  return (size_t)r[mat];
+}
+size_t lin_cols(const tb_model* m, int mat) {
+  const int64_t c[7] = {m->d, m->d, m->d, m->H * m->D, m->d, m->d, m->F};
+  return (size_t)c[mat];
+}
+
+// Pointers of one Linear inside the layer buffers.
+void lin_ptr(tb_model* m, int layer, int mat, int8_t** q, float** s) {
+  const int64_t hq = m->H * m->D, hkv = m->Hkv * m->D;
+  switch (mat) {
+    case 0: *q = m->wqkv + (size_t)layer * m->NQKV * m->d; *s = m->sqkv + (size_t)layer * m->NQKV; break;
+    case 1:
+      *q = m->wqkv + ((size_t)layer * m->NQKV + hq) * m->d;
+      *s = m->sqkv + (size_t)layer * m->NQKV + hq;
+      break;
+    case 2:
+      *q = m->wqkv + ((size_t)layer * m->NQKV + hq + hkv) * m->d;
+      *s = m->sqkv + (size_t)layer * m->NQKV + hq + hkv;
+      break;
+    case 3: *q = m->wo + (size_t)layer * m->d * hq; *s = m->so + (size_t)layer * m->d; break;
+    case 4: *q = m->wgate + (size_t)layer * m->F * m->d; *s = m->sgate + (size_t)layer * m->F; break;
+    case 5: *q = m->wup + (size_t)layer * m->F * m->d; *s = m->sup + (size_t)layer * m->F; break;
+    default: *q = m->wdown + (size_t)layer * m->d * m->F; *s = m->sdown + (size_t)layer * m->d; break;
+  }
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Layer-by-layer forward of S tokens per sequence already embedded in m->h
+// (rows b * S + s), at cache positions host_pos .. host_pos + S - 1.
+tb_status_t forward_layers(tb_model* m, int64_t S) {
+  cudaStream_t st = m->stream;
+  const int64_t rows = m->B * S;
+  const int64_t P = m->host_pos;
+  const float scale = 1.0f / (float)sqrt((double)m->D);
+  for (int64_t l = 0; l < m->L; l++) {
+    int8_t *wq, *wo, *wg, *wu, *wd;
+    float *sq, *so, *sg, *su, *sd;
+    lin_ptr(m, (int)l, 0, &wq, &sq);
+    lin_ptr(m, (int)l, 3, &wo, &so);
+    lin_ptr(m, (int)l, 4, &wg, &sg);
+    lin_ptr(m, (int)l, 5, &wu, &su);
+    lin_ptr(m, (int)l, 6, &wd, &sd);
+    float* kcl = m->kc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    float* vcl = m->vc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    // attention block (models/llama/quantized.go:186-199)
+    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->attn_norm + l * m->d, rows, m->d, m->c.eps, st));
+    TB_TRY(tb_dequant_matmul_i8f32(m->qkv, m->xn, wq, sq, rows, m->NQKV, m->d, 0, (tb_stream_t)st));
+    TB_TRY(tb::rope_rows(m->qkv, m->cos_t, m->sin_t, m->B, S, m->H, m->D, P, m->NQKV, st));
+    TB_TRY(tb::kv_append_rope(kcl, vcl, m->qkv + m->H * m->D, m->qkv + (m->H + m->Hkv) * m->D, m->cos_t, m->sin_t,
+                              m->B, m->Hkv, S, m->D, P, m->Ms, m->NQKV, st));
+    // q rows have stride NQKV; the attention kernels take [B, S, H, D] rows of H * D
+    TB_CUDA(cudaMemcpy2DAsync(m->g, sizeof(float) * m->H * m->D, m->qkv, sizeof(float) * m->NQKV,
+                              sizeof(float) * m->H * m->D, rows, cudaMemcpyDeviceToDevice, st));
+    if (S == 1) {
+      tb::AttnDecodeArgs a{};
+      a.q = m->g;
+      a.kcache = kcl;
+      a.vcache = vcl;
+      a.out = m->attn;
+      a.partial = m->partial;
+      a.pos = nullptr;
+      a.sk = P + 1;
+      a.B = (int)m->B;
+      a.H = (int)m->H;
+      a.Hkv = (int)m->Hkv;
+      a.D = (int)m->D;
+      a.max_seq = (int)m->Ms;
+      a.nsplit = m->nsplit;
+      a.scale = scale;
+      TB_TRY(tb::attn_decode(a, st, false));
+    } else {
+      TB_TRY(tb::attn_prefill(m->attn, m->g, kcl, vcl, (int)m->B, (int)m->H, (int)m->Hkv, (int)S, P + S, (int)m->D,
+                              (int)m->Ms, scale, st));
+    }
+    // o projection + residual
+    if (rows <= 32) {
+      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, 0, (tb_stream_t)st));
+      TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
+    } else {
+      TB_TRY(tb::gemm_i8(m->h, m->attn, wo, so, m->h, (int)rows, (int)m->d, (int)(m->H * m->D), 0, TB_GEMM_BF16X2, st));
+    }
+    // MLP block (models/llama/quantized.go:206-219, :385-417)
+    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->mlp_norm + l * m->d, rows, m->d, m->c.eps, st));
+    TB_TRY(tb_dequant_matmul_i8f32(m->g, m->xn, wg, sg, rows, m->F, m->d, 0, (tb_stream_t)st));
+    TB_TRY(tb_dequant_matmul_i8f32(m->u, m->xn, wu, su, rows, m->F, m->d, 0, (tb_stream_t)st));
+    TB_TRY(tb::silu_mul(m->g, m->g, m->u, rows * m->F, st));
+    if (rows <= 32) {
+      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, 0, (tb_stream_t)st));
+      TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
+    } else {
+      TB_TRY(tb::gemm_i8(m->h, m->g, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, 0, TB_GEMM_BF16X2, st));
+    }
+  }
+  return TB_SUCCESS;
+}
+
+// Final RMSNorm + lm_head on the last row of each sequence, greedy argmax
+// into m->tokens (and the history), position set to host_pos.
+tb_status_t finish_logits(tb_model* m, int64_t S) {
+  cudaStream_t st = m->stream;
+  // gather the last rows: h[b * S + S - 1] -> last[b]
+  TB_CUDA(cudaMemcpy2DAsync(m->last, sizeof(float) * m->d, m->h + (S - 1) * m->d, sizeof(float) * m->d * S,
+                            sizeof(float) * m->d, m->B, cudaMemcpyDeviceToDevice, st));
+  if (m->B <= 8 && tb::gemv_smem_bytes(8, (int)m->d) <= 200 * 1024) {
+    tb::LmHeadArgs a{};
+    a.h = m->last;
+    a.norm_w = m->final_norm;
+    a.eps = m->c.eps;
+    a.w = m->lm_head;
+    a.logits = m->logits;
+    a.argmax_keys = m->keys;
+    a.M = (int)m->B;
+    a.d = (int)m->d;
+    a.V = (int)m->V;
+    TB_TRY(tb::gemv_lmhead(a, st, false));
+    // the tail kernel advances the position by one; pre-compensate
+    int64_t p = m->host_pos - 1;
+    TB_CUDA(cudaMemcpyAsync(m->pos, &p, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, st, false));
+  } else {
+    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->last, nullptr, m->final_norm, m->B, m->d, m->c.eps, st));
+    TB_TRY(tb::gemm_f32_nt(m->logits, m->xn, m->lm_head, (int)m->B, (int)m->V, (int)m->d, st));
+    TB_TRY(tb::argmax_rows(m->tokens, m->logits, m->B, m->V, st));
+    if (m->host_step < m->hist_cap)
+      TB_CUDA(cudaMemcpyAsync(m->history + m->host_step * m->B, m->tokens, sizeof(int64_t) * m->B,
+                              cudaMemcpyDeviceToDevice, st));
+    int64_t s1 = m->host_step + 1;
+    TB_CUDA(cudaMemcpyAsync(m->step, &s1, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+  }
+  m->host_step += 1;
+  // cudaMemcpyAsync from pageable host memory is staged before returning, so
+  // the stack values above may go out of scope; keep the stream ordered.
+  TB_CUDA(cudaStreamSynchronize(st));
+  return TB_SUCCESS;
+}
+
+// Prefill / generic forward of tokens already in m->ids [B, S].
+tb_status_t forward_tokens(tb_model* m, int64_t S) {
+  cudaStream_t st = m->stream;
+  for (int64_t s0 = 0; s0 < S; s0 += m->chunk_s) {
+    const int64_t sc = S - s0 < m->chunk_s ? S - s0 : m->chunk_s;
+    // embed rows b * sc + s of this chunk
+    for (int64_t b = 0; b < m->B; b++)
+      TB_TRY(tb::embedding(m->h + b * sc * m->d, m->embed, m->ids + b * S + s0, sc, m->V, m->d, m->bad, st, false));
+    TB_TRY(forward_layers(m, sc));
+    m->host_pos += sc;
+    if (s0 + sc >= S) TB_TRY(finish_logits(m, sc));
+  }
+  return TB_SUCCESS;
+}
+
+// One kernel of the fused decode step (kind as in tb_model_bench_kernel).
+tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
+  cudaStream_t st = m->stream;
+  const float scale = 1.0f / (float)sqrt((double)m->D);
+  {
+    int8_t *wq, *wo, *wg, *wu, *wd;
+    float *sq, *so, *sg, *su, *sd;
+    lin_ptr(m, (int)l, 0, &wq, &sq);
+    lin_ptr(m, (int)l, 3, &wo, &so);
+    lin_ptr(m, (int)l, 4, &wg, &sg);
+    lin_ptr(m, (int)l, 5, &wu, &su);
+    lin_ptr(m, (int)l, 6, &wd, &sd);
+    float* kcl = m->kc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    float* vcl = m->vc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    tb::QkvArgs qa{};
+    qa.h = m->h;
+    qa.norm_w = m->attn_norm + l * m->d;
+    qa.eps = m->c.eps;
+    qa.q = wq;
+    qa.scale = sq;
+    qa.cos_t = m->cos_t;
+    qa.sin_t = m->sin_t;
+    qa.pos = m->pos;
+    qa.qout = m->qbuf;
+    qa.kcache = kcl;
+    qa.vcache = vcl;
+    qa.M = (int)m->B;
+    qa.d = (int)m->d;
+    qa.H = (int)m->H;
+    qa.Hkv = (int)m->Hkv;
+    qa.D = (int)m->D;
+    qa.max_seq = (int)m->Ms;
+    if (kind == 0) return tb::gemv_qkv_rope(qa, st, pdl);
+    tb::AttnDecodeArgs aa{};
+    aa.q = m->qbuf;
+    aa.kcache = kcl;
+    aa.vcache = vcl;
+    aa.out = m->attn;
+    aa.partial = m->partial;
+    aa.pos = m->pos;
+    aa.B = (int)m->B;
+    aa.H = (int)m->H;
+    aa.Hkv = (int)m->Hkv;
+    aa.D = (int)m->D;
+    aa.max_seq = (int)m->Ms;
+    aa.nsplit = m->nsplit;
+    aa.scale = scale;
+    if (kind == 1) return tb::attn_decode(aa, st, pdl);
+    if (kind == 2)
+      return tb::gemv_plain(m->h, m->attn, wo, so, m->h, (int)m->B, (int)m->d, (int)(m->H * m->D), nullptr, 0.f, st,
+                            pdl);
+    tb::GateUpArgs ga{};
+    ga.h = m->h;
+    ga.norm_w = m->mlp_norm + l * m->d;
+    ga.eps = m->c.eps;
+    ga.gate = wg;
+    ga.up = wu;
+    ga.gate_scale = sg;
+    ga.up_scale = su;
+    ga.act = m->g;
+    ga.M = (int)m->B;
+    ga.d = (int)m->d;
+    ga.F = (int)m->F;
+    if (kind == 3) return tb::gemv_gateup(ga, st, pdl);
+    if (kind == 4)
+      return tb::gemv_plain(m->h, m->g, wd, sd, m->h, (int)m->B, (int)m->d, (int)m->F, nullptr, 0.f, st, pdl);
+  }
+  tb::LmHeadArgs la{};
+  la.h = m->h;
+  la.norm_w = m->final_norm;
+  la.eps = m->c.eps;
+  la.w = m->lm_head;
+  la.logits = m->logits;
+  la.argmax_keys = m->keys;
+  la.M = (int)m->B;
+  la.d = (int)m->d;
+  la.V = (int)m->V;
+  if (kind == 5) return tb::gemv_lmhead(la, st, pdl);
+  return TB_ERROR_INVALID_ARGUMENT;
+}
+
+// One fused decode step (graph body).
+tb_status_t decode_step_fused(tb_model* m) {
+  const bool pdl = m->pdl;
+  TB_TRY(tb::embedding(m->h, m->embed, m->tokens, m->B, m->V, m->d, m->bad, m->stream, pdl));
+  for (int64_t l = 0; l < m->L; l++)
+    for (int kind = 0; kind < 5; kind++) TB_TRY(decode_kernel(m, kind, l, pdl));
+  TB_TRY(decode_kernel(m, 5, 0, pdl));
+  TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, m->stream, pdl));
+  return TB_SUCCESS;
+}
+
+tb_status_t build_graph(tb_model* m) {
+  if (m->graph) return TB_SUCCESS;
+  cudaGraph_t g = nullptr;
+  TB_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  tb_status_t s = decode_step_fused(m);
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (s != TB_SUCCESS) {
+    if (g) cudaGraphDestroy(g);
+    return s;
+  }
+  if (e != cudaSuccess) return tb::cuda_fail(e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(&m->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    m->graph = nullptr;
+    return tb::cuda_fail(e, "cudaGraphInstantiate");
+  }
+  return TB_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device) {
+  TB_INJECT("tb_model_create");
+  TB_REQUIRE(out && cfg);
+  *out = nullptr;
+  TB_REQUIRE(cfg->vocab > 0 && cfg->dim > 0 && cfg->layers > 0 && cfg->heads > 0 && cfg->kv_heads > 0);
+  TB_REQUIRE(cfg->dim % cfg->heads == 0 && cfg->heads % cfg->kv_heads == 0 && cfg->hidden > 0);
+  TB_REQUIRE(cfg->max_seq > 0 && cfg->max_batch > 0);
+  TB_REQUIRE((cfg->dim / cfg->heads) % 2 == 0);
+  DeviceGuard guard(device);
+  TB_CUDA(cudaSetDevice(device));
+  tb_model* m = new tb_model();
+  m->c = *cfg;
+  m->device = device;
+  m->d = cfg->dim;
+  m->H = cfg->heads;
+  m->Hkv = cfg->kv_heads;
+  m->D = cfg->dim / cfg->heads;
+  m->F = cfg->hidden;
+  m->V = cfg->vocab;
+  m->L = cfg->layers;
+  m->Ms = cfg->max_seq;
+  m->B = cfg->max_batch;
+  m->NQKV = (m->H + 2 * m->Hkv) * m->D;
+  m->hist_cap = m->Ms;
+  m->chunk_s = 4096 / m->B > 0 ? 4096 / m->B : 1;
+  if (m->chunk_s > m->Ms) m->chunk_s = m->Ms;
+  m->rows_max = m->B * m->chunk_s;
+  const size_t fused_smem = tb::gemv_smem_bytes(m->B <= 1 ? 1 : (m->B <= 2 ? 2 : (m->B <= 4 ? 4 : 8)), (int)m->d);
+  m->fused = m->B <= 8 && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
+             (m->D == 64 || m->D == 128) && (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 ||
+                                             m->H / m->Hkv == 8);
+  const char* nopdl = getenv("TENDO_B200_NO_PDL");
+  m->pdl = !(nopdl && *nopdl == '1');
+  m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);
+  tb_status_t s = TB_SUCCESS;
+  auto A = [&](tb_status_t r) {
+    if (s == TB_SUCCESS) s = r;
+  };
+  const size_t L = m->L;
+  A(dalloc(m, &m->wqkv, L * m->NQKV * m->d));
+  A(dalloc(m, &m->sqkv, L * m->NQKV));
+  A(dalloc(m, &m->wo, L * m->d * m->H * m->D));
+  A(dalloc(m, &m->so, L * m->d));
+  A(dalloc(m, &m->wgate, L * m->F * m->d));
+  A(dalloc(m, &m->sgate, L * m->F));
+  A(dalloc(m, &m->wup, L * m->F * m->d));
+  A(dalloc(m, &m->sup, L * m->F));
+  A(dalloc(m, &m->wdown, L * m->d * m->F));
+  A(dalloc(m, &m->sdown, L * m->d));
+  A(dalloc(m, &m->attn_norm, L * m->d));
+  A(dalloc(m, &m->mlp_norm, L * m->d));
+  A(dalloc(m, &m->final_norm, (size_t)m->d));
+  A(dalloc(m, &m->embed, (size_t)m->V * m->d));
+  A(dalloc(m, &m->lm_head, (size_t)m->V * m->d));
+  A(dalloc(m, &m->cos_t, (size_t)m->Ms * (m->D / 2)));
+  A(dalloc(m, &m->sin_t, (size_t)m->Ms * (m->D / 2)));
+  const size_t kv = L * m->B * m->Hkv * m->Ms * m->D;
+  A(dalloc(m, &m->kc, kv));
+  A(dalloc(m, &m->vc, kv));
+  const size_t R = (size_t)m->rows_max;
+  A(dalloc(m, &m->h, R * m->d));
+  A(dalloc(m, &m->xn, R * m->d));
+  A(dalloc(m, &m->qkv, R * m->NQKV));
+  A(dalloc(m, &m->attn, R * m->H * m->D));
+  const size_t gw = R * (m->F > m->H * m->D ? m->F : m->H * m->D);
+  A(dalloc(m, &m->g, gw));
+  A(dalloc(m, &m->u, R * m->F));
+  A(dalloc(m, &m->qbuf, (size_t)m->B * m->H * m->D));
+  A(dalloc(m, &m->partial, tb::attn_decode_workspace((int)m->B, (int)m->H, (int)m->D, m->nsplit) / sizeof(float)));
+  A(dalloc(m, &m->logits, (size_t)m->B * m->V));
+  A(dalloc(m, &m->last, (size_t)m->B * m->d));
+  A(dalloc(m, &m->keys, (size_t)m->B));
+  A(dalloc(m, &m->tokens, (size_t)m->B));
+  A(dalloc(m, &m->ids, (size_t)m->B * m->Ms));
+  A(dalloc(m, &m->history, (size_t)m->hist_cap * m->B));
+  A(dalloc(m, &m->pos, 1));
+  A(dalloc(m, &m->step, 1));
+  A(dalloc(m, &m->bad, 1));
+  if (s == TB_SUCCESS) {
+    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) s = tb::cuda_fail(e, "cudaStreamCreate");
+  }
+  if (s == TB_SUCCESS) {
+    std::vector<float> ct((size_t)m->Ms * (m->D / 2)), sn(ct.size());
+    tb_rope_tables_host(ct.data(), sn.data(), (int)m->D, (int)m->Ms, cfg->rope_base);
+    cudaError_t e = cudaMemcpy(m->cos_t, ct.data(), ct.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->sin_t, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(m->keys, 0, sizeof(unsigned long long) * m->B);
+    if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(m->pos, 0, sizeof(int64_t));
+    if (e == cudaSuccess) e = cudaMemset(m->step, 0, sizeof(int64_t));
+    if (e == cudaSuccess) e = cudaMemset(m->bad, 0, sizeof(int32_t));
+    if (e != cudaSuccess) s = tb::cuda_fail(e, "engine init");
+  }
+  if (s != TB_SUCCESS) {
+    tb_model_destroy(m);
+    return s;
+  }
+  *out = m;
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_destroy(tb_model* m) {
+  if (!m) return TB_SUCCESS;
+  DeviceGuard guard(m->device);
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->stream) {
+    cudaStreamSynchronize(m->stream);
+    cudaStreamDestroy(m->stream);
+  }
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_init_synthetic(tb_model* m, uint64_t seed) {
+  TB_INJECT("tb_model_init_synthetic");
+  TB_REQUIRE(m);
+  DeviceGuard guard(m->device);
+  tb_stream_t st = (tb_stream_t)m->stream;
+  for (int l = 0; l < m->L; l++) {
+    for (int mat = 0; mat < 7; mat++) {
+      int8_t* q;
+      float* s;
+      lin_ptr(m, l, mat, &q, &s);
+      TB_TRY(tb_synth_quantized_i8(q, s, (int64_t)lin_rows(m, mat), (int64_t)lin_cols(m, mat), seed,
+                                   (uint64_t)l * TS_MATS + (uint64_t)mat, 0.02, st));
+    }
+  }
+  TB_TRY(tb_synth_normal_f32(m->embed, m->V, m->d, seed, 0x7fff0001ull, 0.02, st));
+  TB_TRY(tb_synth_normal_f32(m->lm_head, m->V, m->d, seed, 0x7fff0002ull, 0.02, st));
+  fill_kernel<<<256, 256, 0, m->stream>>>(m->attn_norm, m->L * m->d, 1.0f);
+  fill_kernel<<<256, 256, 0, m->stream>>>(m->mlp_norm, m->L * m->d, 1.0f);
+  fill_kernel<<<16, 256, 0, m->stream>>>(m->final_norm, m->d, 1.0f);
+  TB_TRY(tb::check_launch("fill_kernel"));
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_set_linear(tb_model* m, int layer, int mat, const int8_t* q_host,
+                                           const float* scale_host) {
+  TB_REQUIRE(m && q_host && scale_host && layer >= 0 && layer < m->L && mat >= 0 && mat < 7);
+  DeviceGuard guard(m->device);
+  int8_t* q;
+  float* s;
+  lin_ptr(m, layer, mat, &q, &s);
+  TB_CUDA(cudaMemcpy(q, q_host, lin_rows(m, mat) * lin_cols(m, mat), cudaMemcpyHostToDevice));
+  TB_CUDA(cudaMemcpy(s, scale_host, lin_rows(m, mat) * sizeof(float), cudaMemcpyHostToDevice));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_get_linear(tb_model* m, int layer, int mat, int8_t* q_host, float* scale_host) {
+  TB_REQUIRE(m && layer >= 0 && layer < m->L && mat >= 0 && mat < 7);
+  DeviceGuard guard(m->device);
+  int8_t* q;
+  float* s;
+  lin_ptr(m, layer, mat, &q, &s);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  if (q_host) TB_CUDA(cudaMemcpy(q_host, q, lin_rows(m, mat) * lin_cols(m, mat), cudaMemcpyDeviceToHost));
+  if (scale_host) TB_CUDA(cudaMemcpy(scale_host, s, lin_rows(m, mat) * sizeof(float), cudaMemcpyDeviceToHost));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_set_tensor(tb_model* m, int which, int layer, const float* host) {
+  TB_REQUIRE(m && host && which >= 0 && which <= 4);
+  DeviceGuard guard(m->device);
+  float* dst = nullptr;
+  size_t n = 0;
+  switch (which) {
+    case 0: dst = m->embed; n = (size_t)m->V * m->d; break;
+    case 1: dst = m->lm_head; n = (size_t)m->V * m->d; break;
+    case 2: dst = m->final_norm; n = (size_t)m->d; break;
+    case 3: TB_REQUIRE(layer >= 0 && layer < m->L); dst = m->attn_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
+    default: TB_REQUIRE(layer >= 0 && layer < m->L); dst = m->mlp_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
+  }
+  TB_CUDA(cudaMemcpy(dst, host, n * sizeof(float), cudaMemcpyHostToDevice));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_get_tensor(tb_model* m, int which, int layer, float* host) {
+  TB_REQUIRE(m && host && which >= 0 && which <= 4);
+  DeviceGuard guard(m->device);
+  const float* src = nullptr;
+  size_t n = 0;
+  switch (which) {
+    case 0: src = m->embed; n = (size_t)m->V * m->d; break;
+    case 1: src = m->lm_head; n = (size_t)m->V * m->d; break;
+    case 2: src = m->final_norm; n = (size_t)m->d; break;
+    case 3: TB_REQUIRE(layer >= 0 && layer < m->L); src = m->attn_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
+    default: TB_REQUIRE(layer >= 0 && layer < m->L); src = m->mlp_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
+  }
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  TB_CUDA(cudaMemcpy(host, src, n * sizeof(float), cudaMemcpyDeviceToHost));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer) {
+  TB_REQUIRE(m && kind >= 0 && kind <= 5 && layer >= 0 && layer < m->L);
+  TB_REQUIRE(m->fused && m->host_pos < m->Ms);
+  DeviceGuard guard(m->device);
+  return decode_kernel(m, kind, layer, false);
+}
+
+extern "C" tb_status_t tb_model_reset(tb_model* m) {
+  TB_REQUIRE(m);
+  DeviceGuard guard(m->device);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  m->host_pos = 0;
+  m->host_step = 0;
+  TB_CUDA(cudaMemset(m->pos, 0, sizeof(int64_t)));
+  TB_CUDA(cudaMemset(m->step, 0, sizeof(int64_t)));
+  TB_CUDA(cudaMemset(m->keys, 0, sizeof(unsigned long long) * m->B));
+  return TB_SUCCESS;
+}
+
+extern "C" int64_t tb_model_position(const tb_model* m) { return m ? m->host_pos : -1; }
+
+extern "C" tb_status_t tb_model_set_position(tb_model* m, int64_t pos) {
+  TB_REQUIRE(m && pos >= 0 && pos <= m->Ms);
+  DeviceGuard guard(m->device);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  m->host_pos = pos;
+  TB_CUDA(cudaMemcpy(m->pos, &pos, sizeof(int64_t), cudaMemcpyHostToDevice));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_forward(tb_model* m, const int64_t* tokens_host, int64_t B, int64_t S,
+                                        float* last_logits_host, int64_t* next_host) {
+  TB_INJECT("tb_model_forward");
+  TB_REQUIRE(m && tokens_host && B == m->B && S >= 1);
+  TB_REQUIRE(m->host_pos + S <= m->Ms);  // nn/rope.go:109-111
+  DeviceGuard guard(m->device);
+  for (int64_t i = 0; i < B * S; i++) TB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->V);
+  TB_CUDA(cudaMemcpyAsync(m->ids, tokens_host, sizeof(int64_t) * B * S, cudaMemcpyHostToDevice, m->stream));
+  TB_TRY(forward_tokens(m, S));
+  if (last_logits_host)
+    TB_CUDA(cudaMemcpyAsync(last_logits_host, m->logits, sizeof(float) * m->B * m->V, cudaMemcpyDeviceToHost, m->stream));
+  if (next_host)
+    TB_CUDA(cudaMemcpyAsync(next_host, m->tokens, sizeof(int64_t) * m->B, cudaMemcpyDeviceToHost, m->stream));
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_decode(tb_model* m, const int64_t* start_tokens_host, int64_t n_steps) {
+  TB_INJECT("tb_model_decode");
+  TB_REQUIRE(m && n_steps >= 0);
+  TB_REQUIRE(m->host_pos + n_steps <= m->Ms);
+  DeviceGuard guard(m->device);
+  if (start_tokens_host) {
+    for (int64_t i = 0; i < m->B; i++) TB_REQUIRE(start_tokens_host[i] >= 0 && start_tokens_host[i] < m->V);
+    TB_CUDA(cudaMemcpyAsync(m->tokens, start_tokens_host, sizeof(int64_t) * m->B, cudaMemcpyHostToDevice, m->stream));
+    TB_CUDA(cudaStreamSynchronize(m->stream));
+  }
+  if (m->fused) {
+    TB_TRY(build_graph(m));
+    for (int64_t i = 0; i < n_steps; i++) TB_CUDA(cudaGraphLaunch(m->graph, m->stream));
+  } else {
+    for (int64_t i = 0; i < n_steps; i++) {
+      TB_CUDA(cudaMemcpyAsync(m->ids, m->tokens, sizeof(int64_t) * m->B, cudaMemcpyDeviceToDevice, m->stream));
+      TB_TRY(forward_tokens(m, 1));  // advances host_pos and the history
+    }
+    return TB_SUCCESS;
+  }
+  m->host_pos += n_steps;
+  m->host_step += n_steps;
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_tokens(tb_model* m, int64_t* out_host, int64_t count) {
+  TB_REQUIRE(m && out_host && count >= 0 && count <= m->hist_cap);
+  DeviceGuard guard(m->device);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  if (count) TB_CUDA(cudaMemcpy(out_host, m->history, sizeof(int64_t) * count * m->B, cudaMemcpyDeviceToHost));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_sync(tb_model* m) {
+  TB_REQUIRE(m);
+  DeviceGuard guard(m->device);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  return TB_SUCCESS;
+}
+
+extern "C" tb_stream_t tb_model_stream(tb_model* m) { return m ? (tb_stream_t)m->stream : nullptr; }
+
+extern "C" int64_t tb_model_launches_per_step(const tb_model* m) {
+  if (!m) return 0;
+  if (!m->fused) return -1;
+  // embedding + per layer (qkv, attention, combine, o, gate/up, down) + lm_head + tail
+  return 1 + m->L * 6 + 2;
+}
+
+extern "C" tb_status_t tb_model_generate_greedy(tb_model* m, const int64_t* prompt_host, int64_t B, int64_t S,
+                                                int64_t n_new, int64_t* out_tokens_host) {
+  TB_INJECT("tb_model_generate_greedy");
+  TB_REQUIRE(m && prompt_host && out_tokens_host && B == m->B && S >= 1 && n_new >= 1);
+  TB_REQUIRE(S + n_new - 1 <= m->Ms && n_new <= m->hist_cap);
+  TB_TRY(tb_model_reset(m));
+  TB_TRY(tb_model_forward(m, prompt_host, B, S, nullptr, nullptr));
+  if (n_new > 1) TB_TRY(tb_model_decode(m, nullptr, n_new - 1));
+  std::vector<int64_t> hist((size_t)(n_new * B));
+  TB_TRY(tb_model_tokens(m, hist.data(), n_new));
+  for (int64_t t = 0; t < n_new; t++)
+    for (int64_t b = 0; b < B; b++) out_tokens_host[b * n_new + t] = hist[(size_t)(t * B + b)];
+  return TB_SUCCESS;
+}

@@ -1,0 +1,98 @@
+// kernels.h — internal launchers shared by the C ABI and the model engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tendo_b200.h"
+
+namespace tb {
+
+struct QkvArgs {
+  const float* h;       // residual stream [M, d]
+  const float* norm_w;  // attn_norm [d]
+  float eps;
+  const int8_t* q;      // [(H + 2 Hkv) * D, d] = [Wq; Wk; Wv]
+  const float* scale;   // [(H + 2 Hkv) * D]
+  const float* cos_t;   // [max_seq, D/2]
+  const float* sin_t;
+  const int64_t* pos;   // device: current position
+  float* qout;          // [M, H * D] post-RoPE
+  float* kcache;        // [M, Hkv, max_seq, D] of this layer
+  float* vcache;
+  int M, d, H, Hkv, D, max_seq;
+};
+
+struct GateUpArgs {
+  const float* h;
+  const float* norm_w;
+  float eps;
+  const int8_t* gate;  // [F, d]
+  const int8_t* up;    // [F, d]
+  const float* gate_scale;
+  const float* up_scale;
+  float* act;  // [M, F]
+  int M, d, F;
+};
+
+struct LmHeadArgs {
+  const float* h;
+  const float* norm_w;
+  float eps;
+  const float* w;  // [V, d] fp32
+  float* logits;   // [M, V] (may be null)
+  unsigned long long* argmax_keys;  // [M] (may be null)
+  int M, d, V;
+};
+
+struct AttnDecodeArgs {
+  const float* q;       // [B, H, D]
+  const float* kcache;  // [B, Hkv, max_seq, D]
+  const float* vcache;
+  float* out;           // [B, H, D]
+  float* partial;       // [B, H, nsplit, D + 2] workspace
+  const int64_t* pos;   // device position of the newest key (Sk = *pos + 1); null: use sk
+  int64_t sk;
+  int B, H, Hkv, D, max_seq, nsplit;
+  float scale;
+};
+
+// gemv.cu
+bool gemv_fast_ok(const float* x, const int8_t* q, int64_t K);
+tb_status_t gemv_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                       int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl);
+tb_status_t gemv_generic(float* out, const float* x, const int8_t* q, const float* scale, int M, int N, int K, int g,
+                         cudaStream_t st);
+tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl);
+tb_status_t gemv_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
+tb_status_t gemv_lmhead(const LmHeadArgs& a, cudaStream_t st, bool pdl);
+
+// attention.cu
+int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq);
+size_t attn_decode_workspace(int B, int H, int D, int nsplit);
+tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const float* vcache, int B, int H,
+                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st);
+
+// gemm.cu: out[M, N] = x[M, K] @ (q * scale)^T (+ resid), M > 32.
+tb_status_t gemm_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                    int N, int K, int group, tb_gemm_mode_t mode, cudaStream_t st);
+tb_status_t gemm_f32_nt(float* out, const float* a, const float* b, int M, int N, int K, cudaStream_t st);
+
+// ops.cu
+tb_status_t embedding(float* out, const float* table, const int64_t* ids, int64_t n, int64_t vocab, int64_t dim,
+                      int32_t* bad, cudaStream_t st, bool pdl);
+tb_status_t rmsnorm(float* out, float* resid_out, const float* in, const float* resid, const float* w, int64_t rows,
+                    int64_t d, float eps, cudaStream_t st);
+tb_status_t kv_append_rope(float* kc, float* vc, const float* k, const float* v, const float* cos_t,
+                           const float* sin_t, int64_t B, int64_t Hkv, int64_t S, int64_t D, int64_t pos,
+                           int64_t max_seq, int64_t ld, cudaStream_t st);
+tb_status_t rope_rows(float* x, const float* cos_t, const float* sin_t, int64_t B, int64_t S, int64_t Hx, int64_t D,
+                      int64_t pos, int64_t ld, cudaStream_t st);
+tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, cudaStream_t st);
+tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st);
+// Decode-step tail: token[m] from the argmax key, history append, key reset, position + 1.
+tb_status_t finish_step(unsigned long long* keys, int64_t* tokens, int64_t* history, int64_t* step, int64_t* pos,
+                        int M, int64_t hist_cap, cudaStream_t st, bool pdl);
+
+}  // namespace tb
