@@ -379,7 +379,6 @@ def run_ours(args):
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
-    del np, math
 
 
 def main():

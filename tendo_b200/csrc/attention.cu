@@ -30,32 +30,59 @@ template <>
 struct VecT<4> {
   using T = float4;
 };
+template <>
+struct VecT<1> {
+  using T = float;
+};
 
 template <int VEC>
 __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
   if constexpr (VEC == 4) {
     float4 t = *reinterpret_cast<const float4*>(p);
     r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+  } else if constexpr (VEC == 1) {
+    r[0] = *p;
   } else {
     float2 t = *reinterpret_cast<const float2*>(p);
     r[0] = t.x; r[1] = t.y;
   }
 }
 
-// grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv head.
+// grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv
+// head.  Each warp takes tiles of U consecutive positions: U K rows and U V
+// rows are loaded at once (2 U 16-byte loads in flight per lane for D = 128),
+// the U scores reduced together, and the running softmax updated once per tile.
 template <int VEC, int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int D = VEC * 32;
+  constexpr int U = 8;
   __shared__ float sm_o[kAttnWarps][G][D];
   __shared__ float sm_ml[kAttnWarps][G][2];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  pdl_launch_dependents();
+  // The position and every cached row before it were written by earlier
+  // decode steps, complete before the preceding kernel could launch this one;
+  // only row *pos comes from that kernel, so the older rows are prefetched
+  // into L2 before waiting on it.
   const int64_t sk = a.pos ? (*a.pos + 1) : a.sk;
-  const int64_t chunk = (sk + a.nsplit - 1) / a.nsplit;
+  int64_t chunk = (sk + a.nsplit - 1) / a.nsplit;
+  chunk = (chunk + U - 1) / U * U;
   const int64_t start = (int64_t)split * chunk;
   const int64_t end = min(start + chunk, sk);
+  const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  {
+    const int64_t pend = min(end, sk - 1);
+    const int lines = D * 4 / 128;
+    for (int64_t t = threadIdx.x; t < (pend - start) * lines; t += kAttnThreads) {
+      const int64_t j = start + t / lines;
+      const int off = (int)(t % lines) * 32;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kb + j * D + off));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + j * D + off));
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
 
   float qr[G][VEC];
 #pragma unroll
@@ -69,38 +96,53 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArg
 #pragma unroll
     for (int e = 0; e < VEC; e++) o[gi][e] = 0.f;
   }
-  const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  constexpr int U = 4;  // positions in flight per warp
-  for (int64_t j0 = start + warp; j0 < end; j0 += kAttnWarps * U) {
+  for (int64_t j0 = start + (int64_t)warp * U; j0 < end; j0 += (int64_t)kAttnWarps * U) {
     float kr[U][VEC], vr[U][VEC];
 #pragma unroll
     for (int u = 0; u < U; u++) {
-      const int64_t j = j0 + (int64_t)u * kAttnWarps;
+      const int64_t j = j0 + u;
       if (j < end) {
         load_vec<VEC>(kr[u], kb + j * D + lane * VEC);
         load_vec<VEC>(vr[u], vb + j * D + lane * VEC);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; e++) kr[u][e] = vr[u][e] = 0.f;
       }
     }
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const int64_t j = j0 + (int64_t)u * kAttnWarps;
-      if (j >= end) break;
+    for (int gi = 0; gi < G; gi++) {
+      float s[U];
 #pragma unroll
-      for (int gi = 0; gi < G; gi++) {
+      for (int u = 0; u < U; u++) {
         float d = 0.f;
 #pragma unroll
         for (int e = 0; e < VEC; e++) d = fmaf(qr[gi][e], kr[u][e], d);
-        d = warp_sum(d);
-        const float s = d * a.scale;
-        const float mn = fmaxf(mx[gi], s);
-        const float corr = expf(mx[gi] - mn);
-        const float p = expf(s - mn);
-        l[gi] = l[gi] * corr + p;
-#pragma unroll
-        for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e] * corr);
-        mx[gi] = mn;
+        s[u] = d;
       }
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        s[u] = (j0 + u < end) ? s[u] * a.scale : -INFINITY;
+        tmax = fmaxf(tmax, s[u]);
+      }
+      const float mn = fmaxf(mx[gi], tmax);  // finite: position j0 < end is valid
+      const float corr = expf(mx[gi] - mn);
+      float psum = 0.f;
+#pragma unroll
+      for (int e = 0; e < VEC; e++) o[gi][e] *= corr;
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const float p = expf(s[u] - mn);
+        psum += p;
+#pragma unroll
+        for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e]);
+      }
+      l[gi] = l[gi] * corr + psum;
+      mx[gi] = mn;
     }
   }
   // merge the warps of this CTA
@@ -274,6 +316,7 @@ tb_status_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
 
 template <int VEC>
 tb_status_t launch_decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  if (VEC == 1 && a.H / a.Hkv > 4) return TB_ERROR_NOT_SUPPORTED;
   switch (a.H / a.Hkv) {
     case 1: return launch_decode<VEC, 1>(a, st, pdl);
     case 2: return launch_decode<VEC, 2>(a, st, pdl);
@@ -287,8 +330,8 @@ tb_status_t launch_decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) 
 
 int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq) {
   (void)H;
-  // About two waves of CTAs over the SMs, never a split shorter than 16 keys.
-  int64_t want = (2LL * sm_count() + (int64_t)B * Hkv - 1) / ((int64_t)B * Hkv);
+  // About four CTAs per SM, never a split shorter than 16 keys.
+  int64_t want = (4LL * sm_count() + (int64_t)B * Hkv - 1) / ((int64_t)B * Hkv);
   int64_t cap = (max_seq + 15) / 16;
   if (want > cap) want = cap;
   if (want > 64) want = 64;
@@ -303,6 +346,7 @@ tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.Hkv > 0 && a.H % a.Hkv == 0);
   if (a.D == 128) return launch_decode_g<4>(a, st, pdl);
   if (a.D == 64) return launch_decode_g<2>(a, st, pdl);
+  if (a.D == 32) return launch_decode_g<1>(a, st, pdl);
   return TB_ERROR_NOT_SUPPORTED;
 }
 
@@ -314,6 +358,8 @@ tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const 
     attn_prefill_kernel<128><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
   } else if (D == 64) {
     attn_prefill_kernel<64><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
+  } else if (D == 32) {
+    attn_prefill_kernel<32><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
   } else {
     return TB_ERROR_NOT_SUPPORTED;
   }

@@ -10,8 +10,14 @@
 namespace tb {
 namespace {
 
-__device__ __forceinline__ int group_stride() { return gridDim.x * kGemvWarps; }
-__device__ __forceinline__ int first_group() { return blockIdx.x * kGemvWarps + (threadIdx.x >> 5); }
+__device__ __forceinline__ int group_stride() { return gridDim.x * (blockDim.x >> 5); }
+__device__ __forceinline__ int first_group() { return blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); }
+
+// Loads in flight per lane: U chunks of each of ROWS rows.
+template <int MT, int ROWS>
+struct Unroll {
+  static constexpr int U = (MT <= 2 ? 8 : 4) / ROWS;
+};
 
 // ---------------------------------------------------------------------------
 // Plain GEMV: out[m, n] = scale[n] * x[m, :] . q[n, :] (+ resid[m, n]).
@@ -22,7 +28,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_plain_kernel(float* out, co
                                                                   const float* __restrict__ scale,
                                                                   const float* resid, int M, int N, int K,
                                                                   const float* __restrict__ norm_w, float eps) {
-  constexpr int ROWS = 4;
+  constexpr int ROWS = 1;
   extern __shared__ __align__(16) float xs[];
   const int ngroups = (N + ROWS - 1) / ROWS;
   int g = first_group();
@@ -39,7 +45,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_plain_kernel(float* out, co
 #pragma unroll
     for (int r = 0; r < ROWS; r++) rp[r] = q + (size_t)min(g * ROWS + r, N - 1) * K;
     float acc[ROWS][MT];
-    gemv_rows<MT, ROWS>(acc, rp, xs, K);
+    gemv_rows<MT, ROWS, Unroll<MT, ROWS>::U>(acc, rp, xs, K);
     if ((threadIdx.x & 31) == 0) {
 #pragma unroll
       for (int r = 0; r < ROWS; r++) {
@@ -68,23 +74,19 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_plain_kernel(float* out, co
 // ---------------------------------------------------------------------------
 template <int MT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_qkv_rope_kernel(QkvArgs a) {
-  constexpr int ROWS = 4;  // two rotate-half pairs
+  constexpr int ROWS = 2;  // one rotate-half pair
   extern __shared__ __align__(16) float xs[];
   const int half = a.D / 2;
   const int npairs = (a.H + 2 * a.Hkv) * half;
-  const int ngroups = (npairs + 1) / 2;
+  const int ngroups = npairs;
   const int K = a.d;
   int g = first_group();
   const int8_t* rp[ROWS];
   int rows[ROWS];
   auto map = [&](int gg) {
-#pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int pr = min(2 * gg + p, npairs - 1);
-      const int t = pr / half, i = pr - t * half;
-      rows[2 * p] = t * a.D + i;
-      rows[2 * p + 1] = t * a.D + i + half;
-    }
+    const int t = gg / half, i = gg - t * half;
+    rows[0] = t * a.D + i;
+    rows[1] = t * a.D + i + half;
 #pragma unroll
     for (int r = 0; r < ROWS; r++) rp[r] = a.q + (size_t)rows[r] * K;
   };
@@ -99,13 +101,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_qkv_rope_kernel(QkvArgs a) 
   for (; g < ngroups; g += group_stride()) {
     map(g);
     float acc[ROWS][MT];
-    gemv_rows<MT, ROWS>(acc, rp, xs, K);
+    gemv_rows<MT, ROWS, Unroll<MT, ROWS>::U>(acc, rp, xs, K);
     const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int pr = 2 * g + p;
-      if (pr >= npairs) continue;
-      const int t = pr / half, i = pr - t * half;
+    {
+      constexpr int p = 0;
+      const int t = g / half, i = g - t * half;
       const float s0 = a.scale[rows[2 * p]], s1 = a.scale[rows[2 * p + 1]];
       const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
 #pragma unroll
@@ -137,19 +137,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_qkv_rope_kernel(QkvArgs a) 
 // ---------------------------------------------------------------------------
 template <int MT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_gateup_kernel(GateUpArgs a) {
-  constexpr int ROWS = 4;
+  constexpr int ROWS = 2;
   extern __shared__ __align__(16) float xs[];
   const int K = a.d, F = a.F;
-  const int ngroups = (F + 1) / 2;
+  const int ngroups = F;
   int g = first_group();
   const int8_t* rp[ROWS];
   auto map = [&](int gg) {
-#pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int j = min(2 * gg + p, F - 1);
-      rp[2 * p] = a.gate + (size_t)j * K;
-      rp[2 * p + 1] = a.up + (size_t)j * K;
-    }
+    rp[0] = a.gate + (size_t)gg * K;
+    rp[1] = a.up + (size_t)gg * K;
   };
   if (g < ngroups) {
     map(g);
@@ -161,12 +157,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_gateup_kernel(GateUpArgs a)
   for (; g < ngroups; g += group_stride()) {
     map(g);
     float acc[ROWS][MT];
-    gemv_rows<MT, ROWS>(acc, rp, xs, K);
+    gemv_rows<MT, ROWS, Unroll<MT, ROWS>::U>(acc, rp, xs, K);
     const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int j = 2 * g + p;
-      if (j >= F) continue;
+    {
+      constexpr int p = 0;
+      const int j = g;
       const float sg = a.gate_scale[j], su = a.up_scale[j];
 #pragma unroll
       for (int m = 0; m < MT; m++) {
@@ -234,7 +229,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_lmhead_kernel(LmHeadArgs a)
 #pragma unroll
     for (int m = 0; m < MT; m++) {
       float s = 0.f;
-      for (int w = 0; w < kGemvWarps; w++) s += red[m * kGemvWarps + w];
+      for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[m * kGemvWarps + w];
       rms[m] = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), a.eps));
     }
     for (int v = threadIdx.x; v < K / 4; v += blockDim.x) {
@@ -363,10 +358,10 @@ __global__ void gemv_generic_kernel(float* out, const float* __restrict__ x, con
 }
 
 template <typename Kern, typename... Args>
-tb_status_t launch(Kern kern, unsigned grid, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+tb_status_t launch(Kern kern, GemvPlan plan, size_t smem, cudaStream_t st, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(plan.warps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -388,12 +383,10 @@ tb_status_t set_smem(Kern kern, size_t smem) {
   return TB_SUCCESS;
 }
 
-// CTAs per SM the GEMVs aim for (persistent grid).
-unsigned gemv_grid(int64_t groups, size_t smem) {
-  int per_sm = smem <= 40 * 1024 ? 4 : (smem <= 72 * 1024 ? 3 : (smem <= 110 * 1024 ? 2 : 1));
-  int64_t want = (groups + kGemvWarps - 1) / kGemvWarps;
-  int64_t cap = (int64_t)sm_count() * per_sm;
-  return (unsigned)(want < cap ? (want < 1 ? 1 : want) : cap);
+// One CTA per SM, warps chosen so the tasks divide evenly (gemv.cuh).
+GemvPlan gemv_grid(int64_t tasks, size_t smem) {
+  (void)smem;
+  return gemv_plan(tasks, sm_count(), kGemvWarps);
 }
 
 int mt_for(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
@@ -422,7 +415,7 @@ tb_status_t gemv_plain(float* out, const float* x, const int8_t* q, const float*
     const int mm = M - m0 < mt_cap ? M - m0 : mt_cap;
     const int MT = mt_for(mm);
     const size_t smem = gemv_smem_bytes(MT, K);
-    const unsigned grid = gemv_grid((N + 3) / 4, smem);
+    const GemvPlan grid = gemv_grid(N, smem);
     float* o = out + (size_t)m0 * N;
     const float* xx = x + (size_t)m0 * K;
     const float* rr = resid ? resid + (size_t)m0 * N : nullptr;
@@ -462,8 +455,8 @@ tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0 && a.D % 2 == 0);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);
-  const int64_t groups = ((int64_t)(a.H + 2 * a.Hkv) * (a.D / 2) + 1) / 2;
-  const unsigned grid = gemv_grid(groups, smem);
+  const int64_t groups = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 2);
+  const GemvPlan grid = gemv_grid(groups, smem);
   switch (MT) {
     case 1: TB_TRY(set_smem(gemv_qkv_rope_kernel<1>, smem)); return launch(gemv_qkv_rope_kernel<1>, grid, smem, st, pdl, a);
     case 2: TB_TRY(set_smem(gemv_qkv_rope_kernel<2>, smem)); return launch(gemv_qkv_rope_kernel<2>, grid, smem, st, pdl, a);
@@ -476,7 +469,7 @@ tb_status_t gemv_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);
-  const unsigned grid = gemv_grid((a.F + 1) / 2, smem);
+  const GemvPlan grid = gemv_grid(a.F, smem);
   switch (MT) {
     case 1: TB_TRY(set_smem(gemv_gateup_kernel<1>, smem)); return launch(gemv_gateup_kernel<1>, grid, smem, st, pdl, a);
     case 2: TB_TRY(set_smem(gemv_gateup_kernel<2>, smem)); return launch(gemv_gateup_kernel<2>, grid, smem, st, pdl, a);
@@ -489,7 +482,7 @@ tb_status_t gemv_lmhead(const LmHeadArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 4 == 0);
   const int MT = mt_for(a.M);
   const size_t smem = (size_t)MT * a.d * sizeof(float) + 8 * kGemvWarps * sizeof(float);
-  const unsigned grid = gemv_grid((a.V + 1) / 2, smem);
+  const GemvPlan grid = gemv_grid((a.V + 1) / 2, smem);
   switch (MT) {
     case 1: TB_TRY(set_smem(gemv_lmhead_kernel<1>, smem)); return launch(gemv_lmhead_kernel<1>, grid, smem, st, pdl, a);
     case 2: TB_TRY(set_smem(gemv_lmhead_kernel<2>, smem)); return launch(gemv_lmhead_kernel<2>, grid, smem, st, pdl, a);

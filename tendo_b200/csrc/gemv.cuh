@@ -22,7 +22,7 @@
 
 namespace tb {
 
-constexpr int kGemvThreads = 512;
+constexpr int kGemvThreads = 512;  // upper bound of the block size
 constexpr int kGemvWarps = kGemvThreads / 32;
 
 // Stage x rows into shared memory (permuted float4 layout).  With `norm`
@@ -84,9 +84,11 @@ __device__ __forceinline__ void stage_x(float* xs, const float* __restrict__ x, 
   __syncthreads();
 }
 
-// Dot products of ROWS weight rows with MT staged x rows over the K range
-// of this lane.  row_ptr[r] points at row r's first byte.
-template <int MT, int ROWS>
+// Dot products of ROWS weight rows with MT staged x rows.  row_ptr[r] points
+// at row r's first byte.  Each lane walks chunks lane, lane + 32, ...; every
+// iteration issues U chunks of every row (U * ROWS 16-byte loads in flight
+// per lane) before consuming them.
+template <int MT, int ROWS, int U>
 __device__ __forceinline__ void gemv_rows(float (&acc)[ROWS][MT], const int8_t* const (&row_ptr)[ROWS],
                                           const float* xs, int K) {
   const int lane = threadIdx.x & 31;
@@ -97,65 +99,38 @@ __device__ __forceinline__ void gemv_rows(float (&acc)[ROWS][MT], const int8_t* 
 #pragma unroll
     for (int m = 0; m < MT; m++) acc[r][m] = 0.f;
 
-  int c = lane;
-  // Two chunks per lane per iteration keeps 2 * ROWS 16-byte loads in flight.
-  for (; c + 32 < chunks; c += 64) {
-    int4 w0[ROWS], w1[ROWS];
+  for (int c0 = lane; c0 < chunks; c0 += 32 * U) {
+    int4 w[U][ROWS];
 #pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-      w0[r] = ld_stream_v4(row_ptr[r] + 16 * c);
-      w1[r] = ld_stream_v4(row_ptr[r] + 16 * (c + 32));
+    for (int u = 0; u < U; u++) {
+      const int c = c0 + 32 * u;
+#pragma unroll
+      for (int r = 0; r < ROWS; r++) w[u][r] = c < chunks ? ld_stream_v4(row_ptr[r] + 16 * c) : make_int4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int cc = c + 32 * h;
+    for (int u = 0; u < U; u++) {
+      const int c = c0 + 32 * u;
+      if (c >= chunks) break;
 #pragma unroll
       for (int m = 0; m < MT; m++) {
-        float4 x0 = xv[(m * 4 + 0) * chunks + cc];
-        float4 x1 = xv[(m * 4 + 1) * chunks + cc];
-        float4 x2 = xv[(m * 4 + 2) * chunks + cc];
-        float4 x3 = xv[(m * 4 + 3) * chunks + cc];
+        const float4 x0 = xv[(m * 4 + 0) * chunks + c];
+        const float4 x1 = xv[(m * 4 + 1) * chunks + c];
+        const float4 x2 = xv[(m * 4 + 2) * chunks + c];
+        const float4 x3 = xv[(m * 4 + 3) * chunks + c];
 #pragma unroll
         for (int r = 0; r < ROWS; r++) {
-          const int4 w = h ? w1[r] : w0[r];
           float a, b, cf, d;
           float s = acc[r][m];
-          i8x4_to_f32((uint32_t)w.x, a, b, cf, d);
+          i8x4_to_f32((uint32_t)w[u][r].x, a, b, cf, d);
           s = fmaf(x0.x, a, s); s = fmaf(x0.y, b, s); s = fmaf(x0.z, cf, s); s = fmaf(x0.w, d, s);
-          i8x4_to_f32((uint32_t)w.y, a, b, cf, d);
+          i8x4_to_f32((uint32_t)w[u][r].y, a, b, cf, d);
           s = fmaf(x1.x, a, s); s = fmaf(x1.y, b, s); s = fmaf(x1.z, cf, s); s = fmaf(x1.w, d, s);
-          i8x4_to_f32((uint32_t)w.z, a, b, cf, d);
+          i8x4_to_f32((uint32_t)w[u][r].z, a, b, cf, d);
           s = fmaf(x2.x, a, s); s = fmaf(x2.y, b, s); s = fmaf(x2.z, cf, s); s = fmaf(x2.w, d, s);
-          i8x4_to_f32((uint32_t)w.w, a, b, cf, d);
+          i8x4_to_f32((uint32_t)w[u][r].w, a, b, cf, d);
           s = fmaf(x3.x, a, s); s = fmaf(x3.y, b, s); s = fmaf(x3.z, cf, s); s = fmaf(x3.w, d, s);
           acc[r][m] = s;
         }
-      }
-    }
-  }
-  for (; c < chunks; c += 32) {
-    int4 w0[ROWS];
-#pragma unroll
-    for (int r = 0; r < ROWS; r++) w0[r] = ld_stream_v4(row_ptr[r] + 16 * c);
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
-      float4 x0 = xv[(m * 4 + 0) * chunks + c];
-      float4 x1 = xv[(m * 4 + 1) * chunks + c];
-      float4 x2 = xv[(m * 4 + 2) * chunks + c];
-      float4 x3 = xv[(m * 4 + 3) * chunks + c];
-#pragma unroll
-      for (int r = 0; r < ROWS; r++) {
-        float a, b, cf, d;
-        float s = acc[r][m];
-        i8x4_to_f32((uint32_t)w0[r].x, a, b, cf, d);
-        s = fmaf(x0.x, a, s); s = fmaf(x0.y, b, s); s = fmaf(x0.z, cf, s); s = fmaf(x0.w, d, s);
-        i8x4_to_f32((uint32_t)w0[r].y, a, b, cf, d);
-        s = fmaf(x1.x, a, s); s = fmaf(x1.y, b, s); s = fmaf(x1.z, cf, s); s = fmaf(x1.w, d, s);
-        i8x4_to_f32((uint32_t)w0[r].z, a, b, cf, d);
-        s = fmaf(x2.x, a, s); s = fmaf(x2.y, b, s); s = fmaf(x2.z, cf, s); s = fmaf(x2.w, d, s);
-        i8x4_to_f32((uint32_t)w0[r].w, a, b, cf, d);
-        s = fmaf(x3.x, a, s); s = fmaf(x3.y, b, s); s = fmaf(x3.z, cf, s); s = fmaf(x3.w, d, s);
-        acc[r][m] = s;
       }
     }
   }
@@ -163,6 +138,24 @@ __device__ __forceinline__ void gemv_rows(float (&acc)[ROWS][MT], const int8_t* 
   for (int r = 0; r < ROWS; r++)
 #pragma unroll
     for (int m = 0; m < MT; m++) acc[r][m] = warp_sum(acc[r][m]);
+}
+
+// Balanced persistent schedule: one CTA per SM, `tasks` spread over
+// gridDim.x * warps warps in rounds, so every SM gets the same number of
+// tasks to within one.
+struct GemvPlan {
+  unsigned grid;
+  unsigned warps;
+};
+
+inline GemvPlan gemv_plan(int64_t tasks, int sms, int max_warps) {
+  if (tasks < 1) tasks = 1;
+  const int64_t grid = tasks < sms ? tasks : sms;
+  const int64_t slots = grid * max_warps;
+  const int64_t rounds = (tasks + slots - 1) / slots;
+  int64_t warps = (tasks + grid * rounds - 1) / (grid * rounds);
+  if (warps < 1) warps = 1;
+  return GemvPlan{(unsigned)grid, (unsigned)warps};
 }
 
 // L2 prefetch of a row group (issued before waiting on the previous kernel:

@@ -1,0 +1,78 @@
+"""Quantized Linear microbench: tb_dequant_matmul_i8f32 on one GPU.
+
+    python -m tendo_b200.microbench [--M 1 8 32 128 2048] [--N 4096 11008] [--K 4096] [--iters 20]
+
+W [N, K] is drawn N(0, 0.02) (seed 42) and int8-quantized per output channel
+on the device; X [M, K] is N(0, 1) (seed 42).  Enough weight copies are
+rotated that every launch streams its weights from HBM, not L2 (126 MB).
+Prints one JSON line per (M, N): microseconds per launch (CUDA events),
+achieved GB/s over the algorithmic bytes N*K + 4N + 4MK + 4MN (the M <= 32
+regime is HBM-bound) and TFLOP/s over 2MNK.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+import tendo_b200 as tb
+
+
+def linear_bytes(M, N, K):
+    return N * K + 4 * N + 4 * M * K + 4 * M * N
+
+
+def run(Ms, Ns, K, iters, mode):
+    be = tb.Backend(0)
+    dev = torch.device("cuda:0")
+    rows = []
+    for N in Ns:
+        w = be.SynthNormal(N, K, 42, tb.STREAM_W, 0.02)
+        qt = be.Quantize(w, 0)
+        del w
+        copies = max(2, math.ceil(400e6 / (N * K)))
+        qs = [qt.data] + [qt.data.clone() for _ in range(copies - 1)]
+        for M in Ms:
+            x = be.SynthNormal(M, K, 42, tb.STREAM_X, 1.0)
+            out = torch.empty((M, N), dtype=torch.float32, device=dev)
+            st = torch.cuda.current_stream()
+            sh = tb._stream(st)
+
+            def launch(i):
+                tb.check(tb.lib.tb_dequant_matmul_i8f32_mode(out.data_ptr(), x.data_ptr(), qs[i % copies].data_ptr(),
+                                                             qt.scale.data_ptr(), M, N, K, 0, mode, sh))
+
+            for i in range(3):
+                launch(i)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            for i in range(iters):
+                launch(i)
+            b.record(st)
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1000.0 / iters
+            byts = linear_bytes(M, N, K)
+            row = {"M": M, "N": N, "K": K, "us": us, "GB_s": byts / (us * 1e-6) / 1e9,
+                   "TFLOP_s": 2.0 * M * N * K / (us * 1e-6) / 1e12, "bytes": byts,
+                   "regime": "gemv" if M <= 32 else "gemm", "weight_copies": copies}
+            rows.append(row)
+            print(json.dumps(row), flush=True)
+    return rows
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--M", type=int, nargs="+", default=[1, 8, 32, 128, 2048])
+    ap.add_argument("--N", type=int, nargs="+", default=[4096, 11008])
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--mode", type=int, default=tb.TB_GEMM_BF16X2)
+    a = ap.parse_args()
+    run(a.M, a.N, a.K, a.iters, a.mode)
+
+
+if __name__ == "__main__":
+    main()
