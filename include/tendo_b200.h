@@ -163,6 +163,26 @@ TB_API tb_status_t tb_attention_f32(float* out, const float* q, const float* kca
                              int64_t H, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int64_t max_seq,
                              float scale, void* workspace, size_t workspace_bytes, tb_stream_t stream);
 
+/* Decode attention (Sq == 1) that allocates nothing and takes no workspace.
+ * No counterpart in the reference: tendo allocates every buffer through its
+ * backend.  It exists for callers that cannot call cudaMalloc at all, such as
+ * a host that reserves the whole GPU into its own pools at start-up, or a
+ * foreign-language binding whose only device allocator is its own tensor
+ * pool and cannot lend a per-call scratch buffer.  Same math and result
+ * layout as tb_attention_f32 with Sq == 1.  Its split-K partials live in one
+ * library-owned device array of TB_ATTENTION_NOALLOC_SCRATCH_BYTES per GPU
+ * (kept until the process exits); sizes whose partials do not fit are
+ * rejected with TB_ERROR_INVALID_ARGUMENT.  The first call on a device looks
+ * up that array's address (cudaGetSymbolAddress) and caches it; make that
+ * first call before any stream capture.  Every call on a device shares the
+ * array, so calls that overlap on the GPU (different streams, or host
+ * threads without ordering) race and corrupt each other's partials. */
+#define TB_ATTENTION_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
+TB_API tb_status_t tb_attention_decode_noalloc_f32(float* out, const float* q, const float* kcache,
+                                                   const float* vcache, int64_t B, int64_t H, int64_t Hkv,
+                                                   int64_t Sk, int64_t D, int64_t max_seq, float scale,
+                                                   tb_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Embedding and sampling
  * ------------------------------------------------------------------------- */

@@ -57,6 +57,7 @@ SIGNATURES = [
     ("tb_attention_workspace_size", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     ("tb_attention_f32", _st,
      [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, ctypes.c_size_t, _vp]),
+    ("tb_attention_decode_noalloc_f32", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     ("tb_embedding_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     ("tb_argmax_f32", _st, [_vp, _vp, _i64, _i64, _vp]),
     ("tb_synth_normal_f32", _st, [_vp, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, _vp]),

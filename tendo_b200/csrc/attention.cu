@@ -11,6 +11,8 @@
 // kernel with the online softmax, so no [S, S] score matrix is stored.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -411,4 +413,77 @@ extern "C" tb_status_t tb_attention_f32(float* out, const float* q, const float*
   }
   return tb::attn_prefill(out, q, kcache, vcache, (int)B, (int)H, (int)Hkv, (int)Sq, Sk, (int)D, (int)max_seq, scale,
                           st);
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention without a caller workspace: the split-K partials go to a
+// library-owned device array instead of a buffer the caller allocates.  The
+// array is shared by every call on a GPU and keeps the previous call's
+// contents; nothing in it needs to start at zero (every split writes its
+// whole partial, empty splits included), but calls that overlap on the GPU
+// race on it.
+// ---------------------------------------------------------------------------
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_attn_scratch[TB_ATTENTION_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the host-side symbol is only a stand-in for it).
+tb_status_t noalloc_scratch(void** out) {
+  int dev = 0;
+  TB_CUDA(cudaGetDevice(&dev));
+  TB_REQUIRE(dev >= 0 && dev < kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
+    if (e != cudaSuccess) return tb::cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_attn_scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TB_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" tb_status_t tb_attention_decode_noalloc_f32(float* out, const float* q, const float* kcache,
+                                                       const float* vcache, int64_t B, int64_t H, int64_t Hkv,
+                                                       int64_t Sk, int64_t D, int64_t max_seq, float scale,
+                                                       tb_stream_t stream) {
+  TB_INJECT("tb_attention_decode_noalloc_f32");
+  TB_REQUIRE(B >= 0 && H > 0 && Hkv > 0 && H % Hkv == 0 && D > 0);
+  TB_REQUIRE(Sk >= 1 && Sk <= max_seq);
+  TB_REQUIRE(B <= 0x7fffffff && H <= 0x7fffffff && max_seq <= 0x7fffffff);
+  if (B == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && q && kcache && vcache);
+  TB_REQUIRE(tb::aligned(q, 16) && tb::aligned(kcache, 16) && tb::aligned(vcache, 16));
+  // As many splits as the caller-workspace path would use, capped by what
+  // fits in the scratch array; a single split that does not fit is rejected.
+  const size_t per_split = (size_t)B * H * (D + 2) * sizeof(float);
+  TB_REQUIRE(per_split <= TB_ATTENTION_NOALLOC_SCRATCH_BYTES);
+  int nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, max_seq);
+  const int fit = (int)(TB_ATTENTION_NOALLOC_SCRATCH_BYTES / per_split);
+  if (nsplit > fit) nsplit = fit;
+  void* scratch = nullptr;
+  TB_TRY(noalloc_scratch(&scratch));
+  tb::AttnDecodeArgs a{};
+  a.q = q;
+  a.kcache = kcache;
+  a.vcache = vcache;
+  a.out = out;
+  a.partial = (float*)scratch;
+  a.pos = nullptr;
+  a.sk = Sk;
+  a.B = (int)B;
+  a.H = (int)H;
+  a.Hkv = (int)Hkv;
+  a.D = (int)D;
+  a.max_seq = (int)max_seq;
+  a.nsplit = nsplit;
+  a.scale = scale;
+  return tb::attn_decode(a, (cudaStream_t)stream, false);
 }
