@@ -181,26 +181,44 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArg
   }
 }
 
-// grid (H, B), D threads: out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
-__global__ void attn_combine_kernel(float* out, const float* partial, int H, int D, int nsplit) {
-  const int h = blockIdx.x, b = blockIdx.y;
+// One warp per (sequence, head): out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+// Lane s holds split s's (m, l) (nsplit <= 64: two per lane), so the max and
+// the weighted sum of l are warp reductions; each lane then sums its D / 32
+// output elements over the splits with independent loads.
+template <int VEC>
+__global__ void attn_combine_kernel(float* out, const float* partial, int B, int H, int nsplit) {
+  constexpr int D = VEC * 32;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
-  const float* p = partial + ((size_t)b * H + h) * nsplit * (D + 2);
-  float m = -INFINITY;
-  for (int s = 0; s < nsplit; s++) m = fmaxf(m, p[(size_t)s * (D + 2) + D]);
-  for (int e = threadIdx.x; e < D; e += blockDim.x) {
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < nsplit; s++) {
-      const float* ps = p + (size_t)s * (D + 2);
-      const float ms = ps[D];
-      if (ms == -INFINITY) continue;
-      const float c = expf(ms - m);
-      L = fmaf(ps[D + 1], c, L);
-      O = fmaf(ps[e], c, O);
-    }
-    out[((size_t)b * H + h) * D + e] = O / L;
+  if (gw >= B * H) return;
+  const float* p = partial + (size_t)gw * nsplit * (D + 2);
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  if (lane < nsplit) {
+    m0 = p[(size_t)lane * (D + 2) + D];
+    l0 = p[(size_t)lane * (D + 2) + D + 1];
   }
+  if (lane + 32 < nsplit) {
+    m1 = p[(size_t)(lane + 32) * (D + 2) + D];
+    l1 = p[(size_t)(lane + 32) * (D + 2) + D + 1];
+  }
+  const float M = warp_max(fmaxf(m0, m1));
+  const float c0 = m0 == -INFINITY ? 0.f : expf(m0 - M);
+  const float c1 = m1 == -INFINITY ? 0.f : expf(m1 - M);
+  const float L = warp_sum(l0 * c0 + l1 * c1);
+  float acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; e++) acc[e] = 0.f;
+  for (int s = 0; s < nsplit; s++) {
+    const float c = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, s & 31);
+    if (c == 0.f) continue;
+    const float* ps = p + (size_t)s * (D + 2) + lane * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; e++) acc[e] = fmaf(ps[e], c, acc[e]);
+  }
+  float* o = out + (size_t)gw * D + lane * VEC;
+#pragma unroll
+  for (int e = 0; e < VEC; e++) o[e] = acc[e] / L;
 }
 
 // ---------------------------------------------------------------------------
@@ -309,9 +327,10 @@ tb_status_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G>, a);
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
-  cfg.gridDim = dim3(a.H, a.B);
-  cfg.blockDim = dim3(a.D);
-  e = cudaLaunchKernelEx(&cfg, attn_combine_kernel, a.out, (const float*)a.partial, a.H, a.D, a.nsplit);
+  const int warps = a.B * a.H;
+  cfg.gridDim = dim3((warps + 3) / 4);
+  cfg.blockDim = dim3(128);
+  e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<VEC>, a.out, (const float*)a.partial, a.B, a.H, a.nsplit);
   if (e != cudaSuccess) return cuda_fail(e, "attn_combine_kernel");
   return TB_SUCCESS;
 }

@@ -3,6 +3,8 @@
 // (RMSNorm prologue; RoPE + KV append, residual and SwiGLU epilogues; the
 // fp32 lm_head with a fused greedy argmax).
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "gemv.cuh"
 #include "kernels.h"
@@ -408,8 +410,24 @@ bool gemv_fast_ok(const float* x, const int8_t* q, int64_t K) {
   return K % 16 == 0 && aligned(x, 16) && aligned(q, 16) && gemv_smem_bytes(1, (int)K) <= 200 * 1024;
 }
 
+bool gemv_use_mma() {
+  static const bool use = [] {
+    const char* e = getenv("TENDO_B200_GEMV");
+    return !(e && strcmp(e, "simt") == 0);
+  }();
+  return use;
+}
+
 tb_status_t gemv_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
                        int M, int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl) {
+  if (gemv_use_mma() && gemv_mma_ok(x, q, M < 8 ? M : 8, K)) {
+    for (int m0 = 0; m0 < M; m0 += 8) {
+      const int mm = M - m0 < 8 ? M - m0 : 8;
+      TB_TRY(gemv_mma_plain(out + (size_t)m0 * N, x + (size_t)m0 * K, q, scale,
+                            resid ? resid + (size_t)m0 * N : nullptr, mm, N, K, norm_w, eps, st, pdl));
+    }
+    return TB_SUCCESS;
+  }
   const int mt_cap = max_mt_for_k(K);
   for (int m0 = 0; m0 < M; m0 += mt_cap) {
     const int mm = M - m0 < mt_cap ? M - m0 : mt_cap;
@@ -453,6 +471,7 @@ tb_status_t gemv_generic(float* out, const float* x, const int8_t* q, const floa
 
 tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0 && a.D % 2 == 0);
+  if (gemv_use_mma() && a.D % 8 == 0 && gemv_mma_ok(a.h, a.q, a.M, a.d)) return gemv_mma_qkv(a, st, pdl);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);
   const int64_t groups = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 2);
@@ -467,6 +486,7 @@ tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl) {
 
 tb_status_t gemv_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0);
+  if (gemv_use_mma() && gemv_mma_ok(a.h, a.gate, a.M, a.d) && tb::aligned(a.up, 16)) return gemv_mma_gateup(a, st, pdl);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);
   const GemvPlan grid = gemv_grid(a.F, smem);

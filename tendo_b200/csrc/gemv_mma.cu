@@ -1,0 +1,495 @@
+// gemv_mma.cu — decode-regime dequant GEMV on the tensor cores.
+//
+// y[m, n] = scale[n] * sum_k x[m, k] * q[n, k] for M <= 8 batch rows.
+//
+// Why the tensor cores for a bandwidth-bound GEMV: on the CUDA cores every
+// int8 weight costs a byte permute, a convert-add and an FMA (3+ issue slots
+// per byte), which left the streaming kernel issue-bound at 45% DRAM
+// throughput.  Here 16 weight bytes of one lane become 8 f16x2 operands
+// (xor + byte permute + HSUB2, exact: int8 values are exact in f16) and four
+// mma.m16n8k16 instructions do the 2 * 16 * 8 * 16 multiply-adds, about 1.6
+// issue slots per weight byte.
+//
+// Operand layout.  A (16 x 16) = x: rows 0..7 are the f16 "hi" parts of the
+// batch rows, rows 8..15 the "lo" parts (x = hi + lo exactly to ~22 bits),
+// so y = D[m] + D[m + 8].  B (16 x 8) = W^T: column n is weight row row(n) of
+// an 8-row tile.  The k order inside an mma is free as long as A and B agree:
+// lane (g = lane / 4, t = lane % 4) loads 16 contiguous bytes of row row(g)
+// at k = 64 kb + 16 t, and mma j of the k-block uses its bytes 4j .. 4j+3 as
+// k-slots {2t, 2t+1} and {2t+8, 2t+9}; the lane's A registers hold x at the
+// same 16 k.  Each x row is kept as fp32 scaled by a power of two so its
+// largest value fits f16 comfortably; the scale is undone on the result.
+//
+// Schedule.  A CTA owns 8-row tiles (tile, tile + grid, ...); its W warps split
+// K (warp w takes k-blocks w, w + W, ...), each lane keeping KPW 16-byte loads
+// in flight per tile.  Partial tiles are summed across warps in shared memory
+// (double-buffered, one barrier per tile) and the epilogue (scale, residual,
+// RoPE + KV append, SwiGLU) runs on the reduced values.  The first tile's
+// weights are requested before griddepcontrol.wait, so under programmatic
+// dependent launch they stream while the previous kernel finishes.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tb {
+namespace {
+
+constexpr int kPad = 8;  // halves of padding per staged x row (bank spread)
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two signed bytes (positions lo, lo+1 of u ^ 0x80808080) as an exact f16x2.
+__device__ __forceinline__ uint32_t i8pair_to_f16x2(uint32_t ux, uint32_t sel) {
+  const uint32_t raw = __byte_perm(ux, 0x64646464u, sel);  // 1024 + (b + 128) per half
+  const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&raw), __halves2half2(__ushort_as_half(0x6480),
+                                                                                     __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+struct MmaSmem {
+  // hi[MT][K + kPad], lo[MT][K + kPad] halves; then per-row scales; then the
+  // double-buffered partial tiles red[2][W][8 m][8 n].
+  static __host__ __device__ size_t x_halves(int MT, int K) { return (size_t)MT * (K + kPad); }
+  static __host__ __device__ size_t bytes(int MT, int K, int W) {
+    return 2 * x_halves(MT, K) * 2 + 16 * sizeof(float) + (size_t)2 * W * 64 * sizeof(float) +
+           (size_t)2 * 8 * 32 * sizeof(float);
+  }
+};
+
+// Stage x (optionally RMSNorm(x) * w) as f16 hi/lo rows scaled by 2^-e_m.
+template <int MT>
+__device__ void stage_x_f16(__half* hi, __half* lo, float* xscale, const float* __restrict__ x, int M, int K,
+                            const float* __restrict__ norm_w, float eps, float* red) {
+  const int nthreads = blockDim.x, warps = nthreads >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = K >> 2;
+  // pass 1: sum of squares (RMSNorm) and max |x| per row
+  float ss[MT], mx[MT];
+#pragma unroll
+  for (int m = 0; m < MT; m++) ss[m] = mx[m] = 0.f;
+  for (int v = threadIdx.x; v < nv; v += nthreads) {
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      if (m < M) {
+        const float4 t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
+        ss[m] += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        float a = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
+        if (norm_w) {
+          const float4 w = reinterpret_cast<const float4*>(norm_w)[v];
+          a = fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w)));
+        }
+        mx[m] = fmaxf(mx[m], a);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    float s = warp_sum(ss[m]), a = warp_max(mx[m]);
+    if (lane == 0) {
+      red[(2 * m) * 32 + warp] = s;
+      red[(2 * m + 1) * 32 + warp] = a;
+    }
+  }
+  __syncthreads();
+  float rms[MT], inv_sc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    float s = 0.f, a = 0.f;
+    for (int w = 0; w < warps; w++) {
+      s += red[(2 * m) * 32 + w];
+      a = fmaxf(a, red[(2 * m + 1) * 32 + w]);
+    }
+    rms[m] = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)) : 1.0f;
+    if (norm_w) a = a / rms[m] * 1.0001f;
+    // power of two that brings max |x| to [2^13, 2^14): exact rescaling
+    int e = 0;
+    if (a > 0.f && isfinite(a)) {
+      frexpf(a, &e);  // a = f * 2^e, f in [0.5, 1)
+      e -= 14;
+    }
+    inv_sc[m] = ldexpf(1.0f, -e);
+    if (threadIdx.x == 0) xscale[m] = ldexpf(1.0f, e);
+  }
+  // pass 2: values -> hi/lo halves
+  for (int v = threadIdx.x; v < nv; v += nthreads) {
+    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w) w4 = reinterpret_cast<const float4*>(norm_w)[v];
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < M) {
+        t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
+        if (norm_w) {
+          t.x = __fmul_rn(__fdiv_rn(t.x, rms[m]), w4.x);
+          t.y = __fmul_rn(__fdiv_rn(t.y, rms[m]), w4.y);
+          t.z = __fmul_rn(__fdiv_rn(t.z, rms[m]), w4.z);
+          t.w = __fmul_rn(__fdiv_rn(t.w, rms[m]), w4.w);
+        }
+        t.x *= inv_sc[m];
+        t.y *= inv_sc[m];
+        t.z *= inv_sc[m];
+        t.w *= inv_sc[m];
+      }
+      const float vals[4] = {t.x, t.y, t.z, t.w};
+      __half h[4], l[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        h[i] = __float2half_rn(vals[i]);
+        l[i] = __float2half_rn(vals[i] - __half2float(h[i]));
+      }
+      __half* hp = hi + (size_t)m * (K + kPad) + 4 * v;
+      __half* lp = lo + (size_t)m * (K + kPad) + 4 * v;
+      *reinterpret_cast<__half2*>(hp) = __halves2half2(h[0], h[1]);
+      *reinterpret_cast<__half2*>(hp + 2) = __halves2half2(h[2], h[3]);
+      *reinterpret_cast<__half2*>(lp) = __halves2half2(l[0], l[1]);
+      *reinterpret_cast<__half2*>(lp + 2) = __halves2half2(l[2], l[3]);
+    }
+  }
+  __syncthreads();
+}
+
+// Row-tile plans: which 8 weight rows (one per B column) a tile covers.
+struct PlainTiles {
+  const int8_t* q;
+  int N, K;
+  __device__ int tiles() const { return (N + 7) / 8; }
+  __device__ const int8_t* row(int tile, int n) const { return q + (size_t)min(tile * 8 + n, N - 1) * K; }
+};
+struct QkvTiles {  // 4 rotate-half pairs: columns n and n + 4 are rows i and i + D/2 of one head
+  const int8_t* q;
+  int heads, D, K;
+  __device__ int tiles() const { return heads * (D / 8); }
+  __device__ int head(int tile) const { return tile / (D / 8); }
+  __device__ int i0(int tile) const { return (tile % (D / 8)) * 4; }
+  __device__ const int8_t* row(int tile, int n) const {
+    const int r = head(tile) * D + i0(tile) + (n & 3) + (n >> 2) * (D / 2);
+    return q + (size_t)r * K;
+  }
+};
+struct GateUpTiles {  // columns 0..3: gate rows j0..j0+3; 4..7: the same up rows
+  const int8_t* gate;
+  const int8_t* up;
+  int F, K;
+  __device__ int tiles() const { return (F + 3) / 4; }
+  __device__ const int8_t* row(int tile, int n) const {
+    const int j = min(tile * 4 + (n & 3), F - 1);
+    return ((n >> 2) ? up : gate) + (size_t)j * K;
+  }
+};
+
+// One warp's share of one tile: k-blocks warp, warp + W, ... (KPW at most).
+template <int KPW>
+__device__ __forceinline__ void load_tile(int4 (&w)[KPW], const int8_t* rowp, int KB, int W, int warp, int t,
+                                          int i0) {
+#pragma unroll
+  for (int i = 0; i < KPW; i++) {
+    const int kb = warp + W * (i0 + i);
+    w[i] = kb < KB ? ld_stream_v4(rowp + (size_t)kb * 64 + 16 * t) : make_int4(0, 0, 0, 0);
+  }
+}
+
+template <int MT, int KPW>
+__device__ __forceinline__ void mma_tile(float (&d)[4], const int4 (&w)[KPW], const __half* hi, const __half* lo,
+                                         int K, int KB, int W, int warp, int g, int t, int i0) {
+#pragma unroll
+  for (int i = 0; i < KPW; i++) {
+    const int kb = warp + W * (i0 + i);
+    if (kb >= KB) break;
+    uint32_t xh[8], xl[8];
+    if (g < MT) {
+      const uint4* ph = reinterpret_cast<const uint4*>(hi + (size_t)g * (K + kPad) + kb * 64 + 16 * t);
+      const uint4* pl = reinterpret_cast<const uint4*>(lo + (size_t)g * (K + kPad) + kb * 64 + 16 * t);
+      const uint4 h0 = ph[0], h1 = ph[1], l0 = pl[0], l1 = pl[1];
+      xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
+      xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
+      xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
+      xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
+    } else {
+#pragma unroll
+      for (int p = 0; p < 8; p++) xh[p] = xl[p] = 0u;
+    }
+    const uint32_t words[4] = {(uint32_t)w[i].x, (uint32_t)w[i].y, (uint32_t)w[i].z, (uint32_t)w[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint32_t ux = words[j] ^ 0x80808080u;
+      const uint32_t b0 = i8pair_to_f16x2(ux, 0x4140);
+      const uint32_t b1 = i8pair_to_f16x2(ux, 0x4342);
+      const uint32_t a[4] = {xh[2 * j], xl[2 * j], xh[2 * j + 1], xl[2 * j + 1]};
+      mma_16816(d, a, b0, b1);
+    }
+  }
+}
+
+// Partial tile of this warp -> red[buf][warp][m][n] (m < MT): y = D[m] + D[m + 8].
+template <int MT>
+__device__ __forceinline__ void store_partial(float* red, const float (&d)[4], int warp, int g, int t) {
+  if (g < MT) {
+    float* r = red + (size_t)warp * 64 + g * 8 + 2 * t;
+    r[0] = d[0] + d[2];
+    r[1] = d[1] + d[3];
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ float reduce_partial(const float* red, int W, int m, int n) {
+  float s = 0.f;
+  for (int w = 0; w < W; w++) s += red[(size_t)w * 64 + m * 8 + n];
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// Generic driver.  Tiles maps tiles to rows; Epi(tile, m, n, y, valid) is
+// called by whole warps (threads m * 8 + n), so partner columns n and n ^ 4
+// can meet through __shfl_xor_sync(.., 4); y already carries the x scale.
+// ---------------------------------------------------------------------------
+template <int MT, int KPW, typename Tiles, typename Epi>
+__device__ __forceinline__ void gemv_mma_body(const Tiles& tiles, const Epi& epi, const float* __restrict__ x,
+                                              int M, int K, const float* __restrict__ norm_w, float eps) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* hi = reinterpret_cast<__half*>(smem);
+  __half* lo = hi + MmaSmem::x_halves(MT, K);
+  float* xscale = reinterpret_cast<float*>(lo + MmaSmem::x_halves(MT, K));
+  const int W = blockDim.x >> 5;
+  float* red = xscale + 16;  // [2][W][64]
+  float* scratch = red + 2 * W * 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int KB = K >> 6;
+  const int ntiles = tiles.tiles();
+  const int nrounds = ((KB + W - 1) / W + KPW - 1) / KPW;
+  int tile = blockIdx.x;
+  int4 w[KPW];
+  if (tile < ntiles) load_tile<KPW>(w, tiles.row(tile, g), KB, W, warp, t, 0);
+  pdl_wait();
+  pdl_launch_dependents();
+  stage_x_f16<MT>(hi, lo, xscale, x, M, K, norm_w, eps, scratch);
+  constexpr int kEpiThreads = ((MT * 8 + 31) / 32) * 32;
+  int buf = 0;
+  for (; tile < ntiles; tile += gridDim.x) {
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    const int8_t* rowp = tiles.row(tile, g);
+    for (int r = 0; r < nrounds; r++) {
+      if (r > 0) load_tile<KPW>(w, rowp, KB, W, warp, t, r * KPW);
+      mma_tile<MT, KPW>(d, w, hi, lo, K, KB, W, warp, g, t, r * KPW);
+    }
+    const int next = tile + gridDim.x;
+    if (next < ntiles) load_tile<KPW>(w, tiles.row(next, g), KB, W, warp, t, 0);
+    float* rb = red + (size_t)buf * W * 64;
+    store_partial<MT>(rb, d, warp, g, t);
+    __syncthreads();
+    if (threadIdx.x < kEpiThreads) {
+      const int m = threadIdx.x >> 3, n = threadIdx.x & 7;
+      const bool valid = m < M && m < MT;
+      const float y = valid ? reduce_partial<MT>(rb, W, m, n) * xscale[m] : 0.f;
+      epi(tile, m, n, y, valid);
+    }
+    buf ^= 1;
+  }
+}
+
+struct PlainEpi {
+  float* out;
+  const float* scale;
+  const float* resid;
+  int N;
+  __device__ __forceinline__ void operator()(int tile, int m, int n, float y, bool valid) const {
+    const int r = tile * 8 + n;
+    if (!valid || r >= N) return;
+    float v = y * scale[r];
+    if (resid) v += resid[(size_t)m * N + r];
+    out[(size_t)m * N + r] = v;
+  }
+};
+
+// Column n < 4 holds row i of a head, column n + 4 row i + D/2: rotate-half
+// at position pos (nn/rope.go:141-197), then q -> qout, k -> cache (post-RoPE),
+// v -> cache (raw).
+struct QkvEpi {
+  QkvArgs a;
+  QkvTiles tiles;
+  int64_t pos;
+  __device__ __forceinline__ void operator()(int tile, int m, int n, float y, bool valid) const {
+    const int half = a.D / 2;
+    const int head = tiles.head(tile), i = tiles.i0(tile) + (n & 3);
+    const int r = head * a.D + i + (n >> 2) * half;
+    const float v = valid ? y * a.scale[r] : 0.f;
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+    if (!valid || n >= 4) return;
+    const float x0 = v, x1 = partner;
+    if (head < a.H + a.Hkv) {
+      const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
+      const float o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      const float o1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+      float* o = head < a.H ? a.qout + ((size_t)m * a.H + head) * a.D
+                            : a.kcache + (((size_t)m * a.Hkv + (head - a.H)) * a.max_seq + pos) * a.D;
+      o[i] = o0;
+      o[i + half] = o1;
+    } else {
+      float* o = a.vcache + (((size_t)m * a.Hkv + (head - a.H - a.Hkv)) * a.max_seq + pos) * a.D;
+      o[i] = x0;
+      o[i + half] = x1;
+    }
+  }
+};
+
+// Columns 0..3 gate rows j0.., 4..7 the same up rows: act = silu(gate) * up.
+struct GateUpEpi {
+  GateUpArgs a;
+  __device__ __forceinline__ void operator()(int tile, int m, int n, float y, bool valid) const {
+    const int j = tile * 4 + (n & 3);
+    const bool in = valid && j < a.F;
+    const float v = in ? y * ((n >> 2) ? a.up_scale[j] : a.gate_scale[j]) : 0.f;
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+    if (!in || n >= 4) return;
+    const float sig = 1.0f / (1.0f + expf(-v));
+    a.act[(size_t)m * a.F + j] = (v * sig) * partner;
+  }
+};
+
+template <int MT, int KPW>
+__global__ void __launch_bounds__(512) gemv_mma_plain_kernel(float* out, const float* __restrict__ x,
+                                                              const int8_t* __restrict__ q,
+                                                              const float* __restrict__ scale, const float* resid,
+                                                              int M, int N, int K, const float* __restrict__ norm_w,
+                                                              float eps) {
+  const PlainTiles tiles{q, N, K};
+  const PlainEpi epi{out, scale, resid, N};
+  gemv_mma_body<MT, KPW>(tiles, epi, x, M, K, norm_w, eps);
+}
+
+template <int MT, int KPW>
+__global__ void __launch_bounds__(512) gemv_mma_qkv_kernel(QkvArgs a) {
+  const QkvTiles tiles{a.q, a.H + 2 * a.Hkv, a.D, a.d};
+  // The position was written by an earlier step's tail kernel, complete before
+  // the preceding kernel could launch this one (programmatic launch chain).
+  const QkvEpi epi{a, tiles, *a.pos};
+  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps);
+}
+
+template <int MT, int KPW>
+__global__ void __launch_bounds__(512) gemv_mma_gateup_kernel(GateUpArgs a) {
+  const GateUpTiles tiles{a.gate, a.up, a.F, a.d};
+  const GateUpEpi epi{a};
+  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+struct MmaShape {
+  int kpw, warps;
+};
+
+// At most 16 warps (the 512-thread launch bound keeps 128 registers per
+// thread); KPW loads per lane per round; more k-blocks than 16 * 16 run in
+// several rounds per tile.  Enough warps for the epilogue (MT * 8 threads).
+MmaShape mma_shape(int K, int MT) {
+  const int KB = K / 64;
+  MmaShape s;
+  s.kpw = KB <= 128 ? 8 : (KB <= 192 ? 12 : 16);
+  s.warps = (KB + s.kpw - 1) / s.kpw;
+  if (s.warps > 16) s.warps = 16;
+  const int min_w = (MT * 8 + 31) / 32;
+  if (s.warps < min_w) s.warps = min_w;
+  return s;
+}
+
+template <typename Kern, typename... Args>
+tb_status_t launch_mma(Kern kern, int64_t tiles, int warps, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv_mma)");
+  }
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, warps * 32, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (occ < 1) return TB_ERROR_NOT_SUPPORTED;
+  if (occ > 4) occ = 4;
+  int64_t grid = (int64_t)sm_count() * occ;
+  if (grid > tiles) grid = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemv_mma)");
+  return TB_SUCCESS;
+}
+
+int mt_of(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+
+#define TB_MMA_DISPATCH(KERN, MT_, KPW_, ...)                                               \
+  do {                                                                                      \
+    if (KPW_ == 12) {                                                                       \
+      switch (MT_) {                                                                        \
+        case 1: return launch_mma(KERN<1, 12>, __VA_ARGS__);                                \
+        case 2: return launch_mma(KERN<2, 12>, __VA_ARGS__);                                \
+        case 4: return launch_mma(KERN<4, 12>, __VA_ARGS__);                                \
+        default: return launch_mma(KERN<8, 12>, __VA_ARGS__);                               \
+      }                                                                                     \
+    } else if (KPW_ == 8) {                                                                 \
+      switch (MT_) {                                                                        \
+        case 1: return launch_mma(KERN<1, 8>, __VA_ARGS__);                                 \
+        case 2: return launch_mma(KERN<2, 8>, __VA_ARGS__);                                 \
+        case 4: return launch_mma(KERN<4, 8>, __VA_ARGS__);                                 \
+        default: return launch_mma(KERN<8, 8>, __VA_ARGS__);                                \
+      }                                                                                     \
+    } else {                                                                                \
+      switch (MT_) {                                                                        \
+        case 1: return launch_mma(KERN<1, 16>, __VA_ARGS__);                                \
+        case 2: return launch_mma(KERN<2, 16>, __VA_ARGS__);                                \
+        case 4: return launch_mma(KERN<4, 16>, __VA_ARGS__);                                \
+        default: return launch_mma(KERN<8, 16>, __VA_ARGS__);                               \
+      }                                                                                     \
+    }                                                                                       \
+  } while (0)
+
+}  // namespace
+
+bool gemv_mma_ok(const float* x, const int8_t* q, int64_t M, int64_t K) {
+  if (M < 1 || M > 8 || K % 64 != 0 || K > 65536) return false;
+  if (!aligned(x, 16) || !aligned(q, 16)) return false;
+  const MmaShape s = mma_shape((int)K, mt_of((int)M));
+  return MmaSmem::bytes(mt_of((int)M), (int)K, s.warps) <= 200 * 1024;
+}
+
+tb_status_t gemv_mma_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                           int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(M);
+  const MmaShape s = mma_shape(K, MT);
+  const size_t smem = MmaSmem::bytes(MT, K, s.warps);
+  const int64_t tiles = (N + 7) / 8;
+  TB_MMA_DISPATCH(gemv_mma_plain_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, out, x, q, scale, resid, M, N, K,
+                  norm_w, eps);
+}
+
+tb_status_t gemv_mma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(a.M);
+  const MmaShape s = mma_shape(a.d, MT);
+  const size_t smem = MmaSmem::bytes(MT, a.d, s.warps);
+  const int64_t tiles = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 8);
+  TB_MMA_DISPATCH(gemv_mma_qkv_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a);
+}
+
+tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(a.M);
+  const MmaShape s = mma_shape(a.d, MT);
+  const size_t smem = MmaSmem::bytes(MT, a.d, s.warps);
+  const int64_t tiles = (a.F + 3) / 4;
+  TB_MMA_DISPATCH(gemv_mma_gateup_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a);
+}
+
+}  // namespace tb

@@ -67,6 +67,16 @@ tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl);
 tb_status_t gemv_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
 tb_status_t gemv_lmhead(const LmHeadArgs& a, cudaStream_t st, bool pdl);
 
+// gemv_mma.cu: the same GEMVs on the tensor cores (M <= 8, K % 64 == 0)
+bool gemv_mma_ok(const float* x, const int8_t* q, int64_t M, int64_t K);
+tb_status_t gemv_mma_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                           int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl);
+tb_status_t gemv_mma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl);
+tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
+// Kernel family for the decode GEMVs: true = tensor cores (default), false =
+// CUDA-core FMA kernels (TENDO_B200_GEMV=simt).
+bool gemv_use_mma();
+
 // attention.cu
 int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq);
 size_t attn_decode_workspace(int B, int H, int D, int nsplit);
