@@ -287,21 +287,8 @@ def run_ours(args):
     # cycling over all layers so weights stream from HBM
     qm.set_position(PROMPT + NEW // 2)  # mean cache length of a step
     kern = {}
-    reps = 3
     for kind in range(6):
-        layers = list(range(CFG["layers"])) if kind < 5 else [0] * 8
-        for layer in layers[:4]:
-            qm.bench_kernel(kind, layer)
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            for layer in layers:
-                qm.bench_kernel(kind, layer)
-        b.record(stream)
-        qm.sync()
-        n = reps * len(layers)
-        us = a.elapsed_time(b) * 1000.0 / n
+        us = qm.time_kernel(kind, reps=3)
         byts = kernel_bytes(kind, PROMPT + NEW // 2)
         per_step = CFG["layers"] if kind < 5 else 1
         kern[KIND_NAMES[kind]] = {"us": us, "bytes": byts, "GB_s": byts / (us * 1e-6) / 1e9,

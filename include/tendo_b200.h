@@ -275,6 +275,10 @@ TB_API tb_stream_t tb_model_stream(tb_model* m);
  * residual, 5 = final RMSNorm + lm_head GEMV + argmax.  Reads and writes
  * the engine's own buffers at the current position. */
 TB_API tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer);
+/* Times one kernel kind of the decode step: `reps` rounds over all layers'
+ * weights launched from one CUDA graph (no host launch cost in the time),
+ * timed with CUDA events on the engine stream; *us_per_launch = average. */
+TB_API tb_status_t tb_model_time_kernel(tb_model* m, int kind, int reps, float* us_per_launch);
 /* Kernel launches one decode step issues. */
 TB_API int64_t tb_model_launches_per_step(const tb_model* m);
 

@@ -72,6 +72,7 @@ SIGNATURES = [
     ("tb_model_get_linear", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     ("tb_model_get_tensor", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("tb_model_bench_kernel", _st, [_vp, ctypes.c_int, ctypes.c_int]),
+    ("tb_model_time_kernel", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("tb_model_reset", _st, [_vp]),
     ("tb_model_position", _i64, [_vp]),
     ("tb_model_forward", _st, [_vp, _vp, _i64, _i64, _vp, _vp]),
@@ -447,6 +448,12 @@ class QuantizedModel:
 
     def bench_kernel(self, kind: int, layer: int):
         check(lib.tb_model_bench_kernel(self.h, kind, layer))
+
+    def time_kernel(self, kind: int, reps: int = 3) -> float:
+        """Average microseconds per launch of one decode-step kernel kind (graph-timed)."""
+        us = ctypes.c_float()
+        check(lib.tb_model_time_kernel(self.h, kind, reps, ctypes.byref(us)))
+        return float(us.value)
 
     def reset(self):
         check(lib.tb_model_reset(self.h))

@@ -73,14 +73,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArg
   const int64_t end = min(start + chunk, sk);
   const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
   const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  {
-    const int64_t pend = min(end, sk - 1);
-    const int lines = D * 4 / 128;
-    for (int64_t t = threadIdx.x; t < (pend - start) * lines; t += kAttnThreads) {
-      const int64_t j = start + t / lines;
-      const int off = (int)(t % lines) * 32;
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(kb + j * D + off));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + j * D + off));
+  if (threadIdx.x == 0) {
+    const int64_t pend = min(end, sk - 1);  // row sk - 1 comes from the preceding kernel
+    if (pend > start) {
+      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
+      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
     }
   }
   pdl_wait();

@@ -87,6 +87,12 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& a, float& b, floa
   d = __uint_as_float(__byte_perm(u, hi, 0x7653)) - 8388736.0f;
 }
 
+// Bulk L2 prefetch through the TMA unit: `bytes` (a multiple of 16) from a
+// 16-byte aligned global address, no registers held while it is in flight.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding grid's memory and
 // let the next grid start launching.  Both are no-ops when the kernel was not
 // launched with the programmatic-serialization attribute.

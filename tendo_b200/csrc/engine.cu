@@ -198,6 +198,7 @@ tb_status_t finish_logits(tb_model* m, int64_t S) {
     a.M = (int)m->B;
     a.d = (int)m->d;
     a.V = (int)m->V;
+    a.l2_prefetch = tb::l2_prefetch_enabled();
     TB_TRY(tb::gemv_lmhead(a, st, false));
     // the tail kernel advances the position by one; pre-compensate
     int64_t p = m->host_pos - 1;
@@ -312,6 +313,7 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
   la.M = (int)m->B;
   la.d = (int)m->d;
   la.V = (int)m->V;
+  la.l2_prefetch = tb::l2_prefetch_enabled();
   if (kind == 5) return tb::gemv_lmhead(la, st, pdl);
   return TB_ERROR_INVALID_ARGUMENT;
 }
@@ -551,6 +553,47 @@ extern "C" tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer) {
   TB_REQUIRE(m->fused && m->host_pos < m->Ms);
   DeviceGuard guard(m->device);
   return decode_kernel(m, kind, layer, false);
+}
+
+extern "C" tb_status_t tb_model_time_kernel(tb_model* m, int kind, int reps, float* us_per_launch) {
+  TB_REQUIRE(m && us_per_launch && kind >= 0 && kind <= 5 && reps >= 1);
+  TB_REQUIRE(m->fused && m->host_pos < m->Ms);
+  DeviceGuard guard(m->device);
+  // reps rounds over every layer's weights (so they stream from HBM), in one
+  // CUDA graph, so the host launch cost is not part of the time
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  TB_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  tb_status_t s = TB_SUCCESS;
+  int64_t launches = 0;
+  for (int r = 0; r < reps && s == TB_SUCCESS; r++)
+    for (int64_t l = 0; l < m->L && s == TB_SUCCESS; l++, launches++) s = decode_kernel(m, kind, kind == 5 ? 0 : l, false);
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (s != TB_SUCCESS) {
+    if (g) cudaGraphDestroy(g);
+    return s;
+  }
+  if (e != cudaSuccess) return tb::cuda_fail(e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return tb::cuda_fail(e, "cudaGraphInstantiate");
+  cudaEvent_t a = nullptr, b = nullptr;
+  float ms = 0.f;
+  e = cudaEventCreate(&a);
+  if (e == cudaSuccess) e = cudaEventCreate(&b);
+  if (e == cudaSuccess) e = cudaGraphLaunch(ge, m->stream);  // warm
+  if (e == cudaSuccess) e = cudaEventRecord(a, m->stream);
+  if (e == cudaSuccess) e = cudaGraphLaunch(ge, m->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(b, m->stream);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  cudaGraphExecDestroy(ge);
+  if (e != cudaSuccess) return tb::cuda_fail(e, "tb_model_time_kernel");
+  *us_per_launch = ms * 1000.0f / (float)launches;
+  return TB_SUCCESS;
 }
 
 extern "C" tb_status_t tb_model_reset(tb_model* m) {

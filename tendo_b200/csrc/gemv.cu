@@ -199,13 +199,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_lmhead_kernel(LmHeadArgs a)
   const int ngroups = (N + ROWS - 1) / ROWS;
   const int lane = threadIdx.x & 31;
   int g = first_group();
-  if (g < ngroups) {
-#pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-      const float* row = a.w + (size_t)min(g * ROWS + r, N - 1) * K;
-      for (int off = lane * 32; off < K; off += 32 * 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
+  // TMA bulk prefetch of this warp's next kAhead row pairs into L2.
+  constexpr int kAhead = 4;
+  auto prefetch_task = [&](int task) {
+    if (task < ngroups) {
+      const int r0 = task * ROWS, rows = min(ROWS, N - r0);
+      if (rows > 0 && (K * 4) % 16 == 0) prefetch_l2_bulk(a.w + (size_t)r0 * K, (uint32_t)(rows * K * 4));
     }
-  }
+  };
+  const bool l2pf = a.l2_prefetch;
+  if (l2pf && lane == 0)
+    for (int i = 0; i < kAhead; i++) prefetch_task(g + i * group_stride());
   pdl_wait();
   pdl_launch_dependents();
   // RMSNorm prologue in the plain layout.
@@ -257,6 +261,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_lmhead_kernel(LmHeadArgs a)
   const float4* xv = reinterpret_cast<const float4*>(xs);
   const int nv = K / 4;
   for (; g < ngroups; g += group_stride()) {
+    if (l2pf && lane == 0) prefetch_task(g + kAhead * group_stride());
     const float4* rp[ROWS];
 #pragma unroll
     for (int r = 0; r < ROWS; r++) rp[r] = reinterpret_cast<const float4*>(a.w + (size_t)min(g * ROWS + r, N - 1) * K);

@@ -29,6 +29,7 @@
 // dependent launch they stream while the previous kernel finishes.
 #include <cuda_fp16.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -162,6 +163,10 @@ struct PlainTiles {
   int N, K;
   __device__ int tiles() const { return (N + 7) / 8; }
   __device__ const int8_t* row(int tile, int n) const { return q + (size_t)min(tile * 8 + n, N - 1) * K; }
+  __device__ void prefetch(int tile) const {
+    const int r0 = tile * 8, rows = min(8, N - r0);
+    if (rows > 0) prefetch_l2_bulk(q + (size_t)r0 * K, (uint32_t)(rows * K));
+  }
 };
 struct QkvTiles {  // 4 rotate-half pairs: columns n and n + 4 are rows i and i + D/2 of one head
   const int8_t* q;
@@ -173,6 +178,11 @@ struct QkvTiles {  // 4 rotate-half pairs: columns n and n + 4 are rows i and i 
     const int r = head(tile) * D + i0(tile) + (n & 3) + (n >> 2) * (D / 2);
     return q + (size_t)r * K;
   }
+  __device__ void prefetch(int tile) const {
+    const int r = head(tile) * D + i0(tile);
+    prefetch_l2_bulk(q + (size_t)r * K, (uint32_t)(4 * K));
+    prefetch_l2_bulk(q + (size_t)(r + D / 2) * K, (uint32_t)(4 * K));
+  }
 };
 struct GateUpTiles {  // columns 0..3: gate rows j0..j0+3; 4..7: the same up rows
   const int8_t* gate;
@@ -182,6 +192,13 @@ struct GateUpTiles {  // columns 0..3: gate rows j0..j0+3; 4..7: the same up row
   __device__ const int8_t* row(int tile, int n) const {
     const int j = min(tile * 4 + (n & 3), F - 1);
     return ((n >> 2) ? up : gate) + (size_t)j * K;
+  }
+  __device__ void prefetch(int tile) const {
+    const int j0 = tile * 4, rows = min(4, F - j0);
+    if (rows > 0) {
+      prefetch_l2_bulk(gate + (size_t)j0 * K, (uint32_t)(rows * K));
+      prefetch_l2_bulk(up + (size_t)j0 * K, (uint32_t)(rows * K));
+    }
   }
 };
 
@@ -252,7 +269,8 @@ __device__ __forceinline__ float reduce_partial(const float* red, int W, int m, 
 // ---------------------------------------------------------------------------
 template <int MT, int KPW, typename Tiles, typename Epi>
 __device__ __forceinline__ void gemv_mma_body(const Tiles& tiles, const Epi& epi, const float* __restrict__ x,
-                                              int M, int K, const float* __restrict__ norm_w, float eps) {
+                                              int M, int K, const float* __restrict__ norm_w, float eps,
+                                              bool l2_prefetch) {
   extern __shared__ __align__(16) unsigned char smem[];
   __half* hi = reinterpret_cast<__half*>(smem);
   __half* lo = hi + MmaSmem::x_halves(MT, K);
@@ -265,6 +283,12 @@ __device__ __forceinline__ void gemv_mma_body(const Tiles& tiles, const Epi& epi
   const int ntiles = tiles.tiles();
   const int nrounds = ((KB + W - 1) / W + KPW - 1) / KPW;
   int tile = blockIdx.x;
+  // The TMA unit streams this CTA's next kPrefetch tiles into L2 ahead of the
+  // register loads (weights never depend on the preceding kernel).
+  constexpr int kPrefetch = 4;
+  if (l2_prefetch && threadIdx.x == 0)
+    for (int i = 0; i < kPrefetch; i++)
+      if (tile + i * (int)gridDim.x < ntiles) tiles.prefetch(tile + i * gridDim.x);
   int4 w[KPW];
   if (tile < ntiles) load_tile<KPW>(w, tiles.row(tile, g), KB, W, warp, t, 0);
   pdl_wait();
@@ -274,6 +298,8 @@ __device__ __forceinline__ void gemv_mma_body(const Tiles& tiles, const Epi& epi
   int buf = 0;
   for (; tile < ntiles; tile += gridDim.x) {
     float d[4] = {0.f, 0.f, 0.f, 0.f};
+    if (l2_prefetch && threadIdx.x == 0 && tile + kPrefetch * (int)gridDim.x < ntiles)
+      tiles.prefetch(tile + kPrefetch * gridDim.x);
     const int8_t* rowp = tiles.row(tile, g);
     for (int r = 0; r < nrounds; r++) {
       if (r > 0) load_tile<KPW>(w, rowp, KB, W, warp, t, r * KPW);
@@ -358,26 +384,26 @@ __global__ void __launch_bounds__(512) gemv_mma_plain_kernel(float* out, const f
                                                               const int8_t* __restrict__ q,
                                                               const float* __restrict__ scale, const float* resid,
                                                               int M, int N, int K, const float* __restrict__ norm_w,
-                                                              float eps) {
+                                                              float eps, bool l2_prefetch) {
   const PlainTiles tiles{q, N, K};
   const PlainEpi epi{out, scale, resid, N};
-  gemv_mma_body<MT, KPW>(tiles, epi, x, M, K, norm_w, eps);
+  gemv_mma_body<MT, KPW>(tiles, epi, x, M, K, norm_w, eps, l2_prefetch);
 }
 
 template <int MT, int KPW>
-__global__ void __launch_bounds__(512) gemv_mma_qkv_kernel(QkvArgs a) {
+__global__ void __launch_bounds__(512) gemv_mma_qkv_kernel(QkvArgs a, bool l2_prefetch) {
   const QkvTiles tiles{a.q, a.H + 2 * a.Hkv, a.D, a.d};
   // The position was written by an earlier step's tail kernel, complete before
   // the preceding kernel could launch this one (programmatic launch chain).
   const QkvEpi epi{a, tiles, *a.pos};
-  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps);
+  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, l2_prefetch);
 }
 
 template <int MT, int KPW>
-__global__ void __launch_bounds__(512) gemv_mma_gateup_kernel(GateUpArgs a) {
+__global__ void __launch_bounds__(512) gemv_mma_gateup_kernel(GateUpArgs a, bool l2_prefetch) {
   const GateUpTiles tiles{a.gate, a.up, a.F, a.d};
   const GateUpEpi epi{a};
-  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps);
+  gemv_mma_body<MT, KPW>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, l2_prefetch);
 }
 
 // ---------------------------------------------------------------------------
@@ -404,12 +430,32 @@ MmaShape mma_shape(int K, int MT) {
 template <typename Kern, typename... Args>
 tb_status_t launch_mma(Kern kern, int64_t tiles, int warps, size_t smem, cudaStream_t st, bool pdl, Args... args) {
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv_mma)");
+    cudaError_t e0 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e0 != cudaSuccess) return cuda_fail(e0, "cudaFuncSetAttribute(gemv_mma)");
   }
   int occ = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, warps * 32, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  cudaError_t e = cudaSuccess;
+  {
+    // occupancy per (kernel, block, smem), cached: the query costs microseconds of host time
+    static thread_local const void* ck[16];
+    static thread_local int cw[16], co[16];
+    static thread_local size_t cs[16];
+    static thread_local int cn = 0;
+    int hit = -1;
+    for (int i = 0; i < cn; i++)
+      if (ck[i] == (const void*)kern && cw[i] == warps && cs[i] == smem) hit = i;
+    if (hit >= 0) {
+      occ = co[hit];
+    } else {
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, warps * 32, smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      const int slot = cn < 16 ? cn++ : 15;
+      ck[slot] = (const void*)kern;
+      cw[slot] = warps;
+      cs[slot] = smem;
+      co[slot] = occ;
+    }
+  }
   if (occ < 1) return TB_ERROR_NOT_SUPPORTED;
   if (occ > 4) occ = 4;
   int64_t grid = (int64_t)sm_count() * occ;
@@ -430,6 +476,7 @@ tb_status_t launch_mma(Kern kern, int64_t tiles, int warps, size_t smem, cudaStr
 }
 
 int mt_of(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+
 
 #define TB_MMA_DISPATCH(KERN, MT_, KPW_, ...)                                               \
   do {                                                                                      \
@@ -459,6 +506,16 @@ int mt_of(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
 
 }  // namespace
 
+// TMA bulk L2 prefetch of upcoming tiles (TENDO_B200_L2PF=1); off by default:
+// measured slower than plain streaming loads on the decode shapes.
+bool l2_prefetch_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TENDO_B200_L2PF");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 bool gemv_mma_ok(const float* x, const int8_t* q, int64_t M, int64_t K) {
   if (M < 1 || M > 8 || K % 64 != 0 || K > 65536) return false;
   if (!aligned(x, 16) || !aligned(q, 16)) return false;
@@ -473,7 +530,7 @@ tb_status_t gemv_mma_plain(float* out, const float* x, const int8_t* q, const fl
   const size_t smem = MmaSmem::bytes(MT, K, s.warps);
   const int64_t tiles = (N + 7) / 8;
   TB_MMA_DISPATCH(gemv_mma_plain_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, out, x, q, scale, resid, M, N, K,
-                  norm_w, eps);
+                  norm_w, eps, l2_prefetch_enabled());
 }
 
 tb_status_t gemv_mma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl) {
@@ -481,7 +538,7 @@ tb_status_t gemv_mma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl) {
   const MmaShape s = mma_shape(a.d, MT);
   const size_t smem = MmaSmem::bytes(MT, a.d, s.warps);
   const int64_t tiles = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 8);
-  TB_MMA_DISPATCH(gemv_mma_qkv_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a);
+  TB_MMA_DISPATCH(gemv_mma_qkv_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a, l2_prefetch_enabled());
 }
 
 tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
@@ -489,7 +546,7 @@ tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   const MmaShape s = mma_shape(a.d, MT);
   const size_t smem = MmaSmem::bytes(MT, a.d, s.warps);
   const int64_t tiles = (a.F + 3) / 4;
-  TB_MMA_DISPATCH(gemv_mma_gateup_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a);
+  TB_MMA_DISPATCH(gemv_mma_gateup_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a, l2_prefetch_enabled());
 }
 
 }  // namespace tb

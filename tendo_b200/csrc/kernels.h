@@ -43,6 +43,7 @@ struct LmHeadArgs {
   float* logits;   // [M, V] (may be null)
   unsigned long long* argmax_keys;  // [M] (may be null)
   int M, d, V;
+  bool l2_prefetch;
 };
 
 struct AttnDecodeArgs {
@@ -76,6 +77,7 @@ tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
 // Kernel family for the decode GEMVs: true = tensor cores (default), false =
 // CUDA-core FMA kernels (TENDO_B200_GEMV=simt).
 bool gemv_use_mma();
+bool l2_prefetch_enabled();
 
 // attention.cu
 int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq);

@@ -41,16 +41,25 @@ def run(Ms, Ns, K, iters, mode):
             sh = tb._stream(st)
 
             def launch(i):
+                nonlocal sh
                 tb.check(tb.lib.tb_dequant_matmul_i8f32_mode(out.data_ptr(), x.data_ptr(), qs[i % copies].data_ptr(),
                                                              qt.scale.data_ptr(), M, N, K, 0, mode, sh))
 
             for i in range(3):
                 launch(i)
+            torch.cuda.synchronize()
+            # the timed launches run from one CUDA graph, so host launch cost is excluded
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                sh = tb._stream(torch.cuda.current_stream())
+                for i in range(iters):
+                    launch(i)
+            graph.replay()
+            torch.cuda.synchronize()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(st)
-            for i in range(iters):
-                launch(i)
+            graph.replay()
             b.record(st)
             torch.cuda.synchronize()
             us = a.elapsed_time(b) * 1000.0 / iters
