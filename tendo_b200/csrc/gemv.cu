@@ -415,21 +415,21 @@ bool gemv_fast_ok(const float* x, const int8_t* q, int64_t K) {
   return K % 16 == 0 && aligned(x, 16) && aligned(q, 16) && gemv_smem_bytes(1, (int)K) <= 200 * 1024;
 }
 
-bool gemv_use_mma() {
-  static const bool use = [] {
-    const char* e = getenv("TENDO_B200_GEMV");
-    return !(e && strcmp(e, "simt") == 0);
-  }();
-  return use;
-}
-
 tb_status_t gemv_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
                        int M, int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl) {
-  if (gemv_use_mma() && gemv_mma_ok(x, q, M < 8 ? M : 8, K)) {
+  const GemvKind kind = gemv_kind();
+  const bool tma = kind == GemvKind::kTma && gemv_tma_ok(x, q, M < 8 ? M : 8, K);
+  const bool mma = kind == GemvKind::kMma && gemv_mma_ok(x, q, M < 8 ? M : 8, K);
+  if (tma || mma) {
     for (int m0 = 0; m0 < M; m0 += 8) {
       const int mm = M - m0 < 8 ? M - m0 : 8;
-      TB_TRY(gemv_mma_plain(out + (size_t)m0 * N, x + (size_t)m0 * K, q, scale,
-                            resid ? resid + (size_t)m0 * N : nullptr, mm, N, K, norm_w, eps, st, pdl));
+      float* o = out + (size_t)m0 * N;
+      const float* xx = x + (size_t)m0 * K;
+      const float* rr = resid ? resid + (size_t)m0 * N : nullptr;
+      if (tma)
+        TB_TRY(gemv_tma_plain(o, xx, q, scale, rr, mm, N, K, norm_w, eps, st, pdl));
+      else
+        TB_TRY(gemv_mma_plain(o, xx, q, scale, rr, mm, N, K, norm_w, eps, st, pdl));
     }
     return TB_SUCCESS;
   }
@@ -476,6 +476,7 @@ tb_status_t gemv_generic(float* out, const float* x, const int8_t* q, const floa
 
 tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0 && a.D % 2 == 0);
+  if (gemv_kind() == GemvKind::kTma && a.D % 8 == 0 && gemv_tma_ok(a.h, a.q, a.M, a.d)) return gemv_tma_qkv(a, st, pdl);
   if (gemv_use_mma() && a.D % 8 == 0 && gemv_mma_ok(a.h, a.q, a.M, a.d)) return gemv_mma_qkv(a, st, pdl);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);
@@ -491,6 +492,8 @@ tb_status_t gemv_qkv_rope(const QkvArgs& a, cudaStream_t st, bool pdl) {
 
 tb_status_t gemv_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   TB_REQUIRE(a.M >= 1 && a.M <= 8 && a.d % 16 == 0);
+  if (gemv_kind() == GemvKind::kTma && gemv_tma_ok(a.h, a.gate, a.M, a.d) && tb::aligned(a.up, 16))
+    return gemv_tma_gateup(a, st, pdl);
   if (gemv_use_mma() && gemv_mma_ok(a.h, a.gate, a.M, a.d) && tb::aligned(a.up, 16)) return gemv_mma_gateup(a, st, pdl);
   const int MT = mt_for(a.M);
   const size_t smem = gemv_smem_bytes(MT, a.d);

@@ -409,6 +409,294 @@ __global__ void __launch_bounds__(512) gemv_mma_gateup_kernel(GateUpArgs a, bool
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// TMA-fed variant: the weight stream goes global -> shared memory through the
+// TMA unit (cp.async.bulk, mbarrier completion) instead of register loads, so
+// the bytes in flight per SM are set by the stage count, not by the L1 miss
+// machinery.  One producer warp (one elected thread) runs up to `stages`
+// chunks ahead, starting before griddepcontrol.wait; W consumer warps convert
+// and multiply from shared memory.  A chunk is 8 rows x Kc bytes (Kc divides
+// K, at most 4096); each row lands at stride RS = Kc (+64 when Kc is a
+// multiple of 128) so the lanes of a 16-byte shared load hit distinct banks.
+// Every wait is bounded: on expiry the kernel counts the event in
+// g_wait_timeouts and carries on, so the host sees an error instead of a hang.
+// ---------------------------------------------------------------------------
+__device__ int g_wait_timeouts;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Waits for the phase of parity `parity`; gives up after a bounded number of
+// polls (seconds at most) and records the timeout.
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t it = 0; it < (1u << 24); it++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return;
+  }
+  atomicAdd(&g_wait_timeouts, 1);
+}
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// stage_x_f16 for the first `nthreads` threads, synchronised with a named barrier.
+template <int MT>
+__device__ void stage_x_f16_n(__half* hi, __half* lo, float* xscale, const float* __restrict__ x, int M, int K,
+                              const float* __restrict__ norm_w, float eps, float* red, int nthreads) {
+  const int warps = nthreads >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = K >> 2;
+  float ss[MT], mx[MT];
+#pragma unroll
+  for (int m = 0; m < MT; m++) ss[m] = mx[m] = 0.f;
+  for (int v = threadIdx.x; v < nv; v += nthreads) {
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      if (m < M) {
+        const float4 t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
+        ss[m] += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        float a = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
+        if (norm_w) {
+          const float4 w = reinterpret_cast<const float4*>(norm_w)[v];
+          a = fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w)));
+        }
+        mx[m] = fmaxf(mx[m], a);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    const float s = warp_sum(ss[m]), a = warp_max(mx[m]);
+    if (lane == 0) {
+      red[(2 * m) * 32 + warp] = s;
+      red[(2 * m + 1) * 32 + warp] = a;
+    }
+  }
+  consumer_sync(nthreads);
+  float rms[MT], inv_sc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    float s = 0.f, a = 0.f;
+    for (int w = 0; w < warps; w++) {
+      s += red[(2 * m) * 32 + w];
+      a = fmaxf(a, red[(2 * m + 1) * 32 + w]);
+    }
+    rms[m] = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)) : 1.0f;
+    if (norm_w) a = a / rms[m] * 1.0001f;
+    int e = 0;
+    if (a > 0.f && isfinite(a)) {
+      frexpf(a, &e);
+      e -= 14;
+    }
+    inv_sc[m] = ldexpf(1.0f, -e);
+    if (threadIdx.x == 0) xscale[m] = ldexpf(1.0f, e);
+  }
+  for (int v = threadIdx.x; v < nv; v += nthreads) {
+    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w) w4 = reinterpret_cast<const float4*>(norm_w)[v];
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < M) {
+        t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
+        if (norm_w) {
+          t.x = __fmul_rn(__fdiv_rn(t.x, rms[m]), w4.x);
+          t.y = __fmul_rn(__fdiv_rn(t.y, rms[m]), w4.y);
+          t.z = __fmul_rn(__fdiv_rn(t.z, rms[m]), w4.z);
+          t.w = __fmul_rn(__fdiv_rn(t.w, rms[m]), w4.w);
+        }
+        t.x *= inv_sc[m];
+        t.y *= inv_sc[m];
+        t.z *= inv_sc[m];
+        t.w *= inv_sc[m];
+      }
+      const float vals[4] = {t.x, t.y, t.z, t.w};
+      __half h[4], l[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        h[i] = __float2half_rn(vals[i]);
+        l[i] = __float2half_rn(vals[i] - __half2float(h[i]));
+      }
+      __half* hp = hi + (size_t)m * (K + kPad) + 4 * v;
+      __half* lp = lo + (size_t)m * (K + kPad) + 4 * v;
+      *reinterpret_cast<__half2*>(hp) = __halves2half2(h[0], h[1]);
+      *reinterpret_cast<__half2*>(hp + 2) = __halves2half2(h[2], h[3]);
+      *reinterpret_cast<__half2*>(lp) = __halves2half2(l[0], l[1]);
+      *reinterpret_cast<__half2*>(lp + 2) = __halves2half2(l[2], l[3]);
+    }
+  }
+  consumer_sync(nthreads);
+}
+
+struct TmaLayout {
+  int Kc, RS, stages, W;
+  size_t stage_bytes, x_off, xs_off, red_off, scr_off, bar_off, total;
+  __host__ __device__ void init(int MT, int K, int Kc_, int stages_, int W_) {
+    Kc = Kc_;
+    RS = (Kc % 128 == 0) ? Kc + 64 : Kc;
+    stages = stages_;
+    W = W_;
+    stage_bytes = (size_t)8 * RS;
+    x_off = (size_t)stages * stage_bytes;
+    xs_off = x_off + (size_t)2 * MT * (K + kPad) * 2;
+    red_off = xs_off + 16 * sizeof(float);
+    scr_off = red_off + (size_t)2 * W * 64 * sizeof(float);
+    bar_off = (scr_off + 512 * sizeof(float) + 15) & ~(size_t)15;
+    total = bar_off + (size_t)2 * stages * sizeof(uint64_t);
+  }
+};
+
+template <int MT, typename Tiles, typename Epi>
+__device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi, const float* __restrict__ x, int M,
+                                              int K, const float* __restrict__ norm_w, float eps, int Kc,
+                                              int stages) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps; warp W produces
+  TmaLayout L;
+  L.init(MT, K, Kc, stages, W);
+  unsigned char* stage_base = smem;
+  __half* hi = reinterpret_cast<__half*>(smem + L.x_off);
+  __half* lo = hi + (size_t)MT * (K + kPad);
+  float* xscale = reinterpret_cast<float*>(smem + L.xs_off);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  float* scratch = reinterpret_cast<float*>(smem + L.scr_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty = full + stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = K / Kc, kbc = Kc / 64;
+  const int ntiles = tiles.tiles();
+  const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int units = my_tiles * nch;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)(W * 32));
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == W) {
+    // producer: weights never depend on the preceding kernel, so no wait here
+    if (lane == 0) {
+      for (int u = 0; u < units; u++) {
+        const int s = u % stages, use = u / stages;
+        if (use > 0) mbar_wait(&empty[s], (uint32_t)((use - 1) & 1));
+        const int tile = (int)blockIdx.x + (u / nch) * (int)gridDim.x, ch = u % nch;
+        unsigned char* dst = stage_base + (size_t)s * L.stage_bytes;
+        mbar_expect_tx(&full[s], (uint32_t)(8 * Kc));
+#pragma unroll
+        for (int n = 0; n < 8; n++) tma_load_1d(dst + (size_t)n * L.RS, tiles.row(tile, n) + (size_t)ch * Kc, (uint32_t)Kc, &full[s]);
+      }
+      // the copies of the last stages land before the consumers finish with
+      // them, so the CTA never exits with a copy in flight
+    }
+    pdl_launch_dependents();
+    return;
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const int nthreads = W * 32;
+  stage_x_f16_n<MT>(hi, lo, xscale, x, M, K, norm_w, eps, scratch, nthreads);
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int kEpiThreads = ((MT * 8 + 31) / 32) * 32;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  int buf = 0;
+  for (int u = 0; u < units; u++) {
+    const int s = u % stages, use = u / stages, ch = u % nch;
+    if (ch == 0) d[0] = d[1] = d[2] = d[3] = 0.f;
+    mbar_wait(&full[s], (uint32_t)(use & 1));
+    const unsigned char* st = stage_base + (size_t)s * L.stage_bytes + (size_t)g * L.RS + 16 * t;
+#pragma unroll 2
+    for (int kb = warp; kb < kbc; kb += W) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(st + kb * 64);
+      const int k = ch * Kc + kb * 64 + 16 * t;
+      uint32_t xh[8], xl[8];
+      if (g < MT) {
+        const uint4* ph = reinterpret_cast<const uint4*>(hi + (size_t)g * (K + kPad) + k);
+        const uint4* pl = reinterpret_cast<const uint4*>(lo + (size_t)g * (K + kPad) + k);
+        const uint4 h0 = ph[0], h1 = ph[1], l0 = pl[0], l1 = pl[1];
+        xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
+        xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
+        xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
+        xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
+      } else {
+#pragma unroll
+        for (int p = 0; p < 8; p++) xh[p] = xl[p] = 0u;
+      }
+      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t ux = words[j] ^ 0x80808080u;
+        const uint32_t b0 = i8pair_to_f16x2(ux, 0x4140);
+        const uint32_t b1 = i8pair_to_f16x2(ux, 0x4342);
+        const uint32_t a[4] = {xh[2 * j], xl[2 * j], xh[2 * j + 1], xl[2 * j + 1]};
+        mma_16816(d, a, b0, b1);
+      }
+    }
+    mbar_arrive(&empty[s]);
+    if (ch == nch - 1) {
+      const int tile = (int)blockIdx.x + (u / nch) * (int)gridDim.x;
+      float* rb = red + (size_t)buf * W * 64;
+      store_partial<MT>(rb, d, warp, g, t);
+      consumer_sync(nthreads);
+      if (threadIdx.x < kEpiThreads) {
+        const int m = threadIdx.x >> 3, n = threadIdx.x & 7;
+        const bool valid = m < M && m < MT;
+        const float y = valid ? reduce_partial<MT>(rb, W, m, n) * xscale[m] : 0.f;
+        epi(tile, m, n, y, valid);
+      }
+      buf ^= 1;
+    }
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(288) gemv_tma_plain_kernel(float* out, const float* __restrict__ x,
+                                                             const int8_t* __restrict__ q,
+                                                             const float* __restrict__ scale, const float* resid,
+                                                             int M, int N, int K, const float* __restrict__ norm_w,
+                                                             float eps, int Kc, int stages) {
+  const PlainTiles tiles{q, N, K};
+  const PlainEpi epi{out, scale, resid, N};
+  gemv_tma_body<MT>(tiles, epi, x, M, K, norm_w, eps, Kc, stages);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(288) gemv_tma_qkv_kernel(QkvArgs a, int Kc, int stages) {
+  const QkvTiles tiles{a.q, a.H + 2 * a.Hkv, a.D, a.d};
+  // The position was written by an earlier step's tail kernel, complete before
+  // the preceding kernel could launch this one (programmatic launch chain).
+  const QkvEpi epi{a, tiles, *a.pos};
+  gemv_tma_body<MT>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(288) gemv_tma_gateup_kernel(GateUpArgs a, int Kc, int stages) {
+  const GateUpTiles tiles{a.gate, a.up, a.F, a.d};
+  const GateUpEpi epi{a};
+  gemv_tma_body<MT>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
+}
+
 struct MmaShape {
   int kpw, warps;
 };
@@ -547,6 +835,126 @@ tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   const size_t smem = MmaSmem::bytes(MT, a.d, s.warps);
   const int64_t tiles = (a.F + 3) / 4;
   TB_MMA_DISPATCH(gemv_mma_gateup_kernel, MT, s.kpw, tiles, s.warps, smem, st, pdl, a, l2_prefetch_enabled());
+}
+
+}  // namespace tb
+
+// ---------------------------------------------------------------------------
+// TMA-fed launchers
+// ---------------------------------------------------------------------------
+namespace tb {
+namespace {
+
+struct TmaPlan {
+  int Kc, stages, W;
+  size_t smem;
+};
+
+// Chunk width: the largest divisor of K/64 k-blocks that keeps Kc <= 4096
+// bytes; as many stages as fit (2..4) next to the staged x.
+bool tma_plan(int MT, int K, TmaPlan* p) {
+  if (K % 64 != 0) return false;
+  const int KB = K / 64;
+  int d = 1;
+  while (KB / d > 64 || KB % d != 0) d++;
+  p->Kc = 64 * (KB / d);
+  const int kbc = KB / d;
+  p->W = kbc < 8 ? kbc : 8;
+  const int min_w = (MT * 8 + 31) / 32;
+  if (p->W < min_w) p->W = min_w;
+  for (int s = 4; s >= 2; s--) {
+    TmaLayout L;
+    L.init(MT, K, p->Kc, s, p->W);
+    if (L.total <= 220 * 1024) {
+      p->stages = s;
+      p->smem = L.total;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <typename Kern, typename... Args>
+tb_status_t launch_tma(Kern kern, int64_t tiles, const TmaPlan& p, cudaStream_t st, bool pdl, Args... args) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv_tma)");
+  int64_t grid = sm_count();
+  if (grid > tiles) grid = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((p.W + 1) * 32);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemv_tma)");
+  return TB_SUCCESS;
+}
+
+#define TB_TMA_DISPATCH(KERN, MT_, ...)                                  \
+  do {                                                                   \
+    switch (MT_) {                                                       \
+      case 1: return launch_tma(KERN<1>, __VA_ARGS__);                   \
+      case 2: return launch_tma(KERN<2>, __VA_ARGS__);                   \
+      case 4: return launch_tma(KERN<4>, __VA_ARGS__);                   \
+      default: return launch_tma(KERN<8>, __VA_ARGS__);                  \
+    }                                                                    \
+  } while (0)
+
+}  // namespace
+
+bool gemv_tma_ok(const float* x, const int8_t* q, int64_t M, int64_t K) {
+  if (M < 1 || M > 8 || K % 64 != 0 || K > 65536) return false;
+  if (!aligned(x, 16) || !aligned(q, 16)) return false;
+  TmaPlan p;
+  return tma_plan(mt_of((int)M), (int)K, &p);
+}
+
+tb_status_t gemv_tma_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                           int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(M);
+  TmaPlan p;
+  if (!tma_plan(MT, K, &p)) return TB_ERROR_NOT_SUPPORTED;
+  const int64_t tiles = (N + 7) / 8;
+  TB_TMA_DISPATCH(gemv_tma_plain_kernel, MT, tiles, p, st, pdl, out, x, q, scale, resid, M, N, K, norm_w, eps, p.Kc,
+                  p.stages);
+}
+
+tb_status_t gemv_tma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(a.M);
+  TmaPlan p;
+  if (!tma_plan(MT, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
+  const int64_t tiles = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 8);
+  TB_TMA_DISPATCH(gemv_tma_qkv_kernel, MT, tiles, p, st, pdl, a, p.Kc, p.stages);
+}
+
+tb_status_t gemv_tma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
+  const int MT = mt_of(a.M);
+  TmaPlan p;
+  if (!tma_plan(MT, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
+  const int64_t tiles = (a.F + 3) / 4;
+  TB_TMA_DISPATCH(gemv_tma_gateup_kernel, MT, tiles, p, st, pdl, a, p.Kc, p.stages);
+}
+
+int take_wait_timeouts() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(int));
+  return v;
+}
+
+GemvKind gemv_kind() {
+  static const GemvKind k = [] {
+    const char* e = getenv("TENDO_B200_GEMV");
+    if (e && strcmp(e, "simt") == 0) return GemvKind::kSimt;
+    if (e && strcmp(e, "mma") == 0) return GemvKind::kMma;
+    return GemvKind::kTma;
+  }();
+  return k;
 }
 
 }  // namespace tb

@@ -74,9 +74,18 @@ tb_status_t gemv_mma_plain(float* out, const float* x, const int8_t* q, const fl
                            int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl);
 tb_status_t gemv_mma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl);
 tb_status_t gemv_mma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
-// Kernel family for the decode GEMVs: true = tensor cores (default), false =
-// CUDA-core FMA kernels (TENDO_B200_GEMV=simt).
-bool gemv_use_mma();
+// TMA-fed tensor-core GEMVs (weights streamed to shared memory by cp.async.bulk).
+bool gemv_tma_ok(const float* x, const int8_t* q, int64_t M, int64_t K);
+tb_status_t gemv_tma_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                           int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl);
+tb_status_t gemv_tma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl);
+tb_status_t gemv_tma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
+// Bounded device waits that expired since the last call (and resets the count).
+int take_wait_timeouts();
+// Kernel family of the decode GEMVs (TENDO_B200_GEMV = tma | mma | simt; default tma).
+enum class GemvKind { kTma, kMma, kSimt };
+GemvKind gemv_kind();
+inline bool gemv_use_mma() { return gemv_kind() == GemvKind::kMma; }
 bool l2_prefetch_enabled();
 
 // attention.cu
