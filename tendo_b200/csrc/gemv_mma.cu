@@ -332,6 +332,21 @@ struct PlainEpi {
     if (resid) v += resid[(size_t)m * N + r];
     out[(size_t)m * N + r] = v;
   }
+  // Split form for the TMA kernel: pre() issues the global loads early.
+  __device__ __forceinline__ float4 pre(int tile, int m, int n, bool valid) const {
+    const int r = tile * 8 + n;
+    float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid && r < N) {
+      c.x = scale[r];
+      if (resid) c.y = resid[(size_t)m * N + r];
+    }
+    return c;
+  }
+  __device__ __forceinline__ void post(int tile, int m, int n, float y, bool valid, float4 c) const {
+    const int r = tile * 8 + n;
+    if (!valid || r >= N) return;
+    out[(size_t)m * N + r] = resid ? y * c.x + c.y : y * c.x;
+  }
 };
 
 // Column n < 4 holds row i of a head, column n + 4 row i + D/2: rotate-half
@@ -363,6 +378,38 @@ struct QkvEpi {
       o[i + half] = x1;
     }
   }
+  __device__ __forceinline__ float4 pre(int tile, int m, int n, bool valid) const {
+    const int half = a.D / 2;
+    const int head = tiles.head(tile), i = tiles.i0(tile) + (n & 3);
+    const int r = head * a.D + i + (n >> 2) * half;
+    float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) {
+      c.x = a.scale[r];
+      c.y = a.cos_t[pos * half + i];
+      c.z = a.sin_t[pos * half + i];
+    }
+    return c;
+  }
+  __device__ __forceinline__ void post(int tile, int m, int n, float y, bool valid, float4 c) const {
+    const int half = a.D / 2;
+    const int head = tiles.head(tile), i = tiles.i0(tile) + (n & 3);
+    const float v = valid ? y * c.x : 0.f;
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+    if (!valid || n >= 4) return;
+    const float x0 = v, x1 = partner;
+    if (head < a.H + a.Hkv) {
+      const float o0 = __fsub_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.z));
+      const float o1 = __fadd_rn(__fmul_rn(x0, c.z), __fmul_rn(x1, c.y));
+      float* o = head < a.H ? a.qout + ((size_t)m * a.H + head) * a.D
+                            : a.kcache + (((size_t)m * a.Hkv + (head - a.H)) * a.max_seq + pos) * a.D;
+      o[i] = o0;
+      o[i + half] = o1;
+    } else {
+      float* o = a.vcache + (((size_t)m * a.Hkv + (head - a.H - a.Hkv)) * a.max_seq + pos) * a.D;
+      o[i] = x0;
+      o[i + half] = x1;
+    }
+  }
 };
 
 // Columns 0..3 gate rows j0.., 4..7 the same up rows: act = silu(gate) * up.
@@ -372,6 +419,21 @@ struct GateUpEpi {
     const int j = tile * 4 + (n & 3);
     const bool in = valid && j < a.F;
     const float v = in ? y * ((n >> 2) ? a.up_scale[j] : a.gate_scale[j]) : 0.f;
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+    if (!in || n >= 4) return;
+    const float sig = 1.0f / (1.0f + expf(-v));
+    a.act[(size_t)m * a.F + j] = (v * sig) * partner;
+  }
+  __device__ __forceinline__ float4 pre(int tile, int m, int n, bool valid) const {
+    const int j = tile * 4 + (n & 3);
+    float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid && j < a.F) c.x = (n >> 2) ? a.up_scale[j] : a.gate_scale[j];
+    return c;
+  }
+  __device__ __forceinline__ void post(int tile, int m, int n, float y, bool valid, float4 c) const {
+    const int j = tile * 4 + (n & 3);
+    const bool in = valid && j < a.F;
+    const float v = in ? y * c.x : 0.f;
     const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
     if (!in || n >= 4) return;
     const float sig = 1.0f / (1.0f + expf(-v));
@@ -619,10 +681,20 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
   stage_x_f16_n<MT>(hi, lo, xscale, x, M, K, norm_w, eps, scratch, nthreads);
   const int g = lane >> 2, t = lane & 3;
   constexpr int kEpiThreads = ((MT * 8 + 31) / 32) * 32;
+  constexpr int kEpiWarps = kEpiThreads / 32;
+  const int epi_groups = W / kEpiWarps;
   float d[4] = {0.f, 0.f, 0.f, 0.f};
   int buf = 0;
   for (int u = 0; u < units; u++) {
-    const int s = u % stages, use = u / stages, ch = u % nch;
+    const int s = u % stages, use = u / stages, ch = u % nch, it = u / nch;
+    const int tile = (int)blockIdx.x + it * (int)gridDim.x;
+    // the epilogue of tile `it` runs on warps [ew0, ew0 + kEpiWarps), rotating
+    const int ew0 = (it % epi_groups) * kEpiWarps;
+    const bool is_epi = ch == nch - 1 && warp >= ew0 && warp < ew0 + kEpiWarps;
+    const int et = (int)threadIdx.x - ew0 * 32, em = et >> 3, en = et & 7;
+    const bool evalid = em < M && em < MT;
+    float4 ec = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (is_epi) ec = epi.pre(tile, em, en, evalid);  // global loads overlap the MMA work below
     if (ch == 0) d[0] = d[1] = d[2] = d[3] = 0.f;
     mbar_wait(&full[s], (uint32_t)(use & 1));
     const unsigned char* st = stage_base + (size_t)s * L.stage_bytes + (size_t)g * L.RS + 16 * t;
@@ -655,15 +727,12 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
     }
     mbar_arrive(&empty[s]);
     if (ch == nch - 1) {
-      const int tile = (int)blockIdx.x + (u / nch) * (int)gridDim.x;
       float* rb = red + (size_t)buf * W * 64;
       store_partial<MT>(rb, d, warp, g, t);
       consumer_sync(nthreads);
-      if (threadIdx.x < kEpiThreads) {
-        const int m = threadIdx.x >> 3, n = threadIdx.x & 7;
-        const bool valid = m < M && m < MT;
-        const float y = valid ? reduce_partial<MT>(rb, W, m, n) * xscale[m] : 0.f;
-        epi(tile, m, n, y, valid);
+      if (warp >= ew0 && warp < ew0 + kEpiWarps) {
+        const float y = evalid ? reduce_partial<MT>(rb, W, em, en) * xscale[em] : 0.f;
+        epi.post(tile, em, en, y, evalid, ec);
       }
       buf ^= 1;
     }
@@ -846,7 +915,7 @@ namespace tb {
 namespace {
 
 struct TmaPlan {
-  int Kc, stages, W;
+  int Kc, stages, W, ctas_per_sm;
   size_t smem;
 };
 
@@ -862,12 +931,25 @@ bool tma_plan(int MT, int K, TmaPlan* p) {
   p->W = kbc < 8 ? kbc : 8;
   const int min_w = (MT * 8 + 31) / 32;
   if (p->W < min_w) p->W = min_w;
+  // two CTAs per SM when two stages each fit in half the shared memory, so
+  // one CTA's tile barrier and epilogue overlap the other's streaming
+  for (int s = 3; s >= 2; s--) {
+    TmaLayout L;
+    L.init(MT, K, p->Kc, s, p->W);
+    if (L.total <= 110 * 1024) {
+      p->stages = s;
+      p->smem = L.total;
+      p->ctas_per_sm = 2;
+      return true;
+    }
+  }
   for (int s = 4; s >= 2; s--) {
     TmaLayout L;
     L.init(MT, K, p->Kc, s, p->W);
     if (L.total <= 220 * 1024) {
       p->stages = s;
       p->smem = L.total;
+      p->ctas_per_sm = 1;
       return true;
     }
   }
@@ -878,7 +960,7 @@ template <typename Kern, typename... Args>
 tb_status_t launch_tma(Kern kern, int64_t tiles, const TmaPlan& p, cudaStream_t st, bool pdl, Args... args) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv_tma)");
-  int64_t grid = sm_count();
+  int64_t grid = (int64_t)sm_count() * p.ctas_per_sm;
   if (grid > tiles) grid = tiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
