@@ -521,33 +521,36 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
 
-// stage_x_f16 for the first `nthreads` threads, synchronised with a named barrier.
-template <int MT>
-__device__ void stage_x_f16_n(__half* hi, __half* lo, float* xscale, const float* __restrict__ x, int M, int K,
-                              const float* __restrict__ norm_w, float eps, float* red, int nthreads) {
+// Stage x (optionally RMSNorm(x) * w) as three int8 digit rows per batch row:
+// u = v / s with s = max|v| / 127, d0 = rint(u), d1 = rint((u - d0) * 128),
+// d2 = rint(((u - d0) * 128 - d1) * 128); u = d0 + d1 / 128 + d2 / 128^2 to
+// within 2^-15 (every remainder step is exact in fp32).  Digit p of row m goes
+// to digit row p * M + m (stride RSX bytes); rows 3M .. 16 RG - 1 are zero.
+template <int RG>
+__device__ void stage_x_digits(int8_t* dig, int RSX, float* xscale, const float* __restrict__ x, int M, int K,
+                               const float* __restrict__ norm_w, float eps, float* red, int nthreads) {
   const int warps = nthreads >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = K >> 2;
-  float ss[MT], mx[MT];
+  constexpr int MX = 16 * RG / 3 + 1;  // batch rows this layout can hold (5 or 10)
+  float ss[MX], mx[MX];
 #pragma unroll
-  for (int m = 0; m < MT; m++) ss[m] = mx[m] = 0.f;
+  for (int m = 0; m < MX; m++) ss[m] = mx[m] = 0.f;
   for (int v = threadIdx.x; v < nv; v += nthreads) {
+    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w) w4 = reinterpret_cast<const float4*>(norm_w)[v];
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
+    for (int m = 0; m < MX; m++) {
       if (m < M) {
         const float4 t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
         ss[m] += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
-        float a = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
-        if (norm_w) {
-          const float4 w = reinterpret_cast<const float4*>(norm_w)[v];
-          a = fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w)));
-        }
-        mx[m] = fmaxf(mx[m], a);
+        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(t.x * w4.x), fabsf(t.y * w4.y)),
+                                   fmaxf(fabsf(t.z * w4.z), fabsf(t.w * w4.w))));
       }
     }
   }
 #pragma unroll
-  for (int m = 0; m < MT; m++) {
+  for (int m = 0; m < MX; m++) {
     const float s = warp_sum(ss[m]), a = warp_max(mx[m]);
     if (lane == 0) {
       red[(2 * m) * 32 + warp] = s;
@@ -555,92 +558,100 @@ __device__ void stage_x_f16_n(__half* hi, __half* lo, float* xscale, const float
     }
   }
   consumer_sync(nthreads);
-  float rms[MT], inv_sc[MT];
+  float rms[MX], inv[MX];
 #pragma unroll
-  for (int m = 0; m < MT; m++) {
+  for (int m = 0; m < MX; m++) {
     float s = 0.f, a = 0.f;
     for (int w = 0; w < warps; w++) {
       s += red[(2 * m) * 32 + w];
       a = fmaxf(a, red[(2 * m + 1) * 32 + w]);
     }
     rms[m] = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)) : 1.0f;
-    if (norm_w) a = a / rms[m] * 1.0001f;
-    int e = 0;
-    if (a > 0.f && isfinite(a)) {
-      frexpf(a, &e);
-      e -= 14;
-    }
-    inv_sc[m] = ldexpf(1.0f, -e);
-    if (threadIdx.x == 0) xscale[m] = ldexpf(1.0f, e);
+    if (norm_w) a = a / rms[m] * 1.0001f;  // bound of max |x / rms * w|
+    const float sc = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
+    inv[m] = 1.0f / sc;
+    if (threadIdx.x == 0 && m < M) xscale[m] = sc;
   }
   for (int v = threadIdx.x; v < nv; v += nthreads) {
     float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
     if (norm_w) w4 = reinterpret_cast<const float4*>(norm_w)[v];
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m < M) {
-        t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
-        if (norm_w) {
-          t.x = __fmul_rn(__fdiv_rn(t.x, rms[m]), w4.x);
-          t.y = __fmul_rn(__fdiv_rn(t.y, rms[m]), w4.y);
-          t.z = __fmul_rn(__fdiv_rn(t.z, rms[m]), w4.z);
-          t.w = __fmul_rn(__fdiv_rn(t.w, rms[m]), w4.w);
-        }
-        t.x *= inv_sc[m];
-        t.y *= inv_sc[m];
-        t.z *= inv_sc[m];
-        t.w *= inv_sc[m];
+    for (int m = 0; m < MX; m++) {
+      if (m >= M) continue;
+      float4 t = reinterpret_cast<const float4*>(x + (size_t)m * K)[v];
+      if (norm_w) {
+        t.x = __fmul_rn(__fdiv_rn(t.x, rms[m]), w4.x);
+        t.y = __fmul_rn(__fdiv_rn(t.y, rms[m]), w4.y);
+        t.z = __fmul_rn(__fdiv_rn(t.z, rms[m]), w4.z);
+        t.w = __fmul_rn(__fdiv_rn(t.w, rms[m]), w4.w);
       }
       const float vals[4] = {t.x, t.y, t.z, t.w};
-      __half h[4], l[4];
+      uint32_t p0 = 0, p1 = 0, p2 = 0;
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        h[i] = __float2half_rn(vals[i]);
-        l[i] = __float2half_rn(vals[i] - __half2float(h[i]));
+        const float u = fminf(fmaxf(vals[i] * inv[m], -127.0f), 127.0f);
+        const float d0 = rintf(u);
+        const float r1 = (u - d0) * 128.0f;
+        const float d1 = rintf(r1);
+        const float d2 = rintf((r1 - d1) * 128.0f);
+        p0 |= ((uint32_t)(int)d0 & 0xffu) << (8 * i);
+        p1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * i);
+        p2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * i);
       }
-      __half* hp = hi + (size_t)m * (K + kPad) + 4 * v;
-      __half* lp = lo + (size_t)m * (K + kPad) + 4 * v;
-      *reinterpret_cast<__half2*>(hp) = __halves2half2(h[0], h[1]);
-      *reinterpret_cast<__half2*>(hp + 2) = __halves2half2(h[2], h[3]);
-      *reinterpret_cast<__half2*>(lp) = __halves2half2(l[0], l[1]);
-      *reinterpret_cast<__half2*>(lp + 2) = __halves2half2(l[2], l[3]);
+      *reinterpret_cast<uint32_t*>(dig + (size_t)(0 * M + m) * RSX + 4 * v) = p0;
+      *reinterpret_cast<uint32_t*>(dig + (size_t)(1 * M + m) * RSX + 4 * v) = p1;
+      *reinterpret_cast<uint32_t*>(dig + (size_t)(2 * M + m) * RSX + 4 * v) = p2;
     }
+  }
+  // zero the unused digit rows
+  for (int i = threadIdx.x; i < (16 * RG - 3 * M) * (K / 4); i += nthreads) {
+    const int r = 3 * M + i / (K / 4), c = i % (K / 4);
+    *reinterpret_cast<uint32_t*>(dig + (size_t)r * RSX + 4 * c) = 0u;
   }
   consumer_sync(nthreads);
 }
 
+__device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 struct TmaLayout {
-  int Kc, RS, stages, W;
+  int Kc, RS, RSX, stages, W;
   size_t stage_bytes, x_off, xs_off, red_off, scr_off, bar_off, total;
-  __host__ __device__ void init(int MT, int K, int Kc_, int stages_, int W_) {
+  __host__ __device__ static int stride(int bytes) { return (bytes % 128 == 0) ? bytes + 64 : bytes; }
+  __host__ __device__ void init(int RG, int K, int Kc_, int stages_, int W_) {
     Kc = Kc_;
-    RS = (Kc % 128 == 0) ? Kc + 64 : Kc;
+    RS = stride(Kc);
+    RSX = stride(K);
     stages = stages_;
     W = W_;
     stage_bytes = (size_t)8 * RS;
     x_off = (size_t)stages * stage_bytes;
-    xs_off = x_off + (size_t)2 * MT * (K + kPad) * 2;
-    red_off = xs_off + 16 * sizeof(float);
-    scr_off = red_off + (size_t)2 * W * 64 * sizeof(float);
-    bar_off = (scr_off + 512 * sizeof(float) + 15) & ~(size_t)15;
+    xs_off = x_off + (size_t)16 * RG * RSX;
+    red_off = (xs_off + 16 * sizeof(float) + 15) & ~(size_t)15;
+    scr_off = red_off + (size_t)2 * W * 16 * RG * 8 * sizeof(int);
+    bar_off = (scr_off + 2 * 16 * 32 * sizeof(float) + 15) & ~(size_t)15;
     total = bar_off + (size_t)2 * stages * sizeof(uint64_t);
   }
 };
 
-template <int MT, typename Tiles, typename Epi>
+// RG row groups of 16 digit rows: RG = 1 serves M <= 5, RG = 2 serves M <= 8.
+template <int RG, typename Tiles, typename Epi>
 __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi, const float* __restrict__ x, int M,
                                               int K, const float* __restrict__ norm_w, float eps, int Kc,
                                               int stages) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps; warp W produces
   TmaLayout L;
-  L.init(MT, K, Kc, stages, W);
+  L.init(RG, K, Kc, stages, W);
   unsigned char* stage_base = smem;
-  __half* hi = reinterpret_cast<__half*>(smem + L.x_off);
-  __half* lo = hi + (size_t)MT * (K + kPad);
+  int8_t* dig = reinterpret_cast<int8_t*>(smem + L.x_off);
   float* xscale = reinterpret_cast<float*>(smem + L.xs_off);
-  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  int* red = reinterpret_cast<int*>(smem + L.red_off);
   float* scratch = reinterpret_cast<float*>(smem + L.scr_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + stages;
@@ -667,10 +678,11 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
         unsigned char* dst = stage_base + (size_t)s * L.stage_bytes;
         mbar_expect_tx(&full[s], (uint32_t)(8 * Kc));
 #pragma unroll
-        for (int n = 0; n < 8; n++) tma_load_1d(dst + (size_t)n * L.RS, tiles.row(tile, n) + (size_t)ch * Kc, (uint32_t)Kc, &full[s]);
+        for (int n = 0; n < 8; n++)
+          tma_load_1d(dst + (size_t)n * L.RS, tiles.row(tile, n) + (size_t)ch * Kc, (uint32_t)Kc, &full[s]);
       }
-      // the copies of the last stages land before the consumers finish with
-      // them, so the CTA never exits with a copy in flight
+      // every copy completes before the consumers release its stage, so the
+      // CTA never exits with a copy in flight
     }
     pdl_launch_dependents();
     return;
@@ -678,12 +690,14 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
   pdl_wait();
   pdl_launch_dependents();
   const int nthreads = W * 32;
-  stage_x_f16_n<MT>(hi, lo, xscale, x, M, K, norm_w, eps, scratch, nthreads);
+  stage_x_digits<RG>(dig, L.RSX, xscale, x, M, K, norm_w, eps, scratch, nthreads);
   const int g = lane >> 2, t = lane & 3;
-  constexpr int kEpiThreads = ((MT * 8 + 31) / 32) * 32;
+  constexpr int MXT = RG == 1 ? 5 : 8;           // batch rows per launch
+  constexpr int kEpiThreads = ((MXT * 8 + 31) / 32) * 32;
   constexpr int kEpiWarps = kEpiThreads / 32;
   const int epi_groups = W / kEpiWarps;
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  const int R = 3 * M;
+  int d[RG][4];
   int buf = 0;
   for (int u = 0; u < units; u++) {
     const int s = u % stages, use = u / stages, ch = u % nch, it = u / nch;
@@ -692,46 +706,57 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
     const int ew0 = (it % epi_groups) * kEpiWarps;
     const bool is_epi = ch == nch - 1 && warp >= ew0 && warp < ew0 + kEpiWarps;
     const int et = (int)threadIdx.x - ew0 * 32, em = et >> 3, en = et & 7;
-    const bool evalid = em < M && em < MT;
+    const bool evalid = em < M;
     float4 ec = make_float4(0.f, 0.f, 0.f, 0.f);
     if (is_epi) ec = epi.pre(tile, em, en, evalid);  // global loads overlap the MMA work below
-    if (ch == 0) d[0] = d[1] = d[2] = d[3] = 0.f;
+    if (ch == 0) {
+#pragma unroll
+      for (int rg = 0; rg < RG; rg++) d[rg][0] = d[rg][1] = d[rg][2] = d[rg][3] = 0;
+    }
     mbar_wait(&full[s], (uint32_t)(use & 1));
     const unsigned char* st = stage_base + (size_t)s * L.stage_bytes + (size_t)g * L.RS + 16 * t;
-#pragma unroll 2
+    const int8_t* xr = dig + (size_t)g * L.RSX + ch * Kc + 16 * t;
+#pragma unroll 4
     for (int kb = warp; kb < kbc; kb += W) {
       const uint4 wv = *reinterpret_cast<const uint4*>(st + kb * 64);
-      const int k = ch * Kc + kb * 64 + 16 * t;
-      uint32_t xh[8], xl[8];
-      if (g < MT) {
-        const uint4* ph = reinterpret_cast<const uint4*>(hi + (size_t)g * (K + kPad) + k);
-        const uint4* pl = reinterpret_cast<const uint4*>(lo + (size_t)g * (K + kPad) + k);
-        const uint4 h0 = ph[0], h1 = ph[1], l0 = pl[0], l1 = pl[1];
-        xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
-        xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
-        xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
-        xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
-      } else {
 #pragma unroll
-        for (int p = 0; p < 8; p++) xh[p] = xl[p] = 0u;
-      }
-      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint32_t ux = words[j] ^ 0x80808080u;
-        const uint32_t b0 = i8pair_to_f16x2(ux, 0x4140);
-        const uint32_t b1 = i8pair_to_f16x2(ux, 0x4342);
-        const uint32_t a[4] = {xh[2 * j], xl[2 * j], xh[2 * j + 1], xl[2 * j + 1]};
-        mma_16816(d, a, b0, b1);
+      for (int rg = 0; rg < RG; rg++) {
+        const uint4 xa = *reinterpret_cast<const uint4*>(xr + (size_t)(16 * rg) * L.RSX + kb * 64);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xr + (size_t)(16 * rg + 8) * L.RSX + kb * 64);
+        imma_16832(d[rg], xa.x, xb.x, xa.y, xb.y, wv.x, wv.y);
+        imma_16832(d[rg], xa.z, xb.z, xa.w, xb.w, wv.z, wv.w);
       }
     }
     mbar_arrive(&empty[s]);
     if (ch == nch - 1) {
-      float* rb = red + (size_t)buf * W * 64;
-      store_partial<MT>(rb, d, warp, g, t);
+      // partial tile of this warp: red[buf][warp][row][n], rows < 3M
+      int* rb = red + (size_t)buf * W * (16 * RG * 8);
+      int* rw = rb + (size_t)warp * (16 * RG * 8);
+#pragma unroll
+      for (int rg = 0; rg < RG; rg++) {
+        const int r0 = 16 * rg + g, r1 = r0 + 8;
+        if (r0 < R) {
+          rw[r0 * 8 + 2 * t] = d[rg][0];
+          rw[r0 * 8 + 2 * t + 1] = d[rg][1];
+        }
+        if (r1 < R) {
+          rw[r1 * 8 + 2 * t] = d[rg][2];
+          rw[r1 * 8 + 2 * t + 1] = d[rg][3];
+        }
+      }
       consumer_sync(nthreads);
       if (warp >= ew0 && warp < ew0 + kEpiWarps) {
-        const float y = evalid ? reduce_partial<MT>(rb, W, em, en) * xscale[em] : 0.f;
+        float y = 0.f;
+        if (evalid) {
+          int s0 = 0, s1 = 0, s2 = 0;
+          for (int w = 0; w < W; w++) {
+            const int* p = rb + (size_t)w * (16 * RG * 8);
+            s0 += p[(0 * M + em) * 8 + en];
+            s1 += p[(1 * M + em) * 8 + en];
+            s2 += p[(2 * M + em) * 8 + en];
+          }
+          y = xscale[em] * ((float)s0 + (float)s1 * (1.0f / 128.0f) + (float)s2 * (1.0f / 16384.0f));
+        }
         epi.post(tile, em, en, y, evalid, ec);
       }
       buf ^= 1;
@@ -739,7 +764,7 @@ __device__ __forceinline__ void gemv_tma_body(const Tiles& tiles, const Epi& epi
   }
 }
 
-template <int MT>
+template <int RG>
 __global__ void __launch_bounds__(288) gemv_tma_plain_kernel(float* out, const float* __restrict__ x,
                                                              const int8_t* __restrict__ q,
                                                              const float* __restrict__ scale, const float* resid,
@@ -747,23 +772,23 @@ __global__ void __launch_bounds__(288) gemv_tma_plain_kernel(float* out, const f
                                                              float eps, int Kc, int stages) {
   const PlainTiles tiles{q, N, K};
   const PlainEpi epi{out, scale, resid, N};
-  gemv_tma_body<MT>(tiles, epi, x, M, K, norm_w, eps, Kc, stages);
+  gemv_tma_body<RG>(tiles, epi, x, M, K, norm_w, eps, Kc, stages);
 }
 
-template <int MT>
+template <int RG>
 __global__ void __launch_bounds__(288) gemv_tma_qkv_kernel(QkvArgs a, int Kc, int stages) {
   const QkvTiles tiles{a.q, a.H + 2 * a.Hkv, a.D, a.d};
   // The position was written by an earlier step's tail kernel, complete before
   // the preceding kernel could launch this one (programmatic launch chain).
   const QkvEpi epi{a, tiles, *a.pos};
-  gemv_tma_body<MT>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
+  gemv_tma_body<RG>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
 }
 
-template <int MT>
+template <int RG>
 __global__ void __launch_bounds__(288) gemv_tma_gateup_kernel(GateUpArgs a, int Kc, int stages) {
   const GateUpTiles tiles{a.gate, a.up, a.F, a.d};
   const GateUpEpi epi{a};
-  gemv_tma_body<MT>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
+  gemv_tma_body<RG>(tiles, epi, a.h, a.M, a.d, a.norm_w, a.eps, Kc, stages);
 }
 
 struct MmaShape {
@@ -921,7 +946,7 @@ struct TmaPlan {
 
 // Chunk width: the largest divisor of K/64 k-blocks that keeps Kc <= 4096
 // bytes; as many stages as fit (2..4) next to the staged x.
-bool tma_plan(int MT, int K, TmaPlan* p) {
+bool tma_plan(int RG, int K, TmaPlan* p) {
   if (K % 64 != 0) return false;
   const int KB = K / 64;
   int d = 1;
@@ -929,13 +954,13 @@ bool tma_plan(int MT, int K, TmaPlan* p) {
   p->Kc = 64 * (KB / d);
   const int kbc = KB / d;
   p->W = kbc < 8 ? kbc : 8;
-  const int min_w = (MT * 8 + 31) / 32;
+  const int min_w = RG == 1 ? 2 : 2;  // the epilogue takes up to two warps
   if (p->W < min_w) p->W = min_w;
   // two CTAs per SM when two stages each fit in half the shared memory, so
   // one CTA's tile barrier and epilogue overlap the other's streaming
   for (int s = 3; s >= 2; s--) {
     TmaLayout L;
-    L.init(MT, K, p->Kc, s, p->W);
+    L.init(RG, K, p->Kc, s, p->W);
     if (L.total <= 110 * 1024) {
       p->stages = s;
       p->smem = L.total;
@@ -945,7 +970,7 @@ bool tma_plan(int MT, int K, TmaPlan* p) {
   }
   for (int s = 4; s >= 2; s--) {
     TmaLayout L;
-    L.init(MT, K, p->Kc, s, p->W);
+    L.init(RG, K, p->Kc, s, p->W);
     if (L.total <= 220 * 1024) {
       p->stages = s;
       p->smem = L.total;
@@ -977,15 +1002,13 @@ tb_status_t launch_tma(Kern kern, int64_t tiles, const TmaPlan& p, cudaStream_t 
   return TB_SUCCESS;
 }
 
-#define TB_TMA_DISPATCH(KERN, MT_, ...)                                  \
+#define TB_TMA_DISPATCH(KERN, RG_, ...)                                  \
   do {                                                                   \
-    switch (MT_) {                                                       \
-      case 1: return launch_tma(KERN<1>, __VA_ARGS__);                   \
-      case 2: return launch_tma(KERN<2>, __VA_ARGS__);                   \
-      case 4: return launch_tma(KERN<4>, __VA_ARGS__);                   \
-      default: return launch_tma(KERN<8>, __VA_ARGS__);                  \
-    }                                                                    \
+    if (RG_ == 1) return launch_tma(KERN<1>, __VA_ARGS__);               \
+    return launch_tma(KERN<2>, __VA_ARGS__);                             \
   } while (0)
+
+int rg_of(int M) { return M <= 5 ? 1 : 2; }
 
 }  // namespace
 
@@ -993,33 +1016,33 @@ bool gemv_tma_ok(const float* x, const int8_t* q, int64_t M, int64_t K) {
   if (M < 1 || M > 8 || K % 64 != 0 || K > 65536) return false;
   if (!aligned(x, 16) || !aligned(q, 16)) return false;
   TmaPlan p;
-  return tma_plan(mt_of((int)M), (int)K, &p);
+  return tma_plan(rg_of((int)M), (int)K, &p);
 }
 
 tb_status_t gemv_tma_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
                            int N, int K, const float* norm_w, float eps, cudaStream_t st, bool pdl) {
-  const int MT = mt_of(M);
+  const int RG = rg_of(M);
   TmaPlan p;
-  if (!tma_plan(MT, K, &p)) return TB_ERROR_NOT_SUPPORTED;
+  if (!tma_plan(RG, K, &p)) return TB_ERROR_NOT_SUPPORTED;
   const int64_t tiles = (N + 7) / 8;
-  TB_TMA_DISPATCH(gemv_tma_plain_kernel, MT, tiles, p, st, pdl, out, x, q, scale, resid, M, N, K, norm_w, eps, p.Kc,
+  TB_TMA_DISPATCH(gemv_tma_plain_kernel, RG, tiles, p, st, pdl, out, x, q, scale, resid, M, N, K, norm_w, eps, p.Kc,
                   p.stages);
 }
 
 tb_status_t gemv_tma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl) {
-  const int MT = mt_of(a.M);
+  const int RG = rg_of(a.M);
   TmaPlan p;
-  if (!tma_plan(MT, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
+  if (!tma_plan(RG, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
   const int64_t tiles = (int64_t)(a.H + 2 * a.Hkv) * (a.D / 8);
-  TB_TMA_DISPATCH(gemv_tma_qkv_kernel, MT, tiles, p, st, pdl, a, p.Kc, p.stages);
+  TB_TMA_DISPATCH(gemv_tma_qkv_kernel, RG, tiles, p, st, pdl, a, p.Kc, p.stages);
 }
 
 tb_status_t gemv_tma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
-  const int MT = mt_of(a.M);
+  const int RG = rg_of(a.M);
   TmaPlan p;
-  if (!tma_plan(MT, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
+  if (!tma_plan(RG, a.d, &p)) return TB_ERROR_NOT_SUPPORTED;
   const int64_t tiles = (a.F + 3) / 4;
-  TB_TMA_DISPATCH(gemv_tma_gateup_kernel, MT, tiles, p, st, pdl, a, p.Kc, p.stages);
+  TB_TMA_DISPATCH(gemv_tma_gateup_kernel, RG, tiles, p, st, pdl, a, p.Kc, p.stages);
 }
 
 int take_wait_timeouts() {
