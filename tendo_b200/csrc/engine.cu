@@ -47,6 +47,10 @@ struct tb_model {
   int nsplit = 1;
   bool fused = false;
   bool pdl = true;
+  bool mk = false;      // whole decode step as one persistent kernel (batch 1)
+  int mk_nsplit = 1;
+  unsigned int* bar_counter = nullptr;
+  int* err_word = nullptr;
   cudaGraphExec_t graph = nullptr;
   std::vector<void*> allocs;
 };
@@ -329,11 +333,60 @@ tb_status_t decode_step_fused(tb_model* m) {
   return TB_SUCCESS;
 }
 
+// Arguments of the persistent decode kernel (decode_mk.cu).
+tb::MkArgs mk_args(tb_model* m) {
+  tb::MkArgs a{};
+  a.L = (int)m->L;
+  a.d = (int)m->d;
+  a.H = (int)m->H;
+  a.Hkv = (int)m->Hkv;
+  a.D = (int)m->D;
+  a.F = (int)m->F;
+  a.V = (int)m->V;
+  a.max_seq = (int)m->Ms;
+  a.nsplit = m->mk_nsplit;
+  a.eps = m->c.eps;
+  a.attn_scale = 1.0f / (float)sqrt((double)m->D);
+  a.wqkv = m->wqkv;
+  a.sqkv = m->sqkv;
+  a.wo = m->wo;
+  a.so = m->so;
+  a.wg = m->wgate;
+  a.sg = m->sgate;
+  a.wu = m->wup;
+  a.su = m->sup;
+  a.wd = m->wdown;
+  a.sd = m->sdown;
+  a.attn_norm = m->attn_norm;
+  a.mlp_norm = m->mlp_norm;
+  a.final_norm = m->final_norm;
+  a.embed = m->embed;
+  a.lm_head = m->lm_head;
+  a.cos_t = m->cos_t;
+  a.sin_t = m->sin_t;
+  a.kc = m->kc;
+  a.vc = m->vc;
+  a.h = m->h;
+  a.q = m->qbuf;
+  a.partial = m->partial;
+  a.act = m->g;
+  a.logits = m->logits;
+  a.keys = m->keys;
+  a.tokens = m->tokens;
+  a.history = m->history;
+  a.step = m->step;
+  a.pos = m->pos;
+  a.hist_cap = m->hist_cap;
+  a.bar_counter = m->bar_counter;
+  a.err = m->err_word;
+  return a;
+}
+
 tb_status_t build_graph(tb_model* m) {
   if (m->graph) return TB_SUCCESS;
   cudaGraph_t g = nullptr;
   TB_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-  tb_status_t s = decode_step_fused(m);
+  tb_status_t s = m->mk ? tb::megakernel_launch(mk_args(m), m->stream) : decode_step_fused(m);
   cudaError_t e = cudaStreamEndCapture(m->stream, &g);
   if (s != TB_SUCCESS) {
     if (g) cudaGraphDestroy(g);
@@ -385,6 +438,16 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);
+  {
+    const char* e = getenv("TENDO_B200_MEGAKERNEL");
+    m->mk = !(e && e[0] == '0') &&
+            tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
+    int ns = tb::sm_count() / (int)m->Hkv;  // one attention unit per SM
+    if (ns < 1) ns = 1;
+    if (ns > 8) ns = 8;
+    if (ns > m->nsplit) ns = m->nsplit;
+    m->mk_nsplit = ns;
+  }
   tb_status_t s = TB_SUCCESS;
   auto A = [&](tb_status_t r) {
     if (s == TB_SUCCESS) s = r;
@@ -429,6 +492,8 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   A(dalloc(m, &m->pos, 1));
   A(dalloc(m, &m->step, 1));
   A(dalloc(m, &m->bad, 1));
+  A(dalloc(m, &m->bar_counter, 1));
+  A(dalloc(m, &m->err_word, 1));
   if (s == TB_SUCCESS) {
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) s = tb::cuda_fail(e, "cudaStreamCreate");
@@ -444,6 +509,8 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
     if (e == cudaSuccess) e = cudaMemset(m->pos, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->step, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->bad, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(m->bar_counter, 0, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(m->err_word, 0, sizeof(int));
     if (e != cudaSuccess) s = tb::cuda_fail(e, "engine init");
   }
   if (s != TB_SUCCESS) {
@@ -661,11 +728,24 @@ extern "C" tb_status_t tb_model_decode(tb_model* m, const int64_t* start_tokens_
   return TB_SUCCESS;
 }
 
+static tb_status_t check_waits(tb_model* m);
+
 extern "C" tb_status_t tb_model_tokens(tb_model* m, int64_t* out_host, int64_t count) {
   TB_REQUIRE(m && out_host && count >= 0 && count <= m->hist_cap);
   DeviceGuard guard(m->device);
   TB_CUDA(cudaStreamSynchronize(m->stream));
   if (count) TB_CUDA(cudaMemcpy(out_host, m->history, sizeof(int64_t) * count * m->B, cudaMemcpyDeviceToHost));
+  return check_waits(m);
+}
+
+// Device-side bounded waits that expired since the last check.
+static tb_status_t check_waits(tb_model* m) {
+  int v = 0, zero = 0;
+  TB_CUDA(cudaMemcpy(&v, m->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    TB_CUDA(cudaMemcpy(m->err_word, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    return TB_ERROR_TIMEOUT;
+  }
   return TB_SUCCESS;
 }
 
@@ -673,7 +753,7 @@ extern "C" tb_status_t tb_model_sync(tb_model* m) {
   TB_REQUIRE(m);
   DeviceGuard guard(m->device);
   TB_CUDA(cudaStreamSynchronize(m->stream));
-  return TB_SUCCESS;
+  return check_waits(m);
 }
 
 extern "C" tb_stream_t tb_model_stream(tb_model* m) { return m ? (tb_stream_t)m->stream : nullptr; }
@@ -682,6 +762,7 @@ extern "C" int64_t tb_model_launches_per_step(const tb_model* m) {
   if (!m) return 0;
   if (!m->fused) return -1;
   // embedding + per layer (qkv, attention, combine, o, gate/up, down) + lm_head + tail
+  if (m->mk) return 1;
   return 1 + m->L * 6 + 2;
 }
 

@@ -58,6 +58,48 @@ struct AttnDecodeArgs {
   float scale;
 };
 
+// decode_mk.cu: the whole batch-1 decode step as one persistent kernel.
+struct MkArgs {
+  int L, d, H, Hkv, D, F, V, max_seq, nsplit;
+  float eps, attn_scale;
+  const int8_t* wqkv;  // [L][(H + 2 Hkv) D][d]
+  const float* sqkv;
+  const int8_t* wo;  // [L][d][H D]
+  const float* so;
+  const int8_t* wg;  // [L][F][d]
+  const float* sg;
+  const int8_t* wu;
+  const float* su;
+  const int8_t* wd;  // [L][d][F]
+  const float* sd;
+  const float* attn_norm;  // [L][d]
+  const float* mlp_norm;
+  const float* final_norm;
+  const float* embed;    // [V][d]
+  const float* lm_head;  // [V][d]
+  const float* cos_t;
+  const float* sin_t;
+  float* kc;  // [L][Hkv][max_seq][D]
+  float* vc;
+  float* h;        // [d]
+  float* q;        // [H D]
+  float* partial;  // [H][nsplit][D + 2]
+  float* act;      // [F]
+  float* logits;   // [V]
+  unsigned long long* keys;
+  int64_t* tokens;
+  int64_t* history;
+  int64_t* step;
+  int64_t* pos;
+  int64_t hist_cap;
+  unsigned int* bar_counter;  // grid-barrier arrivals (zeroed by the launch)
+  int* err;                   // bounded waits that expired
+  int kmax_bytes, xbuf_floats;  // filled by megakernel_launch
+  size_t merge_bytes;
+};
+bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch);
+tb_status_t megakernel_launch(MkArgs a, cudaStream_t st);
+
 // gemv.cu
 bool gemv_fast_ok(const float* x, const int8_t* q, int64_t K);
 tb_status_t gemv_plain(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
