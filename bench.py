@@ -200,6 +200,31 @@ def fill_on_host(m, po):
     del np
 
 
+PHASE_NAMES = ["qkv", "attention", "o", "gateup", "down"]
+
+
+def summarize_phases(us):
+    """Per-token microseconds of the persistent decode kernel by phase: the
+    trace alternates work and barrier-wait intervals (CTA 0's view)."""
+    if us is None or len(us) < 4:
+        return None
+    L = CFG["layers"]
+    out = {"embed": float(us[0]), "barrier_wait": 0.0}
+    for name in PHASE_NAMES:
+        out[name] = 0.0
+    out["barrier_wait"] += float(us[1])
+    for l in range(L):
+        for k, name in enumerate(PHASE_NAMES):
+            i = 2 + 10 * l + 2 * k
+            out[name] += float(us[i])
+            out["barrier_wait"] += float(us[i + 1])
+    i = 2 + 10 * L
+    out["lm_head"] = float(us[i])
+    out["barrier_wait"] += float(us[i + 1])
+    out["total"] = float(sum(us))
+    return {k: round(v, 1) for k, v in out.items()}
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -349,6 +374,7 @@ def run_ours(args):
                "sample": f"{n} greedy decode tokens at positions 512.. of the same 7B workload, oracle restatement "
                          f"of tendo's CPU path on {threads} host threads (weights copied from the device)"}
 
+    phases = summarize_phases(qm.phase_times())
     launches = qm.launches_per_step * NEW * args.steps
     if rank == 0:
         line = {
@@ -359,7 +385,7 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: 6.5 GB int8 weights + 0.52 GB fp32 lm_head stream per token"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clk, "kernels": kern, "first_tokens": toks[:8].tolist(),
+            "clocks": clk, "kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
         }
         print(json.dumps(line), flush=True)
     qm.close()

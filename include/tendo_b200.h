@@ -279,6 +279,12 @@ TB_API tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer);
  * weights launched from one CUDA graph (no host launch cost in the time),
  * timed with CUDA events on the engine stream; *us_per_launch = average. */
 TB_API tb_status_t tb_model_time_kernel(tb_model* m, int kind, int reps, float* us_per_launch);
+/* Phase timeline of the last persistent decode step (batch-1 engines): us[i]
+ * = time between consecutive stamps taken by CTA 0 at the start and at every
+ * grid barrier's arrival and departure (alternating work / barrier wait:
+ * embed, then per layer qkv, attention, o, gate/up, down, then lm_head).
+ * TB_ERROR_NOT_SUPPORTED when the engine decodes with separate kernels. */
+TB_API tb_status_t tb_model_phase_times(tb_model* m, double* us, int max_entries, int* n_out);
 /* Kernel launches one decode step issues. */
 TB_API int64_t tb_model_launches_per_step(const tb_model* m);
 

@@ -83,6 +83,7 @@ SIGNATURES = [
     ("tb_model_sync", _st, [_vp]),
     ("tb_model_stream", _vp, [_vp]),
     ("tb_model_launches_per_step", _i64, [_vp]),
+    ("tb_model_phase_times", _st, [_vp, _vp, ctypes.c_int, _vp]),
 ]
 
 
@@ -505,6 +506,18 @@ class QuantizedModel:
     @property
     def stream_handle(self) -> int:
         return lib.tb_model_stream(self.h) or 0
+
+    def phase_times(self):
+        """Microseconds between the phase stamps of the last persistent decode step."""
+        import numpy as np
+
+        buf = np.zeros(4096, np.float64)
+        n = ctypes.c_int()
+        st = lib.tb_model_phase_times(self.h, buf.ctypes.data, buf.size, ctypes.byref(n))
+        if st == TB_ERROR_NOT_SUPPORTED:
+            return None
+        check(st)
+        return buf[: n.value].copy()
 
     @property
     def launches_per_step(self) -> int:

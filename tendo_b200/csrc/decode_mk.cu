@@ -117,8 +117,25 @@ struct Pipe {
   int u;  // next unit
 };
 
-__device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& target, int* err) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Optional phase trace (CTA 0): arrival and departure time of every barrier.
+struct Trace {
+  uint64_t* buf;
+  int n;
+  __device__ __forceinline__ void stamp() {
+    if (buf && blockIdx.x == 0 && threadIdx.x == 0) buf[n] = global_ns();
+    n++;
+  }
+};
+
+__device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& target, int* err, Trace& tr) {
   named_sync(kMkConsumers);
+  tr.stamp();
   target += gridDim.x;
   if (threadIdx.x == 0) {
     __threadfence();
@@ -136,6 +153,7 @@ __device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& t
     __threadfence();
   }
   named_sync(kMkConsumers);
+  tr.stamp();
 }
 
 // x (global, optionally RMSNorm(x) * w, or shared) -> three int8 digit rows.
@@ -445,6 +463,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
 
   // consumers
   unsigned int target = 0;
+  Trace tr{a.trace, 0};
+  tr.stamp();
   Pipe pp{stages, full, empty, a.err, 0};
   const int64_t pos = *a.pos;
   const int64_t sk = pos + 1;
@@ -454,7 +474,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   // embedding (cpu/backend.go:1289-1339): h = embed[token]
   for (int i = blockIdx.x * kMkConsumers + threadIdx.x; i < a.d; i += gridDim.x * kMkConsumers)
     a.h[i] = a.embed[(size_t)token * a.d + i];
-  grid_sync(a.bar_counter, target, a.err);
+  grid_sync(a.bar_counter, target, a.err, tr);
 
   int buf = 0;
   for (int l = 0; l < a.L; l++) {
@@ -501,7 +521,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
         }
       }
     }
-    grid_sync(a.bar_counter, target, a.err);
+    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- split-K attention over the cache ----
     {
       const int units = a.Hkv * a.nsplit;
@@ -520,7 +540,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
         }
       }
     }
-    grid_sync(a.bar_counter, target, a.err);
+    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- combine + O projection + residual ----
     {
       combine_heads(a, xbuf);
@@ -543,7 +563,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
         if (reduce_tile(y, d, red, buf, it, sc) && lane < 8) a.h[r] = hr + y * cs;
       }
     }
-    grid_sync(a.bar_counter, target, a.err);
+    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- RMSNorm + gate/up + SwiGLU ----
     {
       const Stream s = stream_of(a, 4 * l + 2);
@@ -570,7 +590,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
         }
       }
     }
-    grid_sync(a.bar_counter, target, a.err);
+    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- down projection + residual ----
     {
       const Stream s = stream_of(a, 4 * l + 3);
@@ -592,7 +612,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
         if (reduce_tile(y, d, red, buf, it, sc) && lane < 8) a.h[r] = hr + y * cs;
       }
     }
-    grid_sync(a.bar_counter, target, a.err);
+    grid_sync(a.bar_counter, target, a.err, tr);
   }
 
   // ---- final RMSNorm + fp32 lm_head + greedy argmax ----
@@ -644,7 +664,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     }
     if (lane == 0 && best) atomicMax(a.keys, best);
   }
-  grid_sync(a.bar_counter, target, a.err);
+  grid_sync(a.bar_counter, target, a.err, tr);
   // ---- token, history and position (models/sampling.go:73-83) ----
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     const unsigned long long k = atomicAdd(a.keys, 0ull);

@@ -51,6 +51,8 @@ struct tb_model {
   int mk_nsplit = 1;
   unsigned int* bar_counter = nullptr;
   int* err_word = nullptr;
+  uint64_t* trace = nullptr;  // [2 + 2 * (1 + 5 L + 1)] phase stamps of the last decode step
+  int trace_n = 0;
   cudaGraphExec_t graph = nullptr;
   std::vector<void*> allocs;
 };
@@ -379,6 +381,7 @@ tb::MkArgs mk_args(tb_model* m) {
   a.hist_cap = m->hist_cap;
   a.bar_counter = m->bar_counter;
   a.err = m->err_word;
+  a.trace = m->trace;
   return a;
 }
 
@@ -493,6 +496,8 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   A(dalloc(m, &m->step, 1));
   A(dalloc(m, &m->bad, 1));
   A(dalloc(m, &m->bar_counter, 1));
+  m->trace_n = 1 + 2 * (1 + 5 * (int)m->L + 1);
+  A(dalloc(m, &m->trace, (size_t)m->trace_n));
   A(dalloc(m, &m->err_word, 1));
   if (s == TB_SUCCESS) {
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
@@ -660,6 +665,20 @@ extern "C" tb_status_t tb_model_time_kernel(tb_model* m, int kind, int reps, flo
   cudaGraphExecDestroy(ge);
   if (e != cudaSuccess) return tb::cuda_fail(e, "tb_model_time_kernel");
   *us_per_launch = ms * 1000.0f / (float)launches;
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_phase_times(tb_model* m, double* us, int max_entries, int* n_out) {
+  TB_REQUIRE(m && us && n_out && max_entries >= 0);
+  DeviceGuard guard(m->device);
+  *n_out = 0;
+  if (!m->mk) return TB_ERROR_NOT_SUPPORTED;
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  std::vector<uint64_t> t((size_t)m->trace_n);
+  TB_CUDA(cudaMemcpy(t.data(), m->trace, sizeof(uint64_t) * t.size(), cudaMemcpyDeviceToHost));
+  int n = 0;
+  for (int i = 1; i < m->trace_n && n < max_entries; i++, n++) us[n] = (double)(t[i] - t[i - 1]) * 1e-3;
+  *n_out = n;
   return TB_SUCCESS;
 }
 

@@ -94,6 +94,7 @@ struct MkArgs {
   int64_t hist_cap;
   unsigned int* bar_counter;  // grid-barrier arrivals (zeroed by the launch)
   int* err;                   // bounded waits that expired
+  uint64_t* trace;            // optional: CTA 0 barrier arrival/departure times (ns)
   int kmax_bytes, xbuf_floats;  // filled by megakernel_launch
   size_t merge_bytes;
 };
