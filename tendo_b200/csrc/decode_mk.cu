@@ -14,7 +14,10 @@
 //   final RMSNorm + lm_head + argmax | token, position, history update.
 // Int8 projections use the integer tensor cores: the raw weight bytes are
 // the B operand, the activation row is three int8 digit rows
-// (x / s = d0 + d1 / 128 + d2 / 128^2), accumulation is exact in s32.
+// (x / s = d0 + d1 / 128 + d2 / 128^2), accumulation is exact in s32.  A
+// projection phase keeps every tile's per-warp partial sums in shared memory
+// and runs all of its epilogues after one barrier at the end, so the tile
+// loop itself never synchronises the warps.
 // Every wait (mbarrier or grid barrier) is bounded and counts a timeout in
 // an error word instead of hanging.
 #include <math.h>
@@ -32,19 +35,27 @@ constexpr int kMkThreads = kMkConsumers + 32;
 constexpr int kMkStages = 5;
 constexpr int kMkChunkMax = 4096;
 constexpr int kMkStageBytes = 8 * (kMkChunkMax + 64);
+constexpr int kMkXRegs = 12;  // float4 of x per consumer thread: K <= 12288
+constexpr int kMkPart = kMkWarps * 24;  // ints of partial sums per tile
 
 struct MkLayout {
   size_t stage_off, dig_off, xbuf_off, red_off, bar_off, total;
   int RSX;
-  __host__ __device__ void init(int kmax_bytes, int xbuf_floats, size_t merge_bytes) {
+  // xbuf (fp32 activations, O input and lm_head input) and the per-tile
+  // partial sums share a region: the O phase is done with xbuf once its
+  // digits are staged, and the lm_head phase keeps no partials.
+  __host__ __device__ void init(int kmax_bytes, int xbuf_floats, size_t merge_bytes, int tiles_max) {
     RSX = bank_stride(kmax_bytes);
     stage_off = 0;
     dig_off = (size_t)kMkStages * kMkStageBytes;
     size_t dig_bytes = (size_t)3 * RSX;
     if (dig_bytes < merge_bytes) dig_bytes = merge_bytes;  // the attention merge reuses this region
     xbuf_off = (dig_off + dig_bytes + 127) & ~(size_t)127;
-    red_off = xbuf_off + (size_t)xbuf_floats * sizeof(float);
-    bar_off = (red_off + (size_t)2 * kMkWarps * 24 * sizeof(int) + 64 * sizeof(float) + 15) & ~(size_t)15;
+    size_t xb = (size_t)xbuf_floats * sizeof(float);
+    const size_t pb = (size_t)tiles_max * kMkPart * sizeof(int);
+    if (xb < pb) xb = pb;
+    red_off = (xbuf_off + xb + 15) & ~(size_t)15;
+    bar_off = (red_off + 64 * sizeof(float) + 15) & ~(size_t)15;
     total = bar_off + (size_t)2 * kMkStages * sizeof(uint64_t);
   }
 };
@@ -148,7 +159,7 @@ __device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& t
         atomicAdd(err, 1);
         break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
     }
     __threadfence();
   }
@@ -156,18 +167,30 @@ __device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& t
   tr.stamp();
 }
 
-// x (global, optionally RMSNorm(x) * w, or shared) -> three int8 digit rows.
-// Returns the row scale s (x = s * (d0 + d1/128 + d2/128^2)).
+// x (global, optionally RMSNorm(x) * w, or shared) -> three int8 digit rows,
+// one pass: each thread keeps its float4s in registers between the
+// reduction and the digit step.  Returns the row scale s (x = s * (d0 + d1 /
+// 128 + d2 / 128^2)).
 __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_smem, int K, const float* norm_w,
                               float eps, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = K >> 2;
+  float4 xv[kMkXRegs], wv[kMkXRegs];
+#pragma unroll
+  for (int i = 0; i < kMkXRegs; i++) {
+    const int v = threadIdx.x + i * kMkConsumers;
+    xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (v < nv) {
+      xv[i] = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
+      if (norm_w) wv[i] = reinterpret_cast<const float4*>(norm_w)[v];
+    }
+  }
   float ss = 0.f, mx = 0.f;
-  for (int v = threadIdx.x; v < nv; v += kMkConsumers) {
-    const float4 t = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
+#pragma unroll
+  for (int i = 0; i < kMkXRegs; i++) {
+    const float4 t = xv[i], w4 = wv[i];
     ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
-    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (norm_w) w4 = reinterpret_cast<const float4*>(norm_w)[v];
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w4.x), fabsf(t.y * w4.y)), fmaxf(fabsf(t.z * w4.z), fabsf(t.w * w4.w))));
   }
   ss = warp_sum(ss);
@@ -187,10 +210,13 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
   if (norm_w) a = a / rms * 1.0001f;
   const float sc = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
   const float inv = 1.0f / sc;
-  for (int v = threadIdx.x; v < nv; v += kMkConsumers) {
-    float4 t = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
+#pragma unroll
+  for (int i = 0; i < kMkXRegs; i++) {
+    const int v = threadIdx.x + i * kMkConsumers;
+    if (v >= nv) continue;
+    float4 t = xv[i];
     if (norm_w) {
-      const float4 w4 = reinterpret_cast<const float4*>(norm_w)[v];
+      const float4 w4 = wv[i];
       t.x = __fmul_rn(__fdiv_rn(t.x, rms), w4.x);
       t.y = __fmul_rn(__fdiv_rn(t.y, rms), w4.y);
       t.z = __fmul_rn(__fdiv_rn(t.z, rms), w4.z);
@@ -199,15 +225,15 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
     const float vals[4] = {t.x, t.y, t.z, t.w};
     uint32_t p0 = 0, p1 = 0, p2 = 0;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float uu = fminf(fmaxf(vals[i] * inv, -127.0f), 127.0f);
+    for (int j = 0; j < 4; j++) {
+      const float uu = fminf(fmaxf(vals[j] * inv, -127.0f), 127.0f);
       const float d0 = rintf(uu);
       const float r1 = (uu - d0) * 128.0f;
       const float d1 = rintf(r1);
       const float d2 = rintf((r1 - d1) * 128.0f);
-      p0 |= ((uint32_t)(int)d0 & 0xffu) << (8 * i);
-      p1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * i);
-      p2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * i);
+      p0 |= ((uint32_t)(int)d0 & 0xffu) << (8 * j);
+      p1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
+      p2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
     }
     reinterpret_cast<uint32_t*>(dig)[v] = p0;
     reinterpret_cast<uint32_t*>(dig + RSX)[v] = p1;
@@ -217,12 +243,12 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
   return sc;
 }
 
-// One int8 tile through the pipe: per-warp partial sums of digit rows 0..2
-// (lanes g < 3 hold row g, columns 2t and 2t + 1).
-__device__ __forceinline__ void int8_tile(int (&d)[4], Pipe& pp, const int8_t* dig, int RSX, int Kc, int nch) {
+// One int8 tile through the pipe; this warp's partial sums of digit rows 0..2
+// go to part[warp * 24 + row * 8 + column] (lanes g < 3 hold row g).
+__device__ __forceinline__ void int8_tile(int* part, Pipe& pp, const int8_t* dig, int RSX, int Kc, int nch) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int RS = bank_stride(Kc), kbc = Kc / 64;
-  d[0] = d[1] = d[2] = d[3] = 0;
+  int d[4] = {0, 0, 0, 0};
   for (int ch = 0; ch < nch; ch++, pp.u++) {
     const int st = pp.u % kMkStages, use = pp.u / kMkStages;
     mbarrier_wait(&pp.full[st], (uint32_t)(use & 1), pp.err);
@@ -238,32 +264,25 @@ __device__ __forceinline__ void int8_tile(int (&d)[4], Pipe& pp, const int8_t* d
     }
     mbarrier_arrive(&pp.empty[st]);
   }
+  if (g < 3) {
+    part[warp * 24 + g * 8 + 2 * t] = d[0];
+    part[warp * 24 + g * 8 + 2 * t + 1] = d[1];
+  }
 }
 
-// Cross-warp sum of a tile's partials; lanes n < 8 of the returning warp get
-// y[n] = s * (D0 + D1/128 + D2/128^2).  Called by all consumers.
-__device__ __forceinline__ bool reduce_tile(float& y, const int (&d)[4], int* red, int& buf, int it, float sc) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  int* rb = red + buf * (kMkWarps * 24);
-  if (g < 3) {
-    rb[warp * 24 + g * 8 + 2 * t] = d[0];
-    rb[warp * 24 + g * 8 + 2 * t + 1] = d[1];
-  }
-  named_sync(kMkConsumers);
-  buf ^= 1;
-  const bool mine = warp == (it % kMkWarps);  // the epilogue rotates over the warps
-  y = 0.f;
-  if (mine && lane < 8) {
-    int s0 = 0, s1 = 0, s2 = 0;
+// After the phase barrier: y of column `lane` (< 8) of tile `it`.
+__device__ __forceinline__ float tile_value(const int* part_all, int it, float sc) {
+  const int lane = threadIdx.x & 31;
+  if (lane >= 8) return 0.f;
+  const int* p = part_all + it * kMkPart;
+  int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
-    for (int w = 0; w < kMkWarps; w++) {
-      s0 += rb[w * 24 + lane];
-      s1 += rb[w * 24 + 8 + lane];
-      s2 += rb[w * 24 + 16 + lane];
-    }
-    y = sc * ((float)s0 + (float)s1 * (1.0f / 128.0f) + (float)s2 * (1.0f / 16384.0f));
+  for (int w = 0; w < kMkWarps; w++) {
+    s0 += p[w * 24 + lane];
+    s1 += p[w * 24 + 8 + lane];
+    s2 += p[w * 24 + 16 + lane];
   }
-  return mine;
+  return sc * ((float)s0 + (float)s1 * (1.0f / 128.0f) + (float)s2 * (1.0f / 16384.0f));
 }
 
 template <int VEC, int G>
@@ -373,7 +392,7 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
         O = fmaf(mw[e], c, O);
       }
     }
-    float* part = a.partial + ((size_t)(kvh * G + gi) * a.nsplit + split) * (D + 2);
+    float* part = a.partial + ((size_t)(kvh * G + gi) * a.nsplit + split) * (D + 4);
     part[e] = O;
     if (e == 0) {
       part[D] = m;
@@ -384,26 +403,37 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
 }
 
 // Combine the split partials of every head into xbuf[H * D] (shared memory).
+// Each warp takes heads warp, warp + 8, ...; lane s < nsplit loads split s's
+// (m, l) so the maximum and the weighted sum are warp reductions, then every
+// lane sums its D / 32 elements over the splits.
 __device__ void combine_heads(const MkArgs& a, float* xbuf) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int D = a.D;
+  const int D = a.D, vec = D / 32;
   for (int h = warp; h < a.H; h += kMkWarps) {
-    const float* p = a.partial + (size_t)h * a.nsplit * (D + 2);
-    float m = -INFINITY;
-    for (int s = 0; s < a.nsplit; s++) m = fmaxf(m, ldcg(p + (size_t)s * (D + 2) + D));
-    float L = 0.f;
+    const float* p = a.partial + (size_t)h * a.nsplit * (D + 4);
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < a.nsplit) {
+      ms = ldcg(p + (size_t)lane * (D + 4) + D);
+      ls = ldcg(p + (size_t)lane * (D + 4) + D + 1);
+    }
+    const float m = warp_max(ms);
+    const float c = ms == -INFINITY ? 0.f : expf(ms - m);
+    const float L = warp_sum(ls * c);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int s = 0; s < a.nsplit; s++) {
-      const float ms = ldcg(p + (size_t)s * (D + 2) + D);
-      if (ms != -INFINITY) L = fmaf(ldcg(p + (size_t)s * (D + 2) + D + 1), expf(ms - m), L);
-    }
-    for (int e = lane; e < D; e += 32) {
-      float O = 0.f;
-      for (int s = 0; s < a.nsplit; s++) {
-        const float ms = ldcg(p + (size_t)s * (D + 2) + D);
-        if (ms != -INFINITY) O = fmaf(ldcg(p + (size_t)s * (D + 2) + e), expf(ms - m), O);
+      const float cs = __shfl_sync(0xffffffffu, c, s);
+      const float* ps = p + (size_t)s * (D + 4) + lane * vec;
+      if (vec == 4) {
+        const float4 o4 = ldcg4(ps);
+        acc[0] = fmaf(o4.x, cs, acc[0]);
+        acc[1] = fmaf(o4.y, cs, acc[1]);
+        acc[2] = fmaf(o4.z, cs, acc[2]);
+        acc[3] = fmaf(o4.w, cs, acc[3]);
+      } else {
+        for (int e = 0; e < vec; e++) acc[e] = fmaf(ldcg(ps + e), cs, acc[e]);
       }
-      xbuf[h * D + e] = O / L;
     }
+    for (int e = 0; e < vec; e++) xbuf[h * D + lane * vec + e] = acc[e] / L;
   }
   named_sync(kMkConsumers);
 }
@@ -417,13 +447,13 @@ __device__ __forceinline__ unsigned long long greedy_key(float v, int idx) {
 __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   MkLayout Ly;
-  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes);
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
   unsigned char* stages = smem + Ly.stage_off;
   int8_t* dig = reinterpret_cast<int8_t*>(smem + Ly.dig_off);
   float* merge = reinterpret_cast<float*>(smem + Ly.dig_off);
   float* xbuf = reinterpret_cast<float*>(smem + Ly.xbuf_off);
-  int* red = reinterpret_cast<int*>(smem + Ly.red_off);
-  float* redf = reinterpret_cast<float*>(red + 2 * kMkWarps * 24);
+  int* part = reinterpret_cast<int*>(smem + Ly.xbuf_off);  // shares the region with xbuf
+  float* redf = reinterpret_cast<float*>(smem + Ly.red_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Ly.bar_off);
   uint64_t* empty = full + kMkStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -476,47 +506,38 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     a.h[i] = a.embed[(size_t)token * a.d + i];
   grid_sync(a.bar_counter, target, a.err, tr);
 
-  int buf = 0;
   for (int l = 0; l < a.L; l++) {
     // ---- RMSNorm + Q/K/V + RoPE + KV append ----
     {
       const Stream s = stream_of(a, 4 * l + 0);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.attn_norm + (size_t)l * a.d, a.eps, redf);
+      int nt = 0;
+      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
+        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      named_sync(kMkConsumers);
       const float* sqkv = a.sqkv + (size_t)l * (a.H + 2 * a.Hkv) * a.D;
       float* kcl = a.kc + (size_t)l * a.Hkv * a.max_seq * a.D;
       float* vcl = a.vc + (size_t)l * a.Hkv * a.max_seq * a.D;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, it++) {
+      for (int it = warp; it < nt; it += kMkWarps) {
+        const int tile = blockIdx.x + it * gridDim.x;
         const int per = a.D / 8, head = tile / per, i = (tile % per) * 4 + (lane & 3);
         const int r = head * a.D + i + ((lane >> 2) & 1) * half;
-        // epilogue constants, loaded before the tile's MMA work
-        const bool pre = warp == (it % kMkWarps) && lane < 8;
-        float cs = 0.f, c = 0.f, sn = 0.f;
-        if (pre) {
-          cs = sqkv[r];
-          c = a.cos_t[pos * half + i];
-          sn = a.sin_t[pos * half + i];
-        }
-        int d[4];
-        int8_tile(d, pp, dig, Ly.RSX, Kc, nch);
-        float y;
-        if (reduce_tile(y, d, red, buf, it, sc)) {
-          const float v = y * cs;
-          const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
-          if (lane < 4) {
-            if (head < a.H + a.Hkv) {
-              const float o0 = __fsub_rn(__fmul_rn(v, c), __fmul_rn(partner, sn));
-              const float o1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(partner, c));
-              float* o = head < a.H ? a.q + (size_t)head * a.D
-                                    : kcl + ((size_t)(head - a.H) * a.max_seq + pos) * a.D;
-              o[i] = o0;
-              o[i + half] = o1;
-            } else {
-              float* o = vcl + ((size_t)(head - a.H - a.Hkv) * a.max_seq + pos) * a.D;
-              o[i] = v;
-              o[i + half] = partner;
-            }
+        const float y = tile_value(part, it, sc);
+        const float v = lane < 8 ? y * sqkv[r] : 0.f;
+        const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+        if (lane < 4) {
+          if (head < a.H + a.Hkv) {
+            const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
+            const float o0 = __fsub_rn(__fmul_rn(v, c), __fmul_rn(partner, sn));
+            const float o1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(partner, c));
+            float* o = head < a.H ? a.q + (size_t)head * a.D : kcl + ((size_t)(head - a.H) * a.max_seq + pos) * a.D;
+            o[i] = o0;
+            o[i + half] = o1;
+          } else {
+            float* o = vcl + ((size_t)(head - a.H - a.Hkv) * a.max_seq + pos) * a.D;
+            o[i] = v;
+            o[i + half] = partner;
           }
         }
       }
@@ -547,20 +568,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 1);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, xbuf, true, HD, nullptr, 0.f, redf);
+      int nt = 0;
+      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
+        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      named_sync(kMkConsumers);
       const float* so = a.so + (size_t)l * a.d;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, it++) {
-        const int r = tile * 8 + (lane & 7);
-        const bool pre = warp == (it % kMkWarps) && lane < 8;
-        float cs = 0.f, hr = 0.f;
-        if (pre) {
-          cs = so[r];
-          hr = ldcg(a.h + r);
-        }
-        int d[4];
-        int8_tile(d, pp, dig, Ly.RSX, Kc, nch);
-        float y;
-        if (reduce_tile(y, d, red, buf, it, sc) && lane < 8) a.h[r] = hr + y * cs;
+      for (int it = warp; it < nt; it += kMkWarps) {
+        const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
+        const float y = tile_value(part, it, sc);
+        if (lane < 8) a.h[r] = ldcg(a.h + r) + y * so[r];
       }
     }
     grid_sync(a.bar_counter, target, a.err, tr);
@@ -569,24 +585,20 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 2);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.mlp_norm + (size_t)l * a.d, a.eps, redf);
+      int nt = 0;
+      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
+        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      named_sync(kMkConsumers);
       const float* sg = a.sg + (size_t)l * a.F;
       const float* su = a.su + (size_t)l * a.F;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, it++) {
-        const int j = tile * 4 + (lane & 3);
-        const bool pre = warp == (it % kMkWarps) && lane < 8;
-        float cs = 0.f;
-        if (pre) cs = (lane >> 2) ? su[j] : sg[j];
-        int d[4];
-        int8_tile(d, pp, dig, Ly.RSX, Kc, nch);
-        float y;
-        if (reduce_tile(y, d, red, buf, it, sc)) {
-          const float v = y * cs;
-          const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
-          if (lane < 4) {
-            const float sig = 1.0f / (1.0f + expf(-v));
-            a.act[j] = (v * sig) * partner;
-          }
+      for (int it = warp; it < nt; it += kMkWarps) {
+        const int j = (blockIdx.x + it * gridDim.x) * 4 + (lane & 3);
+        const float y = tile_value(part, it, sc);
+        const float v = lane < 8 ? y * ((lane >> 2) ? su[j] : sg[j]) : 0.f;
+        const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
+        if (lane < 4) {
+          const float sig = 1.0f / (1.0f + expf(-v));
+          a.act[j] = (v * sig) * partner;
         }
       }
     }
@@ -596,20 +608,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 3);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.act, false, a.F, nullptr, 0.f, redf);
+      int nt = 0;
+      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
+        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      named_sync(kMkConsumers);
       const float* sd = a.sd + (size_t)l * a.d;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, it++) {
-        const int r = tile * 8 + (lane & 7);
-        const bool pre = warp == (it % kMkWarps) && lane < 8;
-        float cs = 0.f, hr = 0.f;
-        if (pre) {
-          cs = sd[r];
-          hr = ldcg(a.h + r);
-        }
-        int d[4];
-        int8_tile(d, pp, dig, Ly.RSX, Kc, nch);
-        float y;
-        if (reduce_tile(y, d, red, buf, it, sc) && lane < 8) a.h[r] = hr + y * cs;
+      for (int it = warp; it < nt; it += kMkWarps) {
+        const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
+        const float y = tile_value(part, it, sc);
+        if (lane < 8) a.h[r] = ldcg(a.h + r) + y * sd[r];
       }
     }
     grid_sync(a.bar_counter, target, a.err, tr);
@@ -678,13 +685,23 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   }
 }
 
-}  // namespace
-
-size_t megakernel_smem(const MkArgs& a) {
-  MkLayout Ly;
-  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes);
-  return Ly.total;
+int max_tiles_per_cta(const MkArgs& a, int grid) {
+  int t = (a.H + 2 * a.Hkv) * (a.D / 8);
+  if (a.d / 8 > t) t = a.d / 8;
+  if (a.F / 4 > t) t = a.F / 4;
+  return (t + grid - 1) / grid;
 }
+
+void fill_sizes(MkArgs& a, int grid) {
+  int kmax = a.d > a.H * a.D ? a.d : a.H * a.D;
+  if (a.F > kmax) kmax = a.F;
+  a.kmax_bytes = kmax;
+  a.xbuf_floats = a.H * a.D > a.d ? a.H * a.D : a.d;
+  a.merge_bytes = (size_t)kMkWarps * (a.H / a.Hkv) * (a.D + 2) * sizeof(float);
+  a.tiles_max = max_tiles_per_cta(a, grid);
+}
+
+}  // namespace
 
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch) {
   if (batch != 1) return false;
@@ -692,28 +709,34 @@ bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch)
   if (d % 8 || F % 4 || D % 8 || (D != 64 && D != 128)) return false;
   const int G = H / Hkv;
   if (H % Hkv || (G != 1 && G != 2 && G != 4 && G != 8)) return false;
-  (void)V;
   int kmax = d > H * D ? d : H * D;
   if (F > kmax) kmax = F;
-  const int xbuf = H * D > d ? H * D : d;
+  if (kmax > 4 * kMkConsumers * kMkXRegs) return false;  // digits staged from registers
+  MkArgs a{};
+  a.d = d;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.F = F;
+  a.V = V;
+  fill_sizes(a, sm_count());
   MkLayout Ly;
-  Ly.init(kmax, xbuf, (size_t)kMkWarps * G * (D + 2) * sizeof(float));
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
   return Ly.total <= 227 * 1024;
 }
 
 tb_status_t megakernel_launch(MkArgs a, cudaStream_t st) {
-  int kmax = a.d > a.H * a.D ? a.d : a.H * a.D;
-  if (a.F > kmax) kmax = a.F;
-  a.kmax_bytes = kmax;
-  a.xbuf_floats = a.H * a.D > a.d ? a.H * a.D : a.d;
-  a.merge_bytes = (size_t)kMkWarps * (a.H / a.Hkv) * (a.D + 2) * sizeof(float);
-  const size_t smem = megakernel_smem(a);
+  const int grid = sm_count();
+  fill_sizes(a, grid);
+  MkLayout Ly;
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
+  const size_t smem = Ly.total;
   cudaError_t e = cudaFuncSetAttribute(decode_megakernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_megakernel)");
   e = cudaMemsetAsync(a.bar_counter, 0, sizeof(unsigned int), st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(barrier)");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count());
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kMkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -95,7 +95,7 @@ struct MkArgs {
   unsigned int* bar_counter;  // grid-barrier arrivals (zeroed by the launch)
   int* err;                   // bounded waits that expired
   uint64_t* trace;            // optional: CTA 0 barrier arrival/departure times (ns)
-  int kmax_bytes, xbuf_floats;  // filled by megakernel_launch
+  int kmax_bytes, xbuf_floats, tiles_max;  // filled by megakernel_launch
   size_t merge_bytes;
 };
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch);
