@@ -209,18 +209,19 @@ def summarize_phases(us):
     if us is None or len(us) < 4:
         return None
     L = CFG["layers"]
-    out = {"embed": float(us[0]), "barrier_wait": 0.0}
-    for name in PHASE_NAMES:
-        out[name] = 0.0
-    out["barrier_wait"] += float(us[1])
+    # intervals per layer: qkv [stage, tiles, epilogue, wait], attention [work, wait],
+    # o [combine, stage, tiles, epilogue, wait], gate/up and down [stage, tiles, epilogue, wait]
+    names = ["qkv.stage", "qkv.tiles", "qkv.epi", "wait", "attention", "wait", "o.combine", "o.stage", "o.tiles",
+             "o.epi", "wait", "gateup.stage", "gateup.tiles", "gateup.epi", "wait", "down.stage", "down.tiles",
+             "down.epi", "wait"]
+    out = {"embed": float(us[0]), "wait": float(us[1])}
     for l in range(L):
-        for k, name in enumerate(PHASE_NAMES):
-            i = 2 + 10 * l + 2 * k
-            out[name] += float(us[i])
-            out["barrier_wait"] += float(us[i + 1])
-    i = 2 + 10 * L
-    out["lm_head"] = float(us[i])
-    out["barrier_wait"] += float(us[i + 1])
+        for k, name in enumerate(names):
+            out[name] = out.get(name, 0.0) + float(us[2 + 19 * l + k])
+    i = 2 + 19 * L
+    out["lm_head.norm"] = float(us[i])
+    out["lm_head.tiles"] = float(us[i + 1])
+    out["wait"] += float(us[i + 2])
     out["total"] = float(sum(us))
     return {k: round(v, 1) for k, v in out.items()}
 

@@ -37,6 +37,7 @@ constexpr int kMkChunkMax = 4096;
 constexpr int kMkStageBytes = 8 * (kMkChunkMax + 64);
 constexpr int kMkXRegs = 12;  // float4 of x per consumer thread: K <= 12288
 constexpr int kMkPart = kMkWarps * 24;  // ints of partial sums per tile
+constexpr int kMkMaxSplit = 8;          // attention splits per kv head
 
 struct MkLayout {
   size_t stage_off, dig_off, xbuf_off, red_off, bar_off, total;
@@ -402,38 +403,44 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
   named_sync(kMkConsumers);  // merge is reused by the next unit
 }
 
-// Combine the split partials of every head into xbuf[H * D] (shared memory).
-// Each warp takes heads warp, warp + 8, ...; lane s < nsplit loads split s's
-// (m, l) so the maximum and the weighted sum are warp reductions, then every
-// lane sums its D / 32 elements over the splits.
+// Combine the split partials of every head into xbuf[H * D] (shared memory):
+// one thread per 4 output elements, every (m, l, o) load of its splits issued
+// before any is used (one L2 round trip per element group).
 __device__ void combine_heads(const MkArgs& a, float* xbuf) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int D = a.D, vec = D / 32;
-  for (int h = warp; h < a.H; h += kMkWarps) {
+  const int D = a.D, n4 = a.H * D / 4, d4 = D / 4;
+  for (int idx = threadIdx.x; idx < n4; idx += kMkConsumers) {
+    const int h = idx / d4, e4 = idx - h * d4;
     const float* p = a.partial + (size_t)h * a.nsplit * (D + 4);
-    float ms = -INFINITY, ls = 0.f;
-    if (lane < a.nsplit) {
-      ms = ldcg(p + (size_t)lane * (D + 4) + D);
-      ls = ldcg(p + (size_t)lane * (D + 4) + D + 1);
-    }
-    const float m = warp_max(ms);
-    const float c = ms == -INFINITY ? 0.f : expf(ms - m);
-    const float L = warp_sum(ls * c);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < a.nsplit; s++) {
-      const float cs = __shfl_sync(0xffffffffu, c, s);
-      const float* ps = p + (size_t)s * (D + 4) + lane * vec;
-      if (vec == 4) {
-        const float4 o4 = ldcg4(ps);
-        acc[0] = fmaf(o4.x, cs, acc[0]);
-        acc[1] = fmaf(o4.y, cs, acc[1]);
-        acc[2] = fmaf(o4.z, cs, acc[2]);
-        acc[3] = fmaf(o4.w, cs, acc[3]);
-      } else {
-        for (int e = 0; e < vec; e++) acc[e] = fmaf(ldcg(ps + e), cs, acc[e]);
+    float ms[kMkMaxSplit], ls[kMkMaxSplit];
+    float4 os[kMkMaxSplit];
+#pragma unroll
+    for (int s = 0; s < kMkMaxSplit; s++) {
+      ms[s] = -INFINITY;
+      ls[s] = 0.f;
+      os[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s < a.nsplit) {
+        const float* ps = p + (size_t)s * (D + 4);
+        ms[s] = ldcg(ps + D);
+        ls[s] = ldcg(ps + D + 1);
+        os[s] = ldcg4(ps + 4 * e4);
       }
     }
-    for (int e = 0; e < vec; e++) xbuf[h * D + lane * vec + e] = acc[e] / L;
+    float m = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kMkMaxSplit; s++) m = fmaxf(m, ms[s]);
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMkMaxSplit; s++) {
+      const float c = ms[s] == -INFINITY ? 0.f : expf(ms[s] - m);
+      L = fmaf(ls[s], c, L);
+      O.x = fmaf(os[s].x, c, O.x);
+      O.y = fmaf(os[s].y, c, O.y);
+      O.z = fmaf(os[s].z, c, O.z);
+      O.w = fmaf(os[s].w, c, O.w);
+    }
+    const float inv = 1.0f / L;
+    reinterpret_cast<float4*>(xbuf)[idx] = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   }
   named_sync(kMkConsumers);
 }
@@ -512,10 +519,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 0);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.attn_norm + (size_t)l * a.d, a.eps, redf);
+      tr.stamp();
       int nt = 0;
       for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
         int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
       named_sync(kMkConsumers);
+      tr.stamp();
       const float* sqkv = a.sqkv + (size_t)l * (a.H + 2 * a.Hkv) * a.D;
       float* kcl = a.kc + (size_t)l * a.Hkv * a.max_seq * a.D;
       float* vcl = a.vc + (size_t)l * a.Hkv * a.max_seq * a.D;
@@ -565,13 +574,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     // ---- combine + O projection + residual ----
     {
       combine_heads(a, xbuf);
+      tr.stamp();
       const Stream s = stream_of(a, 4 * l + 1);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, xbuf, true, HD, nullptr, 0.f, redf);
+      tr.stamp();
       int nt = 0;
       for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
         int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
       named_sync(kMkConsumers);
+      tr.stamp();
       const float* so = a.so + (size_t)l * a.d;
       for (int it = warp; it < nt; it += kMkWarps) {
         const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
@@ -585,10 +597,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 2);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.mlp_norm + (size_t)l * a.d, a.eps, redf);
+      tr.stamp();
       int nt = 0;
       for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
         int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
       named_sync(kMkConsumers);
+      tr.stamp();
       const float* sg = a.sg + (size_t)l * a.F;
       const float* su = a.su + (size_t)l * a.F;
       for (int it = warp; it < nt; it += kMkWarps) {
@@ -608,10 +622,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       const Stream s = stream_of(a, 4 * l + 3);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
       const float sc = stage_digits(dig, Ly.RSX, a.act, false, a.F, nullptr, 0.f, redf);
+      tr.stamp();
       int nt = 0;
       for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
         int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
       named_sync(kMkConsumers);
+      tr.stamp();
       const float* sd = a.sd + (size_t)l * a.d;
       for (int it = warp; it < nt; it += kMkWarps) {
         const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
@@ -640,6 +656,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     for (int i = threadIdx.x; i < a.d; i += kMkConsumers)
       xbuf[i] = __fmul_rn(__fdiv_rn(ldcg(a.h + i), rms), a.final_norm[i]);
     named_sync(kMkConsumers);
+    tr.stamp();
     const Stream s = stream_of(a, 4 * a.L);
     const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc, RS = bank_stride(Kc);
     const int fpc = Kc / 4;  // floats per chunk

@@ -445,9 +445,9 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
     m->mk = !(e && e[0] == '0') &&
             tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
-    int ns = tb::sm_count() / (int)m->Hkv;  // one attention unit per SM
+    int ns = tb::sm_count() / (int)m->Hkv;  // about one attention unit per SM
     if (ns < 1) ns = 1;
-    if (ns > 8) ns = 8;
+    if (ns > 8) ns = 8;  // kMkMaxSplit
     if (ns > m->nsplit) ns = m->nsplit;
     m->mk_nsplit = ns;
   }
@@ -496,7 +496,8 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   A(dalloc(m, &m->step, 1));
   A(dalloc(m, &m->bad, 1));
   A(dalloc(m, &m->bar_counter, 1));
-  m->trace_n = 1 + 2 * (1 + 5 * (int)m->L + 1);
+  // start, embed barrier (2), per layer 19 stamps, lm_head (1 + barrier 2)
+  m->trace_n = 1 + 2 + 19 * (int)m->L + 3;
   A(dalloc(m, &m->trace, (size_t)m->trace_n));
   A(dalloc(m, &m->err_word, 1));
   if (s == TB_SUCCESS) {
