@@ -211,7 +211,7 @@ def summarize_phases(us):
     L = CFG["layers"]
     # intervals per layer: qkv [stage, tiles, epilogue, wait], attention [work, wait],
     # o [combine, stage, tiles, epilogue, wait], gate/up and down [stage, tiles, epilogue, wait]
-    names = ["qkv.stage", "qkv.tiles", "qkv.epi", "wait", "attention", "wait", "o.combine", "o.stage", "o.tiles",
+    names = ["qkv.stage", "qkv.tiles", "qkv.epi", "wait", "attention", "wait", "o.start", "o.stage", "o.tiles",
              "o.epi", "wait", "gateup.stage", "gateup.tiles", "gateup.epi", "wait", "down.stage", "down.tiles",
              "down.epi", "wait"]
     out = {"embed": float(us[0]), "wait": float(us[1])}

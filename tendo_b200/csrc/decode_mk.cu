@@ -169,29 +169,29 @@ __device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& t
 }
 
 // x (global, optionally RMSNorm(x) * w, or shared) -> three int8 digit rows,
-// one pass: each thread keeps its float4s in registers between the
-// reduction and the digit step.  Returns the row scale s (x = s * (d0 + d1 /
-// 128 + d2 / 128^2)).
-__device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_smem, int K, const float* norm_w,
-                              float eps, float* red) {
+// one pass: each thread keeps its NV float4s in registers between the
+// reduction and the digit step (NV * 4 * 256 >= K).  Returns the row scale s
+// (x = s * (d0 + d1 / 128 + d2 / 128^2)).
+template <int NV>
+__device__ float stage_digits_n(int8_t* dig, int RSX, const float* src, bool src_smem, int K, const float* norm_w,
+                                float eps, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = K >> 2;
-  float4 xv[kMkXRegs], wv[kMkXRegs];
+  float4 xv[NV];
 #pragma unroll
-  for (int i = 0; i < kMkXRegs; i++) {
+  for (int i = 0; i < NV; i++) {
     const int v = threadIdx.x + i * kMkConsumers;
     xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    wv[i] = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (v < nv) {
-      xv[i] = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
-      if (norm_w) wv[i] = reinterpret_cast<const float4*>(norm_w)[v];
-    }
+    if (v < nv) xv[i] = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
   }
   float ss = 0.f, mx = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMkXRegs; i++) {
-    const float4 t = xv[i], w4 = wv[i];
+  for (int i = 0; i < NV; i++) {
+    const int v = threadIdx.x + i * kMkConsumers;
+    const float4 t = xv[i];
     ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w && v < nv) w4 = reinterpret_cast<const float4*>(norm_w)[v];
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w4.x), fabsf(t.y * w4.y)), fmaxf(fabsf(t.z * w4.z), fabsf(t.w * w4.w))));
   }
   ss = warp_sum(ss);
@@ -212,12 +212,12 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
   const float sc = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
   const float inv = 1.0f / sc;
 #pragma unroll
-  for (int i = 0; i < kMkXRegs; i++) {
+  for (int i = 0; i < NV; i++) {
     const int v = threadIdx.x + i * kMkConsumers;
     if (v >= nv) continue;
     float4 t = xv[i];
     if (norm_w) {
-      const float4 w4 = wv[i];
+      const float4 w4 = reinterpret_cast<const float4*>(norm_w)[v];
       t.x = __fmul_rn(__fdiv_rn(t.x, rms), w4.x);
       t.y = __fmul_rn(__fdiv_rn(t.y, rms), w4.y);
       t.z = __fmul_rn(__fdiv_rn(t.z, rms), w4.z);
@@ -232,9 +232,9 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
       const float r1 = (uu - d0) * 128.0f;
       const float d1 = rintf(r1);
       const float d2 = rintf((r1 - d1) * 128.0f);
-      p0 |= ((uint32_t)(int)d0 & 0xffu) << (8 * j);
-      p1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
-      p2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
+      p0 |= ((uint32_t)__float2int_rn(d0) & 0xffu) << (8 * j);
+      p1 |= ((uint32_t)__float2int_rn(d1) & 0xffu) << (8 * j);
+      p2 |= ((uint32_t)__float2int_rn(d2) & 0xffu) << (8 * j);
     }
     reinterpret_cast<uint32_t*>(dig)[v] = p0;
     reinterpret_cast<uint32_t*>(dig + RSX)[v] = p1;
@@ -242,6 +242,12 @@ __device__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_s
   }
   named_sync(kMkConsumers);
   return sc;
+}
+
+__device__ __forceinline__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_smem, int K,
+                                              const float* norm_w, float eps, float* red) {
+  if (K <= 4 * 4 * kMkConsumers) return stage_digits_n<4>(dig, RSX, src, src_smem, K, norm_w, eps, red);
+  return stage_digits_n<kMkXRegs>(dig, RSX, src, src_smem, K, norm_w, eps, red);
 }
 
 // One int8 tile through the pipe; this warp's partial sums of digit rows 0..2
@@ -400,49 +406,48 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
       part[D + 1] = L;
     }
   }
-  named_sync(kMkConsumers);  // merge is reused by the next unit
-}
-
-// Combine the split partials of every head into xbuf[H * D] (shared memory):
-// one thread per 4 output elements, every (m, l, o) load of its splits issued
-// before any is used (one L2 round trip per element group).
-__device__ void combine_heads(const MkArgs& a, float* xbuf) {
-  const int D = a.D, n4 = a.H * D / 4, d4 = D / 4;
-  for (int idx = threadIdx.x; idx < n4; idx += kMkConsumers) {
-    const int h = idx / d4, e4 = idx - h * d4;
-    const float* p = a.partial + (size_t)h * a.nsplit * (D + 4);
-    float ms[kMkMaxSplit], ls[kMkMaxSplit];
-    float4 os[kMkMaxSplit];
-#pragma unroll
-    for (int s = 0; s < kMkMaxSplit; s++) {
-      ms[s] = -INFINITY;
-      ls[s] = 0.f;
-      os[s] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (s < a.nsplit) {
-        const float* ps = p + (size_t)s * (D + 4);
-        ms[s] = ldcg(ps + D);
-        ls[s] = ldcg(ps + D + 1);
-        os[s] = ldcg4(ps + 4 * e4);
-      }
-    }
-    float m = -INFINITY;
-#pragma unroll
-    for (int s = 0; s < kMkMaxSplit; s++) m = fmaxf(m, ms[s]);
-    float L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int s = 0; s < kMkMaxSplit; s++) {
-      const float c = ms[s] == -INFINITY ? 0.f : expf(ms[s] - m);
-      L = fmaf(ls[s], c, L);
-      O.x = fmaf(os[s].x, c, O.x);
-      O.y = fmaf(os[s].y, c, O.y);
-      O.z = fmaf(os[s].z, c, O.z);
-      O.w = fmaf(os[s].w, c, O.w);
-    }
-    const float inv = 1.0f / L;
-    reinterpret_cast<float4*>(xbuf)[idx] = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+  // the last split of this kv head to finish combines all its splits
+  __threadfence();
+  named_sync(kMkConsumers);
+  int* flag = reinterpret_cast<int*>(merge);
+  if (threadIdx.x == 0) {
+    const unsigned int ticket = atomicAdd(a.head_done + kvh, 1u);
+    flag[0] = ticket == (unsigned int)(a.nsplit - 1);
   }
   named_sync(kMkConsumers);
+  const bool last = flag[0] != 0;
+  named_sync(kMkConsumers);
+  if (last) {
+    __threadfence();
+    for (int idx = threadIdx.x; idx < G * D; idx += kMkConsumers) {
+      const int gi = idx / D, e = idx - gi * D;
+      const float* p = a.partial + (size_t)(kvh * G + gi) * a.nsplit * (D + 4);
+      float ms[kMkMaxSplit], ls[kMkMaxSplit], os[kMkMaxSplit];
+#pragma unroll
+      for (int s = 0; s < kMkMaxSplit; s++) {
+        ms[s] = -INFINITY;
+        ls[s] = os[s] = 0.f;
+        if (s < a.nsplit) {
+          ms[s] = ldcg(p + (size_t)s * (D + 4) + D);
+          ls[s] = ldcg(p + (size_t)s * (D + 4) + D + 1);
+          os[s] = ldcg(p + (size_t)s * (D + 4) + e);
+        }
+      }
+      float m = -INFINITY;
+#pragma unroll
+      for (int s = 0; s < kMkMaxSplit; s++) m = fmaxf(m, ms[s]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int s = 0; s < kMkMaxSplit; s++) {
+        const float c = ms[s] == -INFINITY ? 0.f : expf(ms[s] - m);
+        L = fmaf(ls[s], c, L);
+        O = fmaf(os[s], c, O);
+      }
+      a.attn[(size_t)(kvh * G + gi) * D + e] = O / L;
+    }
+    if (threadIdx.x == 0) a.head_done[kvh] = 0u;  // ready for the next step
+  }
+  named_sync(kMkConsumers);  // merge is reused by the next unit
 }
 
 __device__ __forceinline__ unsigned long long greedy_key(float v, int idx) {
@@ -571,13 +576,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       }
     }
     grid_sync(a.bar_counter, target, a.err, tr);
-    // ---- combine + O projection + residual ----
+    // ---- O projection + residual (the attention phase left the combined heads in a.attn) ----
     {
-      combine_heads(a, xbuf);
       tr.stamp();
       const Stream s = stream_of(a, 4 * l + 1);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
-      const float sc = stage_digits(dig, Ly.RSX, xbuf, true, HD, nullptr, 0.f, redf);
+      const float sc = stage_digits(dig, Ly.RSX, a.attn, false, HD, nullptr, 0.f, redf);
       tr.stamp();
       int nt = 0;
       for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)

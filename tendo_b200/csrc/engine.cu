@@ -50,6 +50,7 @@ struct tb_model {
   bool mk = false;      // whole decode step as one persistent kernel (batch 1)
   int mk_nsplit = 1;
   unsigned int* bar_counter = nullptr;
+  unsigned int* head_done = nullptr;
   int* err_word = nullptr;
   uint64_t* trace = nullptr;  // [2 + 2 * (1 + 5 L + 1)] phase stamps of the last decode step
   int trace_n = 0;
@@ -371,6 +372,8 @@ tb::MkArgs mk_args(tb_model* m) {
   a.h = m->h;
   a.q = m->qbuf;
   a.partial = m->partial;
+  a.attn = m->attn;
+  a.head_done = m->head_done;
   a.act = m->g;
   a.logits = m->logits;
   a.keys = m->keys;
@@ -496,6 +499,7 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   A(dalloc(m, &m->step, 1));
   A(dalloc(m, &m->bad, 1));
   A(dalloc(m, &m->bar_counter, 1));
+  A(dalloc(m, &m->head_done, (size_t)m->Hkv));
   // start, embed barrier (2), per layer 19 stamps, lm_head (1 + barrier 2)
   m->trace_n = 1 + 2 + 19 * (int)m->L + 3;
   A(dalloc(m, &m->trace, (size_t)m->trace_n));
@@ -516,6 +520,7 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
     if (e == cudaSuccess) e = cudaMemset(m->step, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->bad, 0, sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMemset(m->bar_counter, 0, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(m->head_done, 0, sizeof(unsigned int) * m->Hkv);
     if (e == cudaSuccess) e = cudaMemset(m->err_word, 0, sizeof(int));
     if (e != cudaSuccess) s = tb::cuda_fail(e, "engine init");
   }

@@ -83,7 +83,9 @@ struct MkArgs {
   float* vc;
   float* h;        // [d]
   float* q;        // [H D]
-  float* partial;  // [H][nsplit][D + 2]
+  float* partial;  // [H][nsplit][D + 4]
+  float* attn;     // [H D] combined attention output
+  unsigned int* head_done;  // [Hkv] splits finished this step (zero between steps)
   float* act;      // [F]
   float* logits;   // [V]
   unsigned long long* keys;
