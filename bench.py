@@ -309,8 +309,9 @@ def run_ours(args):
     total_tokens = world * args.steps * NEW
     value = total_tokens / (ms_max / 1000.0)
 
-    # per-kernel timing of the decode step's kernels (same stream, CUDA events),
-    # cycling over all layers so weights stream from HBM
+    # per-kernel timing of the multi-kernel decode step (the path taken when
+    # the persistent kernel does not apply: batch > 1, unsupported shapes),
+    # same stream, CUDA events, cycling over all layers so weights stream from HBM
     qm.set_position(PROMPT + NEW // 2)  # mean cache length of a step
     kern = {}
     for kind in range(6):
@@ -335,14 +336,27 @@ def run_ours(args):
     ms_per_tok = ms_max / (args.steps * NEW)
     model_bytes = statistics.mean(step_bytes(PROMPT + i) for i in range(NEW))
     model_gbs = model_bytes / (ms_per_tok / 1000.0) / 1e9
+    persistent = qm.launches_per_step == 1
+    if persistent:
+        # the whole token is one launch of the persistent decode kernel: its
+        # average launch duration is the timed region over the launches in it
+        dom = "decode_megakernel"
+        dom_gbs = model_gbs
+    else:
+        dom_gbs = kern[dom]["GB_s"]
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get(dom)
+        with open(os.path.join(ROOT, "profiles", "traffic.txt")) as f:
+            for line in f:
+                parts = line.split("#")[0].split()
+                if len(parts) == 2 and parts[0] == dom:
+                    traffic = float(parts[1])
     except (OSError, ValueError):
         traffic = None
-    roofline = {"bound": "hbm", "achieved": kern[dom]["GB_s"], "peak": hbm_peak, "unit": "GB/s",
-                "frac": kern[dom]["GB_s"] / hbm_peak, "traffic": traffic, "kernel": dom, "peak_source": peak_src,
+    roofline = {"bound": "hbm", "achieved": dom_gbs, "peak": hbm_peak, "unit": "GB/s",
+                "frac": dom_gbs / hbm_peak, "traffic": traffic, "kernel": dom, "peak_source": peak_src,
+                "bytes_per_launch": model_bytes if persistent else kern[dom]["bytes"],
+                "launch_us": ms_per_tok * 1000.0 if persistent else kern[dom]["us"],
                 "model_achieved": model_gbs, "model_frac": model_gbs / hbm_peak,
                 "model_bytes_per_token": model_bytes}
 
@@ -386,7 +400,7 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: 6.5 GB int8 weights + 0.52 GB fp32 lm_head stream per token"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clk, "kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
+            "clocks": clk, "standalone_kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
         }
         print(json.dumps(line), flush=True)
     qm.close()

@@ -1,6 +1,7 @@
 """Quantized Linear microbench: tb_dequant_matmul_i8f32 on one GPU.
 
     python -m tendo_b200.microbench [--M 1 8 32 128 2048] [--N 4096 11008] [--K 4096] [--iters 20]
+    python -m tendo_b200.microbench --decode-layers 8 [--tokens 4]
 
 W [N, K] is drawn N(0, 0.02) (seed 42) and int8-quantized per output channel
 on the device; X [M, K] is N(0, 1) (seed 42).  Enough weight copies are
@@ -8,6 +9,12 @@ rotated that every launch streams its weights from HBM, not L2 (126 MB).
 Prints one JSON line per (M, N): microseconds per launch (CUDA events),
 achieved GB/s over the algorithmic bytes N*K + 4N + 4MK + 4MN (the M <= 32
 regime is HBM-bound) and TFLOP/s over 2MNK.
+
+--decode-layers L runs the batch-1 decode step of a Llama-7B-width model cut
+to L layers (d 4096, 32x128 heads, F 11008, vocab 32000, KV capacity 1024):
+a 512-token prompt, then `--tokens` decode tokens, one persistent-kernel
+launch each.  It is the small case for profiling that kernel (about 2.5 GB
+on the device at L = 8).
 """
 from __future__ import annotations
 
@@ -72,15 +79,36 @@ def run(Ms, Ns, K, iters, mode):
     return rows
 
 
+def decode_small(layers, tokens):
+    cfg = dict(vocab=32000, dim=4096, layers=layers, heads=32, kv_heads=32, hidden=11008, max_seq=1024,
+               rope_base=10000.0, eps=1e-6)
+    qm = tb.QuantizedModel(cfg, batch=1, device=0)
+    qm.init_synthetic(0)
+    prompt = tb.synth_tokens(512, cfg["vocab"], 0)
+    _, first = qm.forward(prompt[None, :], want_logits=False)
+    qm.set_position(512)
+    qm.decode(tokens, start_tokens=first)
+    qm.sync()
+    out = {"layers": layers, "tokens": tokens, "launches_per_token": qm.launches_per_step,
+           "first_tokens": qm.tokens(tokens + 1)[:, 0][:4].tolist()}
+    print(json.dumps(out), flush=True)
+    qm.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--decode-layers", type=int, default=0)
+    ap.add_argument("--tokens", type=int, default=4)
     ap.add_argument("--M", type=int, nargs="+", default=[1, 8, 32, 128, 2048])
     ap.add_argument("--N", type=int, nargs="+", default=[4096, 11008])
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--mode", type=int, default=tb.TB_GEMM_BF16X2)
     a = ap.parse_args()
-    run(a.M, a.N, a.K, a.iters, a.mode)
+    if a.decode_layers > 0:
+        decode_small(a.decode_layers, a.tokens)
+    else:
+        run(a.M, a.N, a.K, a.iters, a.mode)
 
 
 if __name__ == "__main__":
