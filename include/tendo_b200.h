@@ -81,18 +81,23 @@ TB_API tb_status_t tb_dequantize_i8_f32(float* w, const int8_t* q, const float* 
  * channel) and popcornDequantizeMatmulGrouped_i8f32 (cuda/popcorn.go:1353-1363,
  * group_size > 0), reached from cuda.Backend.DequantizeMatmul
  * (cuda/backend.go:676-721).  M <= 32 runs the fused-dequant int8 GEMV;
- * larger M runs the tensor-core GEMM (int8 tiles widened to bf16 in shared
- * memory, fp32 accumulation), x carried as a bf16 hi + lo pair so the result
- * stays within 1e-3 of the fp32 path. */
+ * larger M runs the tcgen05 tensor-core GEMM: each row of x is split into
+ * three int8 digit rows (x = s (d0 + d1/128 + d2/128^2), s = max|x|/127) and
+ * every digit row times the raw int8 weights is summed exactly in s32
+ * (tcgen05.mma kind::i8), so the result is within 2^-21 s sum|w| of the
+ * fp32 product.  Per-group scales (group_size > 0) run the CUDA-core GEMM.
+ * The digit rows need scratch: this entry point keeps one library-owned
+ * buffer per device, allocated on first use and grown on demand (calls that
+ * overlap in time on one device must use tb_dequant_matmul_i8f32_ws). */
 TB_API tb_status_t tb_dequant_matmul_i8f32(float* out, const float* x, const int8_t* q, const float* scale,
                                     int64_t M, int64_t N, int64_t K, int64_t group_size,
                                     tb_stream_t stream);
 
-/* Precision modes of the tensor-core GEMM (M > 32). */
+/* GEMM modes for M > 32. */
 typedef enum {
-  TB_GEMM_BF16X2 = 0, /* x = hi + lo bf16 pair, two MMAs: ~fp32 accuracy (default) */
-  TB_GEMM_BF16 = 1,   /* x rounded once to bf16, one MMA: 1e-2 class accuracy */
-  TB_GEMM_SIMT = 2    /* fp32 CUDA-core tiles (no tensor cores) */
+  TB_GEMM_I8X3 = 0, /* tcgen05 kind::i8, three digit rows of x: within 2^-21 s sum|w| (default) */
+  TB_GEMM_I8X2 = 1, /* tcgen05 kind::i8, two digit rows: within 2^-14 s sum|w|, 1.5x fewer MMAs */
+  TB_GEMM_SIMT = 2  /* fp32 CUDA-core tiles (no tensor cores) */
 } tb_gemm_mode_t;
 
 /* tb_dequant_matmul_i8f32 with the GEMM mode chosen by the caller (used for
@@ -100,6 +105,19 @@ typedef enum {
 TB_API tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, const int8_t* q, const float* scale,
                                          int64_t M, int64_t N, int64_t K, int64_t group_size,
                                          tb_gemm_mode_t mode, tb_stream_t stream);
+
+/* Scratch bytes tb_dequant_matmul_i8f32_ws needs for these sizes and mode
+ * (0 when no scratch is used: M <= 32, per-group scales, TB_GEMM_SIMT). */
+TB_API size_t tb_dequant_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                               tb_gemm_mode_t mode);
+
+/* tb_dequant_matmul_i8f32_mode with caller-owned scratch (the Go backend's
+ * pool): allocates nothing.  workspace_bytes below the size above returns
+ * TB_ERROR_INVALID_ARGUMENT. */
+TB_API tb_status_t tb_dequant_matmul_i8f32_ws(float* out, const float* x, const int8_t* q, const float* scale,
+                                              int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                              tb_gemm_mode_t mode, void* workspace, size_t workspace_bytes,
+                                              tb_stream_t stream);
 
 /* out[M, N] = a[M, K] @ b[N, K]^T in fp32: the fp32 lm_head projection
  * (models/llama/quantized.go:164-172, cuBLAS SGEMM in cuda/ops.go:182-330). */

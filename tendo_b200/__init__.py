@@ -25,8 +25,8 @@ TB_ERROR_OUT_OF_MEMORY = 4
 TB_ERROR_TIMEOUT = 5
 TB_ERROR_INJECTED = 6
 
-TB_GEMM_BF16X2 = 0
-TB_GEMM_BF16 = 1
+TB_GEMM_I8X3 = 0
+TB_GEMM_I8X2 = 1
 TB_GEMM_SIMT = 2
 
 _vp = ctypes.c_void_p
@@ -45,6 +45,8 @@ SIGNATURES = [
     ("tb_dequantize_i8_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("tb_dequant_matmul_i8f32", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     ("tb_dequant_matmul_i8f32_mode", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _st, _vp]),
+    ("tb_dequant_matmul_workspace_size", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _st]),
+    ("tb_dequant_matmul_i8f32_ws", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _st, _vp, ctypes.c_size_t, _vp]),
     ("tb_matmul_nt_f32", _st, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("tb_rmsnorm_f32", _st, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     ("tb_add_rmsnorm_f32", _st, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
@@ -207,7 +209,7 @@ class Backend:
         return q
 
     # nn.QuantizedLinearBackend.DequantizeMatmul (nn/quantize.go:251-258; cuda/backend.go:676-721)
-    def DequantizeMatmul(self, x, qweight, scale, group_size: int = 0, mode: int = TB_GEMM_BF16X2):
+    def DequantizeMatmul(self, x, qweight, scale, group_size: int = 0, mode: int = TB_GEMM_I8X3):
         torch = _torch()
         _need_cuda(x, qweight, scale)
         K = x.shape[-1]
@@ -218,8 +220,11 @@ class Backend:
             qweight = self.PackQ(qweight.contiguous())
         M = x.numel() // K if K else 0
         out = torch.empty((*x.shape[:-1], N), dtype=torch.float32, device=x.device)
-        check(lib.tb_dequant_matmul_i8f32_mode(_ptr(out), _ptr(x), _ptr(qweight), _ptr(scale), M, N, K, group_size,
-                                               mode, _stream()))
+        # scratch of the tensor-core path from the caller's allocator (tendo's pool)
+        ws_bytes = int(lib.tb_dequant_matmul_workspace_size(M, N, K, group_size, mode))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+        check(lib.tb_dequant_matmul_i8f32_ws(_ptr(out), _ptr(x), _ptr(qweight), _ptr(scale), M, N, K, group_size,
+                                             mode, _ptr(ws) if ws is not None else None, ws_bytes, _stream()))
         return out
 
     def MatMulNT(self, a, b):

@@ -73,29 +73,108 @@ extern "C" const char* tb_get_last_cuda_error_string(void) { return tb::g_last_c
 
 extern "C" int tb_version(void) { return 100; }
 
-extern "C" tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, const int8_t* q, const float* scale,
-                                                    int64_t M, int64_t N, int64_t K, int64_t group_size,
-                                                    tb_gemm_mode_t mode, tb_stream_t stream) {
-  TB_INJECT("tb_dequant_matmul_i8f32");
-  TB_REQUIRE(M >= 0 && N >= 0 && K > 0 && group_size >= 0);
-  TB_REQUIRE(group_size == 0 || K % group_size == 0);
-  TB_REQUIRE(M <= 0x7fffffff && N <= 0x7fffffff && K <= 0x7fffffff);
-  TB_REQUIRE(mode == TB_GEMM_BF16X2 || mode == TB_GEMM_BF16 || mode == TB_GEMM_SIMT);
-  if (M == 0 || N == 0) return TB_SUCCESS;
-  TB_REQUIRE(out && x && q && scale);
-  cudaStream_t st = (cudaStream_t)stream;
+namespace {
+
+int gemm_planes(tb_gemm_mode_t mode) { return mode == TB_GEMM_I8X2 ? 2 : 3; }
+
+size_t dqmm_workspace(int64_t M, int64_t K, int64_t group_size, tb_gemm_mode_t mode) {
+  if (M <= 32 || group_size > 0 || mode == TB_GEMM_SIMT) return 0;
+  return tb::gemm_tc_workspace(M, K, gemm_planes(mode));
+}
+
+// One library-owned scratch buffer per device for the entry points without a
+// workspace argument: allocated on first use, grown (after a device
+// synchronisation) when a larger call arrives.
+std::mutex g_arena_mu;
+struct ArenaSlot {
+  void* p = nullptr;
+  size_t n = 0;
+};
+ArenaSlot g_arena[64];
+
+tb_status_t arena_get(size_t bytes, void** out) {
+  int dev = 0;
+  TB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return TB_ERROR_NOT_SUPPORTED;
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  ArenaSlot& a = g_arena[dev];
+  if (a.n < bytes) {
+    if (a.p) {
+      TB_CUDA(cudaDeviceSynchronize());
+      TB_CUDA(cudaFree(a.p));
+      a.p = nullptr;
+      a.n = 0;
+    }
+    const size_t want = bytes + bytes / 4;
+    TB_CUDA(cudaMalloc(&a.p, want));
+    a.n = want;
+  }
+  *out = a.p;
+  return TB_SUCCESS;
+}
+
+tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
+                 int64_t group_size, tb_gemm_mode_t mode, void* ws, size_t ws_bytes, bool arena, cudaStream_t st) {
   if (M <= 32) {
     if (group_size == 0 && tb::gemv_fast_ok(x, q, K))
       return tb::gemv_plain(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, nullptr, 0.f, st, false);
     return tb::gemv_generic(out, x, q, scale, (int)M, (int)N, (int)K, group_size > 0 ? (int)group_size : (int)K, st);
   }
-  return tb::gemm_i8(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, (int)group_size, mode, st);
+  const size_t need = dqmm_workspace(M, K, group_size, mode);
+  if (need > 0 && tb::gemm_tc_ok(q, M, N, K) && (uintptr_t)x % 16 == 0) {
+    if (arena) {
+      TB_TRY(arena_get(need, &ws));
+    } else {
+      TB_REQUIRE(ws && ws_bytes >= need);
+    }
+    return tb::gemm_tc(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, gemm_planes(mode), ws, st);
+  }
+  if (!arena && need > 0) TB_REQUIRE(ws && ws_bytes >= need);
+  return tb::gemm_simt_i8(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, (int)group_size, st);
+}
+
+}  // namespace
+
+#define TB_DQMM_ARGS_CHECK()                                                 \
+  do {                                                                        \
+    TB_REQUIRE(M >= 0 && N >= 0 && K > 0 && group_size >= 0);                \
+    TB_REQUIRE(group_size == 0 || K % group_size == 0);                       \
+    TB_REQUIRE(M <= 0x7fffffff && N <= 0x7fffffff && K <= 0x7fffffff);        \
+    TB_REQUIRE(mode == TB_GEMM_I8X3 || mode == TB_GEMM_I8X2 || mode == TB_GEMM_SIMT); \
+  } while (0)
+
+extern "C" size_t tb_dequant_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                                   tb_gemm_mode_t mode) {
+  (void)N;
+  if (M < 0 || K <= 0 || group_size < 0) return 0;
+  return dqmm_workspace(M, K, group_size, mode);
+}
+
+extern "C" tb_status_t tb_dequant_matmul_i8f32_ws(float* out, const float* x, const int8_t* q, const float* scale,
+                                                  int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                                  tb_gemm_mode_t mode, void* workspace, size_t workspace_bytes,
+                                                  tb_stream_t stream) {
+  TB_INJECT("tb_dequant_matmul_i8f32");
+  TB_DQMM_ARGS_CHECK();
+  if (M == 0 || N == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && x && q && scale);
+  return dqmm(out, x, q, scale, M, N, K, group_size, mode, workspace, workspace_bytes, false, (cudaStream_t)stream);
+}
+
+extern "C" tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, const int8_t* q, const float* scale,
+                                                    int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                                    tb_gemm_mode_t mode, tb_stream_t stream) {
+  TB_INJECT("tb_dequant_matmul_i8f32");
+  TB_DQMM_ARGS_CHECK();
+  if (M == 0 || N == 0) return TB_SUCCESS;
+  TB_REQUIRE(out && x && q && scale);
+  return dqmm(out, x, q, scale, M, N, K, group_size, mode, nullptr, 0, true, (cudaStream_t)stream);
 }
 
 extern "C" tb_status_t tb_dequant_matmul_i8f32(float* out, const float* x, const int8_t* q, const float* scale,
                                                int64_t M, int64_t N, int64_t K, int64_t group_size,
                                                tb_stream_t stream) {
-  return tb_dequant_matmul_i8f32_mode(out, x, q, scale, M, N, K, group_size, TB_GEMM_BF16X2, stream);
+  return tb_dequant_matmul_i8f32_mode(out, x, q, scale, M, N, K, group_size, TB_GEMM_I8X3, stream);
 }
 
 extern "C" tb_status_t tb_matmul_nt_f32(float* out, const float* a, const float* b, int64_t M, int64_t N, int64_t K,

@@ -53,6 +53,8 @@ struct tb_model {
   unsigned int* head_done = nullptr;
   int* err_word = nullptr;
   uint64_t* trace = nullptr;  // [2 + 2 * (1 + 5 L + 1)] phase stamps of the last decode step
+  int8_t* tcdig = nullptr;    // digit rows of the prefill projections' activations (tcgen05 GEMM)
+  float* tcs = nullptr;       // their row scales
   int trace_n = 0;
   cudaGraphExec_t graph = nullptr;
   std::vector<void*> allocs;
@@ -61,6 +63,8 @@ struct tb_model {
 namespace {
 
 using tb::ceil_div;
+
+constexpr int kTcPlanes = 3;  // digit rows of the prefill GEMM's activations
 
 template <typename T>
 tb_status_t dalloc(tb_model* m, T** p, size_t count) {
@@ -125,6 +129,9 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
   const int64_t rows = m->B * S;
   const int64_t P = m->host_pos;
   const float scale = 1.0f / (float)sqrt((double)m->D);
+  // rows > 32: projections on the tcgen05 GEMM (digit rows of the activations)
+  const bool tc = rows > 32 && tb::gemm_tc_ok(m->wqkv, rows, m->NQKV, m->d) &&
+                  tb::gemm_tc_ok(m->wo, rows, m->d, m->H * m->D) && tb::gemm_tc_ok(m->wdown, rows, m->d, m->F);
   for (int64_t l = 0; l < m->L; l++) {
     int8_t *wq, *wo, *wg, *wu, *wd;
     float *sq, *so, *sg, *su, *sd;
@@ -136,8 +143,15 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     float* kcl = m->kc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
     float* vcl = m->vc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
     // attention block (models/llama/quantized.go:186-199)
-    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->attn_norm + l * m->d, rows, m->d, m->c.eps, st));
-    TB_TRY(tb_dequant_matmul_i8f32(m->qkv, m->xn, wq, sq, rows, m->NQKV, m->d, 0, (tb_stream_t)st));
+    if (tc) {
+      TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->h, (int)rows, (int)m->d, kTcPlanes, m->attn_norm + l * m->d,
+                                m->c.eps, st));
+      TB_TRY(tb::gemm_tc_run(m->qkv, m->tcdig, m->tcs, wq, sq, nullptr, (int)rows, (int)m->NQKV, (int)m->d, kTcPlanes,
+                             st));
+    } else {
+      TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->attn_norm + l * m->d, rows, m->d, m->c.eps, st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->qkv, m->xn, wq, sq, rows, m->NQKV, m->d, 0, (tb_stream_t)st));
+    }
     TB_TRY(tb::rope_rows(m->qkv, m->cos_t, m->sin_t, m->B, S, m->H, m->D, P, m->NQKV, st));
     TB_TRY(tb::kv_append_rope(kcl, vcl, m->qkv + m->H * m->D, m->qkv + (m->H + m->Hkv) * m->D, m->cos_t, m->sin_t,
                               m->B, m->Hkv, S, m->D, P, m->Ms, m->NQKV, st));
@@ -169,19 +183,33 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, 0, (tb_stream_t)st));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
+    } else if (tc) {
+      const int HD = (int)(m->H * m->D);
+      TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->attn, (int)rows, HD, kTcPlanes, nullptr, 0.f, st));
+      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wo, so, m->h, (int)rows, (int)m->d, HD, kTcPlanes, st));
     } else {
-      TB_TRY(tb::gemm_i8(m->h, m->attn, wo, so, m->h, (int)rows, (int)m->d, (int)(m->H * m->D), 0, TB_GEMM_BF16X2, st));
+      TB_TRY(tb::gemm_simt_i8(m->h, m->attn, wo, so, m->h, (int)rows, (int)m->d, (int)(m->H * m->D), 0, st));
     }
     // MLP block (models/llama/quantized.go:206-219, :385-417)
-    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->mlp_norm + l * m->d, rows, m->d, m->c.eps, st));
-    TB_TRY(tb_dequant_matmul_i8f32(m->g, m->xn, wg, sg, rows, m->F, m->d, 0, (tb_stream_t)st));
-    TB_TRY(tb_dequant_matmul_i8f32(m->u, m->xn, wu, su, rows, m->F, m->d, 0, (tb_stream_t)st));
+    if (tc) {
+      TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->h, (int)rows, (int)m->d, kTcPlanes, m->mlp_norm + l * m->d,
+                                m->c.eps, st));
+      TB_TRY(tb::gemm_tc_run(m->g, m->tcdig, m->tcs, wg, sg, nullptr, (int)rows, (int)m->F, (int)m->d, kTcPlanes, st));
+      TB_TRY(tb::gemm_tc_run(m->u, m->tcdig, m->tcs, wu, su, nullptr, (int)rows, (int)m->F, (int)m->d, kTcPlanes, st));
+    } else {
+      TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->mlp_norm + l * m->d, rows, m->d, m->c.eps, st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->g, m->xn, wg, sg, rows, m->F, m->d, 0, (tb_stream_t)st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->u, m->xn, wu, su, rows, m->F, m->d, 0, (tb_stream_t)st));
+    }
     TB_TRY(tb::silu_mul(m->g, m->g, m->u, rows * m->F, st));
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, 0, (tb_stream_t)st));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
+    } else if (tc) {
+      TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->g, (int)rows, (int)m->F, kTcPlanes, nullptr, 0.f, st));
+      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, kTcPlanes, st));
     } else {
-      TB_TRY(tb::gemm_i8(m->h, m->g, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, 0, TB_GEMM_BF16X2, st));
+      TB_TRY(tb::gemm_simt_i8(m->h, m->g, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, 0, st));
     }
   }
   return TB_SUCCESS;
@@ -504,6 +532,12 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   m->trace_n = 1 + 2 + 19 * (int)m->L + 3;
   A(dalloc(m, &m->trace, (size_t)m->trace_n));
   A(dalloc(m, &m->err_word, 1));
+  {
+    int64_t kmax = m->d > m->H * m->D ? m->d : m->H * m->D;
+    if (m->F > kmax) kmax = m->F;
+    A(dalloc(m, &m->tcdig, (size_t)kTcPlanes * R * kmax));
+    A(dalloc(m, &m->tcs, R));
+  }
   if (s == TB_SUCCESS) {
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) s = tb::cuda_fail(e, "cudaStreamCreate");

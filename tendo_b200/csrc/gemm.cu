@@ -1,4 +1,6 @@
-// gemm.cu — prefill-regime (M > 32) dequant GEMM, CUDA-core fp32 tiles.
+// gemm.cu — CUDA-core fp32 GEMM tiles: the quantized Linear for per-group
+// scales and shapes the tcgen05 path (gemm_tc.cu) does not take, and the fp32
+// lm_head of the multi-row paths.
 //
 // out[M, N] = x[M, K] @ W^T (+ resid) with W = q * scale dequantized to fp32
 // while the tile is staged in shared memory (the same rounding as
@@ -80,9 +82,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_simt_kernel(float* out, con
 
 }  // namespace
 
-tb_status_t gemm_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
-                    int N, int K, int group, tb_gemm_mode_t mode, cudaStream_t st) {
-  (void)mode;  // the tensor-core modes fall back to the CUDA-core tiles in this build
+tb_status_t gemm_simt_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
+                         int M, int N, int K, int group, cudaStream_t st) {
   const int g = group > 0 ? group : K;
   dim3 grid((N + GBN - 1) / GBN, (M + GBM - 1) / GBM);
   gemm_simt_kernel<int8_t><<<grid, kGemmThreads, 0, st>>>(out, x, q, scale, resid, M, N, K, g);

@@ -1,0 +1,421 @@
+// gemm_tc.cu — the prefill-regime quantized Linear (M > 32) on the
+// 5th-generation tensor cores.
+//
+// out[M, N] = x[M, K] @ (q * scale)^T (+ resid), q int8 [N, K] as stored.
+//
+// The fp32 activations are split per row into int8 digit planes:
+//   x[m, k] / s_m = d0 + d1 / 128 (+ d2 / 128^2),   s_m = max_k |x[m, k]| / 127,
+// (tc_digits_kernel; optionally of RMSNorm(x) * norm_w, so the norm costs no
+// extra pass).  Every plane times the raw weight bytes is an exact s32 sum on
+// tcgen05.mma kind::i8, so the only approximation is the digit truncation:
+// below 2^-21 (three planes) or 2^-14 (two planes) of s_m per element.
+//
+// gemm_tc_kernel: one 128 x 128 output tile per CTA, 4 warps.
+//   warp 0 lane 0: TMA producer — per 128-byte K block, the NP digit-plane
+//     tiles and the weight tile (128 rows x 128 bytes each, 128-byte
+//     swizzle) into a ring of shared-memory stages (mbarrier completion);
+//   warp 1 lane 0: MMA issuer — per K block 4 x NP tcgen05.mma (M 128,
+//     N 128, K 32), plane p accumulating in TMEM columns [128 p, 128 p + 128);
+//     tcgen05.commit releases the stage when its MMAs are done;
+//   all 4 warps: epilogue — each thread owns one output row (its TMEM lane),
+//     reads the plane accumulators with tcgen05.ld and writes
+//     s_m * scale[n] * (D0 + D1 / 128 + D2 / 128^2) (+ resid).
+// Consecutive CTAs share a weight tile (blockIdx.x walks M first), so a
+// weight tile streams from HBM once and the other M tiles read it from L2.
+// Every wait is bounded (counted in the library's timeout word).
+#include <cuda.h>  // CUtensorMap and the tensor-map encoder's types (resolved through the runtime)
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tma_common.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 128;  // kTcBK in bytes = int8 elements
+constexpr int kTcTile = kTcBM * kTcBK;                 // 16 KB: one operand tile
+constexpr int kTcThreads = 128;
+constexpr int kTcMaxK = 65536;  // |sum of K products| < 2^31 for every plane
+
+template <int NP>
+struct TcCfg {
+  static constexpr int kStageBytes = (NP + 1) * kTcTile;
+  static constexpr int kStages = NP == 3 ? 3 : 4;
+  static constexpr int kTmemCols = NP == 3 ? 512 : 256;  // NP x 128 accumulator columns, power of two
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
+};
+
+// ---------------------------------------------------------------------------
+// digit planes
+// ---------------------------------------------------------------------------
+template <int NP>
+__global__ void __launch_bounds__(256) tc_digits_kernel(int8_t* __restrict__ dig, float* __restrict__ srow,
+                                                        const float* __restrict__ x, int M, int K,
+                                                        const float* __restrict__ norm_w, float eps) {
+  __shared__ float red[2][8];
+  const int m = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * K);
+  const float4* wr = reinterpret_cast<const float4*>(norm_w);
+  const int nv = K >> 2;
+  float ss = 0.f, mx = 0.f;
+  for (int v = threadIdx.x; v < nv; v += 256) {
+    const float4 t = xr[v];
+    ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    const float4 w = norm_w ? wr[v] : make_float4(1.f, 1.f, 1.f, 1.f);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w))));
+  }
+  ss = warp_sum(ss);
+  mx = warp_max(mx);
+  if (lane == 0) {
+    red[0][warp] = ss;
+    red[1][warp] = mx;
+  }
+  __syncthreads();
+  float tot = 0.f, a = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; w++) {
+    tot += red[0][w];
+    a = fmaxf(a, red[1][w]);
+  }
+  // RMSNorm as cpu/backend.go:606-652: rms = sqrt(sumSq / d + eps), out = (x / rms) * w
+  const float rms = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)) : 1.0f;
+  if (norm_w) a = a / rms * 1.0001f;  // covers the rounding of (x / rms) * w against (x * w) / rms
+  const float s = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
+  const float inv = 1.0f / s;
+  if (threadIdx.x == 0) srow[m] = s;
+  uint32_t* d0 = reinterpret_cast<uint32_t*>(dig + (size_t)m * K);
+  const size_t plane = (size_t)M * K / 4;  // uint32 per plane
+  for (int v = threadIdx.x; v < nv; v += 256) {
+    float4 t = xr[v];
+    if (norm_w) {
+      const float4 w = wr[v];
+      t.x = __fmul_rn(__fdiv_rn(t.x, rms), w.x);
+      t.y = __fmul_rn(__fdiv_rn(t.y, rms), w.y);
+      t.z = __fmul_rn(__fdiv_rn(t.z, rms), w.z);
+      t.w = __fmul_rn(__fdiv_rn(t.w, rms), w.w);
+    }
+    const float vals[4] = {t.x, t.y, t.z, t.w};
+    uint32_t p[3] = {0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float u = fminf(fmaxf(vals[j] * inv, -127.0f), 127.0f);
+      const float e0 = rintf(u);
+      const float r1 = (u - e0) * 128.0f;
+      const float e1 = rintf(r1);
+      const float e2 = rintf((r1 - e1) * 128.0f);
+      p[0] |= ((uint32_t)__float2int_rn(e0) & 0xffu) << (8 * j);
+      p[1] |= ((uint32_t)__float2int_rn(e1) & 0xffu) << (8 * j);
+      p[2] |= ((uint32_t)__float2int_rn(e2) & 0xffu) << (8 * j);
+    }
+#pragma unroll
+    for (int q = 0; q < NP; q++) d0[q * plane + v] = p[q];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA primitives
+// ---------------------------------------------------------------------------
+// Shared-memory matrix descriptor of a K-major operand tile stored with the
+// 128-byte swizzle: rows of 128 bytes, 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4)  // start address
+         | ((uint64_t)1 << 16)                 // leading byte offset (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)       // stride byte offset: one 8-row group
+         | ((uint64_t)1 << 46)                 // descriptor version (tcgen05)
+         | ((uint64_t)2 << 61);                // 128-byte swizzle
+}
+
+// Instruction descriptor: kind::i8, D s32, A and B signed 8-bit, both
+// K-major, M 128, N 128.
+constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
+                              ((uint32_t)(kTcBM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdescI8), "r"(accumulate)
+      : "memory");
+}
+// Arrives on `bar` once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Keeps the uses of r after the preceding (volatile) wait.
+__device__ __forceinline__ void pin32(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j++) asm volatile("" : "+r"(r[j]));
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   float* out, const float* __restrict__ srow, const float* __restrict__ scale,
+                   const float* resid, int M, int N, int K, int vec_ok, int* err) {
+  using C = TcCfg<NP>;
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment of the swizzled tiles (in the shared address space)
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* done = empty + C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kTcBM, n0 = blockIdx.y * kTcBN;
+  const int nk = (K + kTcBK - 1) / kTcBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; s++) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    mbarrier_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // producer
+    for (int kb = 0; kb < nk; kb++) {
+      const int s = kb % C::kStages, use = kb / C::kStages;
+      if (use > 0) mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), err);
+      unsigned char* st = smem + (size_t)s * C::kStageBytes;
+      mbarrier_expect_tx(&full[s], (uint32_t)C::kStageBytes);
+#pragma unroll
+      for (int p = 0; p < NP; p++) tma_load_3d(st + p * kTcTile, &tmA, kb * kTcBK, m0, p, &full[s]);
+      tma_load_2d(st + NP * kTcTile, &tmB, kb * kTcBK, n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    for (int kb = 0; kb < nk; kb++) {
+      const int s = kb % C::kStages, use = kb / C::kStages;
+      mbarrier_wait(&full[s], (uint32_t)(use & 1), err);
+      tc_fence_after();
+      const uint32_t a0 = smem_addr(smem + (size_t)s * C::kStageBytes);
+      const uint32_t b0 = a0 + NP * kTcTile;
+#pragma unroll
+      for (int kk = 0; kk < kTcBK / 32; kk++) {
+#pragma unroll
+        for (int p = 0; p < NP; p++)
+          tc_mma_i8(tmem + p * kTcBN, sw128_desc(a0 + p * kTcTile + kk * 32), sw128_desc(b0 + kk * 32),
+                    (kb | kk) != 0);
+      }
+      tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    tc_commit(done);
+  }
+  __syncwarp();
+
+  // epilogue: thread = output row m0 + 32 warp + lane = TMEM lane 32 warp + lane
+  mbarrier_wait(done, 0u, err);
+  __syncwarp();  // tcgen05.ld is warp-collective
+  tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  const bool live = row < M;
+  const float sr = live ? srow[row] : 0.f;
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  for (int c = 0; c < kTcBN; c += 32) {
+    uint32_t acc[NP][32];
+#pragma unroll
+    for (int p = 0; p < NP; p++) tmem_ld32(lane_base + p * kTcBN + c, acc[p]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int p = 0; p < NP; p++) pin32(acc[p]);
+    if (!live) continue;
+    float* orow = out + (size_t)row * N;
+    const float* rrow = resid ? resid + (size_t)row * N : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const int n = n0 + c + j;
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        float t = (float)(int)acc[0][j + e] + (float)(int)acc[1][j + e] * (1.0f / 128.0f);
+        if (NP == 3) t += (float)(int)acc[NP - 1][j + e] * (1.0f / 16384.0f);
+        y[e] = t;
+      }
+      if (vec_ok && n + 3 < N) {
+        const float4 sc = *reinterpret_cast<const float4*>(scale + n);
+        float4 o = make_float4(sr * sc.x * y[0], sr * sc.y * y[1], sr * sc.z * y[2], sr * sc.w * y[3]);
+        if (rrow) {
+          const float4 r = *reinterpret_cast<const float4*>(rrow + n);
+          o.x += r.x;
+          o.y += r.y;
+          o.z += r.z;
+          o.w += r.w;
+        }
+        *reinterpret_cast<float4*>(orow + n) = o;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          if (n + e < N) {
+            float o = sr * scale[n + e] * y[e];
+            if (rrow) o += rrow[n + e];
+            orow[n + e] = o;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+bool device_is_sm100() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+template <int NP>
+tb_status_t launch_tc(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
+                      const float* resid, int M, int N, int K, cudaStream_t st) {
+  using C = TcCfg<NP>;
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return TB_ERROR_NOT_SUPPORTED;
+  CUtensorMap ta, tbm;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, (cuuint64_t)NP};
+    const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)M * (cuuint64_t)K};
+    const cuuint32_t box[3] = {kTcBK, kTcBM, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = enc(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(dig), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return TB_ERROR_NOT_SUPPORTED;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {kTcBK, kTcBN};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return TB_ERROR_NOT_SUPPORTED;
+  }
+  static std::once_flag once[2];
+  static cudaError_t attr_err[2];
+  std::call_once(once[NP - 2], [] {
+    attr_err[NP - 2] =
+        cudaFuncSetAttribute(gemm_tc_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+  });
+  if (attr_err[NP - 2] != cudaSuccess) return cuda_fail(attr_err[NP - 2], "cudaFuncSetAttribute(gemm_tc)");
+  const int vec_ok = (N % 4 == 0) && ((uintptr_t)out % 16 == 0) && ((uintptr_t)scale % 16 == 0) &&
+                     (!resid || (uintptr_t)resid % 16 == 0);
+  int* err = wait_timeout_word();
+  const dim3 grid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
+  gemm_tc_kernel<NP><<<grid, kTcThreads, C::kSmem, st>>>(ta, tbm, out, srow, scale, resid, M, N, K, vec_ok, err);
+  return check_launch("gemm_tc_kernel");
+}
+
+}  // namespace
+
+size_t gemm_tc_workspace(int64_t M, int64_t K, int planes) {
+  const size_t dig = ((size_t)planes * (size_t)M * (size_t)K + 255) & ~(size_t)255;
+  return dig + (size_t)M * sizeof(float);
+}
+
+bool gemm_tc_ok(const void* q, int64_t M, int64_t N, int64_t K) {
+  static const bool sm100 = device_is_sm100();
+  return sm100 && M >= 1 && N >= 1 && K >= 16 && K % 16 == 0 && K <= kTcMaxK && M <= 0x7fffffff / 4 &&
+         N <= 65535 * kTcBN && ((uintptr_t)q % 16 == 0) && encode_tiled() != nullptr;
+}
+
+tb_status_t gemm_tc_digits(int8_t* dig, float* srow, const float* x, int M, int K, int planes, const float* norm_w,
+                           float eps, cudaStream_t st) {
+  if (M <= 0) return TB_SUCCESS;
+  if (K % 4 != 0 || (uintptr_t)x % 16 != 0 || (norm_w && (uintptr_t)norm_w % 16 != 0))
+    return TB_ERROR_NOT_SUPPORTED;
+  if (planes == 3)
+    tc_digits_kernel<3><<<M, 256, 0, st>>>(dig, srow, x, M, K, norm_w, eps);
+  else
+    tc_digits_kernel<2><<<M, 256, 0, st>>>(dig, srow, x, M, K, norm_w, eps);
+  return check_launch("tc_digits_kernel");
+}
+
+tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
+                        const float* resid, int M, int N, int K, int planes, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return TB_SUCCESS;
+  if (planes == 3) return launch_tc<3>(out, dig, srow, q, scale, resid, M, N, K, st);
+  return launch_tc<2>(out, dig, srow, q, scale, resid, M, N, K, st);
+}
+
+tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
+                    int K, int planes, void* ws, cudaStream_t st) {
+  int8_t* dig = static_cast<int8_t*>(ws);
+  float* srow = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + gemm_tc_workspace(M, K, planes) -
+                                         (size_t)M * sizeof(float));
+  TB_TRY(gemm_tc_digits(dig, srow, x, M, K, planes, nullptr, 0.f, st));
+  return gemm_tc_run(out, dig, srow, q, scale, resid, M, N, K, planes, st);
+}
+
+}  // namespace tb

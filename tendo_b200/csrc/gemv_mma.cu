@@ -1045,6 +1045,12 @@ tb_status_t gemv_tma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl) {
   TB_TMA_DISPATCH(gemv_tma_gateup_kernel, RG, tiles, p, st, pdl, a, p.Kc, p.stages);
 }
 
+int* wait_timeout_word() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_wait_timeouts) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
 int take_wait_timeouts() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(int)) != cudaSuccess) return -1;

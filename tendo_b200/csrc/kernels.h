@@ -127,6 +127,8 @@ tb_status_t gemv_tma_qkv(const QkvArgs& a, cudaStream_t st, bool pdl);
 tb_status_t gemv_tma_gateup(const GateUpArgs& a, cudaStream_t st, bool pdl);
 // Bounded device waits that expired since the last call (and resets the count).
 int take_wait_timeouts();
+// Device address of that count, for kernels in other files.
+int* wait_timeout_word();
 // Kernel family of the decode GEMVs (TENDO_B200_GEMV = tma | mma | simt; default tma).
 enum class GemvKind { kTma, kMma, kSimt };
 GemvKind gemv_kind();
@@ -140,9 +142,24 @@ tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const float* vcache, int B, int H,
                          int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st);
 
-// gemm.cu: out[M, N] = x[M, K] @ (q * scale)^T (+ resid), M > 32.
-tb_status_t gemm_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
-                    int N, int K, int group, tb_gemm_mode_t mode, cudaStream_t st);
+// gemm_tc.cu: the prefill-regime quantized Linear on the 5th-generation
+// tensor cores.  x rows are split into `planes` int8 digit rows
+// (x = s_m (d0 + d1 / 128 [+ d2 / 128^2]), optionally of RMSNorm(x) * norm_w),
+// then out[M, N] = s_m scale[n] sum_p 128^-p (d_p . q_n) (+ resid) with the
+// digit products summed exactly in s32 by tcgen05.mma kind::i8.
+size_t gemm_tc_workspace(int64_t M, int64_t K, int planes);
+bool gemm_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
+tb_status_t gemm_tc_digits(int8_t* dig, float* srow, const float* x, int M, int K, int planes, const float* norm_w,
+                           float eps, cudaStream_t st);
+tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
+                        const float* resid, int M, int N, int K, int planes, cudaStream_t st);
+// digits + GEMM with the digit rows in `ws` (gemm_tc_workspace bytes).
+tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
+                    int K, int planes, void* ws, cudaStream_t st);
+
+// gemm.cu: out[M, N] = x[M, K] @ (q * scale)^T (+ resid) on CUDA cores.
+tb_status_t gemm_simt_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
+                         int M, int N, int K, int group, cudaStream_t st);
 tb_status_t gemm_f32_nt(float* out, const float* a, const float* b, int M, int N, int K, cudaStream_t st);
 
 // ops.cu

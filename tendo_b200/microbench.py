@@ -103,7 +103,7 @@ def main():
     ap.add_argument("--N", type=int, nargs="+", default=[4096, 11008])
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--mode", type=int, default=tb.TB_GEMM_BF16X2)
+    ap.add_argument("--mode", type=int, default=tb.TB_GEMM_I8X3)
     a = ap.parse_args()
     if a.decode_layers > 0:
         decode_small(a.decode_layers, a.tokens)

@@ -135,6 +135,19 @@ def test_argument_validation_needs_no_gpu(tb):
     assert L.tb_quantize_i8_f32(None, None, None, 4, 10, 3, None) == tb.TB_ERROR_INVALID_ARGUMENT
     assert L.tb_dequant_matmul_i8f32(None, None, None, None, -1, 4, 4, 0, None) == tb.TB_ERROR_INVALID_ARGUMENT
     assert L.tb_dequant_matmul_i8f32(None, None, None, None, 1, 4, 12, 5, None) == tb.TB_ERROR_INVALID_ARGUMENT
+    # the tensor-core GEMM's scratch: none for the GEMV, per-group or CUDA-core
+    # modes; digit rows + row scales otherwise; a short workspace is rejected
+    # before any launch
+    assert L.tb_dequant_matmul_workspace_size(32, 4096, 4096, 0, tb.TB_GEMM_I8X3) == 0
+    assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 128, tb.TB_GEMM_I8X3) == 0
+    assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 0, tb.TB_GEMM_SIMT) == 0
+    assert L.tb_dequant_matmul_workspace_size(33, 4096, 4096, 0, tb.TB_GEMM_I8X3) == 3 * 33 * 4096 + 33 * 4
+    assert L.tb_dequant_matmul_workspace_size(33, 4096, 4096, 0, tb.TB_GEMM_I8X2) == 2 * 33 * 4096 + 33 * 4
+    fake = 4096  # never dereferenced: the size check comes first
+    assert L.tb_dequant_matmul_i8f32_ws(fake, fake, fake, fake, 64, 64, 64, 0, tb.TB_GEMM_I8X3, None, 0,
+                                        None) == tb.TB_ERROR_INVALID_ARGUMENT
+    assert L.tb_dequant_matmul_i8f32_ws(fake, fake, fake, fake, 64, 64, 64, 0, 7, fake, 1 << 20,
+                                        None) == tb.TB_ERROR_INVALID_ARGUMENT
     # empty problems are no-ops
     assert L.tb_dequant_matmul_i8f32(None, None, None, None, 0, 4, 16, 0, None) == 0
     assert L.tb_rmsnorm_f32(None, None, None, 0, 8, 1e-5, None) == 0
