@@ -31,7 +31,7 @@ namespace {
 
 constexpr int kMkWarps = 8;  // consumer warps
 constexpr int kMkConsumers = kMkWarps * 32;
-constexpr int kMkThreads = kMkConsumers + 32;
+constexpr int kMkThreads = kMkConsumers + 32;  // + producer warp
 constexpr int kMkStages = 5;
 constexpr int kMkChunkMax = 4096;
 constexpr int kMkStageBytes = 8 * (kMkChunkMax + 64);
@@ -120,6 +120,37 @@ __device__ __forceinline__ const int8_t* row_of(const Stream& s, int tile, int n
   if (s.kind == 3 && r >= s.rows) r = s.rows - 1;
   return s.base + (size_t)r * s.row_bytes;
 }
+
+// Walks this CTA's weight-stream units (phase p, tile, chunk) in consumption order.
+struct UnitCursor {
+  Stream s;
+  int p, tile, ch, Kc, nch;
+  bool done;
+  __device__ __forceinline__ void load(const MkArgs& a) {
+    for (; p <= 4 * a.L; p++) {
+      s = stream_of(a, p);
+      Kc = chunk_bytes(s.row_bytes);
+      nch = s.row_bytes / Kc;
+      tile = blockIdx.x;
+      ch = 0;
+      if (tile < s.ntiles) return;
+    }
+    done = true;
+  }
+  __device__ __forceinline__ void start(const MkArgs& a) {
+    p = 0;
+    done = false;
+    load(a);
+  }
+  __device__ __forceinline__ void advance(const MkArgs& a) {
+    if (++ch < nch) return;
+    ch = 0;
+    tile += gridDim.x;
+    if (tile < s.ntiles) return;
+    p++;
+    load(a);
+  }
+};
 
 struct Pipe {
   unsigned char* stages;
@@ -292,6 +323,16 @@ __device__ __forceinline__ float tile_value(const int* part_all, int it, float s
   return sc * ((float)s0 + (float)s1 * (1.0f / 128.0f) + (float)s2 * (1.0f / 16384.0f));
 }
 
+// L2-only load whose line is marked evict-first: the KV rows of a layer are
+// read once per token.
+__device__ __forceinline__ float4 ld_evict_first4(const float* p, uint64_t pol) {
+  float4 v;
+  asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
 template <int VEC, int G>
 __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, float* merge) {
   constexpr int D = VEC * 32, U = 8;
@@ -302,6 +343,8 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
   const int64_t start = (int64_t)split * chunk, end = min(start + chunk, sk);
   const float* kb = a.kc + (((size_t)l * a.Hkv + kvh) * a.max_seq) * D;
   const float* vb = a.vc + (((size_t)l * a.Hkv + kvh) * a.max_seq) * D;
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   float qr[G][VEC];
 #pragma unroll
   for (int gi = 0; gi < G; gi++)
@@ -324,7 +367,7 @@ __device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, flo
       for (int e = 0; e < VEC; e++) kr[u][e] = vr[u][e] = 0.f;
       if (j < end) {
         if constexpr (VEC == 4) {
-          const float4 k4 = ldcg4(kb + j * D + lane * 4), v4 = ldcg4(vb + j * D + lane * 4);
+          const float4 k4 = ld_evict_first4(kb + j * D + lane * 4, pol), v4 = ld_evict_first4(vb + j * D + lane * 4, pol);
           kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
           vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
         } else {
@@ -481,28 +524,29 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   if (warp == kMkWarps) {
     // producer: the step's weight tiles in consumption order
     if (lane == 0) {
-      int u = 0;
-      for (int p = 0; p <= 4 * a.L; p++) {
-        const Stream s = stream_of(a, p);
-        const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc, RS = bank_stride(Kc);
-        for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x) {
-          for (int ch = 0; ch < nch; ch++, u++) {
-            const int st = u % kMkStages, use = u / kMkStages;
-            if (use > 0) mbarrier_wait(&empty[st], (uint32_t)((use - 1) & 1), a.err);
-            unsigned char* dst = stages + (size_t)st * kMkStageBytes;
-            mbarrier_expect_tx(&full[st], (uint32_t)(8 * Kc));
+      // weights are read once per token: evict them first, so the activations,
+      // norm weights, channel scales and KV rows the consumers touch stay in L2
+      uint64_t policy;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      UnitCursor c;
+      c.start(a);
+      for (int u = 0; !c.done; u++) {
+        const int st = u % kMkStages, use = u / kMkStages;
+        if (use > 0) mbarrier_wait(&empty[st], (uint32_t)((use - 1) & 1), a.err);
+        unsigned char* dst = stages + (size_t)st * kMkStageBytes;
+        const int RS = bank_stride(c.Kc);
+        mbarrier_expect_tx(&full[st], (uint32_t)(8 * c.Kc));
 #pragma unroll
-            for (int n = 0; n < 8; n++)
-              bulk_copy_g2s(dst + (size_t)n * RS, row_of(s, tile, n) + (size_t)ch * Kc, (uint32_t)Kc, &full[st]);
-          }
-        }
+        for (int n = 0; n < 8; n++)
+          bulk_copy_g2s_hint(dst + (size_t)n * RS, row_of(c.s, c.tile, n) + (size_t)c.ch * c.Kc, (uint32_t)c.Kc,
+                             &full[st], policy);
+        c.advance(a);
       }
       // every copy lands before the consumers release its stage, so the CTA
       // never exits with a copy in flight
     }
     return;
   }
-
   // consumers
   unsigned int target = 0;
   Trace tr{a.trace, 0};
