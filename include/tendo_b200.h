@@ -80,24 +80,26 @@ TB_API tb_status_t tb_dequantize_i8_f32(float* w, const int8_t* q, const float* 
  * Replaces popcornDequantizeMatmul_i8f32 (cuda/popcorn.go:1306-1315, per
  * channel) and popcornDequantizeMatmulGrouped_i8f32 (cuda/popcorn.go:1353-1363,
  * group_size > 0), reached from cuda.Backend.DequantizeMatmul
- * (cuda/backend.go:676-721).  M <= 32 runs the fused-dequant int8 GEMV;
- * larger M runs the tcgen05 tensor-core GEMM: each row of x is split into
- * three int8 digit rows (x = s (d0 + d1/128 + d2/128^2), s = max|x|/127) and
- * every digit row times the raw int8 weights is summed exactly in s32
- * (tcgen05.mma kind::i8), so the result is within 2^-21 s sum|w| of the
- * fp32 product.  Per-group scales (group_size > 0) run the CUDA-core GEMM.
- * The digit rows need scratch: this entry point keeps one library-owned
- * buffer per device, allocated on first use and grown on demand (calls that
- * overlap in time on one device must use tb_dequant_matmul_i8f32_ws). */
+ * (cuda/backend.go:676-721).  Both regimes run on the tcgen05 tensor cores:
+ * each row of x is split into three int8 digit rows (x = s (d0 + d1/128 +
+ * d2/128^2), s = max|x|/127) and every digit row times the raw int8 weights
+ * is summed exactly in s32 (tcgen05.mma kind::i8), so the result is within
+ * 2^-21 s sum|w| of the fp32 product.  M <= 32: the weights are the MMA's
+ * 128-row operand and the (tile, K block) work is split evenly over the SMs
+ * (K % 128 == 0; other K run the CUDA-core GEMV).  M > 32: 128 x 128 output
+ * tiles.  Per-group scales (group_size > 0) run the CUDA-core kernels.
+ * Scratch: this entry point keeps library-owned buffers per device,
+ * allocated on first use and grown on demand (calls that overlap in time on
+ * one device must use tb_dequant_matmul_i8f32_ws). */
 TB_API tb_status_t tb_dequant_matmul_i8f32(float* out, const float* x, const int8_t* q, const float* scale,
                                     int64_t M, int64_t N, int64_t K, int64_t group_size,
                                     tb_stream_t stream);
 
-/* GEMM modes for M > 32. */
+/* Quantized-Linear kernel modes. */
 typedef enum {
   TB_GEMM_I8X3 = 0, /* tcgen05 kind::i8, three digit rows of x: within 2^-21 s sum|w| (default) */
-  TB_GEMM_I8X2 = 1, /* tcgen05 kind::i8, two digit rows: within 2^-14 s sum|w|, 1.5x fewer MMAs */
-  TB_GEMM_SIMT = 2  /* fp32 CUDA-core tiles (no tensor cores) */
+  TB_GEMM_I8X2 = 1, /* M > 32: two digit rows, within 2^-14 s sum|w|, 1.5x fewer MMAs (M <= 32: as I8X3) */
+  TB_GEMM_SIMT = 2  /* fp32 CUDA-core kernels (no tensor cores) */
 } tb_gemm_mode_t;
 
 /* tb_dequant_matmul_i8f32 with the GEMM mode chosen by the caller (used for
@@ -112,8 +114,8 @@ TB_API size_t tb_dequant_matmul_workspace_size(int64_t M, int64_t N, int64_t K, 
                                                tb_gemm_mode_t mode);
 
 /* tb_dequant_matmul_i8f32_mode with caller-owned scratch (the Go backend's
- * pool): allocates nothing.  workspace_bytes below the size above returns
- * TB_ERROR_INVALID_ARGUMENT. */
+ * pool): allocates nothing; any contents on entry.  workspace_bytes below the
+ * size above returns TB_ERROR_INVALID_ARGUMENT. */
 TB_API tb_status_t tb_dequant_matmul_i8f32_ws(float* out, const float* x, const int8_t* q, const float* scale,
                                               int64_t M, int64_t N, int64_t K, int64_t group_size,
                                               tb_gemm_mode_t mode, void* workspace, size_t workspace_bytes,

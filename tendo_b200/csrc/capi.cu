@@ -77,27 +77,32 @@ namespace {
 
 int gemm_planes(tb_gemm_mode_t mode) { return mode == TB_GEMM_I8X2 ? 2 : 3; }
 
-size_t dqmm_workspace(int64_t M, int64_t K, int64_t group_size, tb_gemm_mode_t mode) {
-  if (M <= 32 || group_size > 0 || mode == TB_GEMM_SIMT) return 0;
+size_t dqmm_workspace(int64_t M, int64_t N, int64_t K, int64_t group_size, tb_gemm_mode_t mode) {
+  if (group_size > 0 || mode == TB_GEMM_SIMT) return 0;
+  if (M <= tb::kGemvTcMaxM) {
+    if (K % 128 != 0) return 0;
+    return tb::gemv_tc_zeroed_bytes(M, N, K) + tb::gemv_tc_scratch_bytes(M, N, K);
+  }
   return tb::gemm_tc_workspace(M, K, gemm_planes(mode));
 }
 
-// One library-owned scratch buffer per device for the entry points without a
-// workspace argument: allocated on first use, grown (after a device
-// synchronisation) when a larger call arrives.
+// Library-owned buffers per device for the entry points without a workspace
+// argument: kind 0 is plain scratch, kind 1 is kept zero between calls (the
+// GEMV's split-tile counters and sums).  Allocated on first use, grown (after
+// a device synchronisation) when a larger call arrives.
 std::mutex g_arena_mu;
 struct ArenaSlot {
   void* p = nullptr;
   size_t n = 0;
 };
-ArenaSlot g_arena[64];
+ArenaSlot g_arena[2][64];
 
-tb_status_t arena_get(size_t bytes, void** out) {
+tb_status_t arena_get(int kind, size_t bytes, void** out) {
   int dev = 0;
   TB_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return TB_ERROR_NOT_SUPPORTED;
   std::lock_guard<std::mutex> lk(g_arena_mu);
-  ArenaSlot& a = g_arena[dev];
+  ArenaSlot& a = g_arena[kind][dev];
   if (a.n < bytes) {
     if (a.p) {
       TB_CUDA(cudaDeviceSynchronize());
@@ -107,6 +112,7 @@ tb_status_t arena_get(size_t bytes, void** out) {
     }
     const size_t want = bytes + bytes / 4;
     TB_CUDA(cudaMalloc(&a.p, want));
+    if (kind == 1) TB_CUDA(cudaMemset(a.p, 0, want));
     a.n = want;
   }
   *out = a.p;
@@ -116,14 +122,29 @@ tb_status_t arena_get(size_t bytes, void** out) {
 tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
                  int64_t group_size, tb_gemm_mode_t mode, void* ws, size_t ws_bytes, bool arena, cudaStream_t st) {
   if (M <= 32) {
+    const size_t gneed = dqmm_workspace(M, N, K, group_size, mode);
+    if (gneed > 0 && tb::gemv_tc_ok(q, M, N, K) && (uintptr_t)x % 16 == 0) {
+      const size_t zb = tb::gemv_tc_zeroed_bytes(M, N, K), sb = tb::gemv_tc_scratch_bytes(M, N, K);
+      void *zero = nullptr, *scratch = nullptr;
+      if (arena) {
+        TB_TRY(arena_get(1, zb, &zero));
+        if (sb) TB_TRY(arena_get(0, sb, &scratch));
+      } else {
+        TB_REQUIRE(ws && ws_bytes >= gneed);
+        zero = ws;
+        scratch = static_cast<unsigned char*>(ws) + zb;
+      }
+      return tb::gemv_tc(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, zero, !arena, scratch, st);
+    }
+    if (!arena && gneed > 0) TB_REQUIRE(ws && ws_bytes >= gneed);
     if (group_size == 0 && tb::gemv_fast_ok(x, q, K))
       return tb::gemv_plain(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, nullptr, 0.f, st, false);
     return tb::gemv_generic(out, x, q, scale, (int)M, (int)N, (int)K, group_size > 0 ? (int)group_size : (int)K, st);
   }
-  const size_t need = dqmm_workspace(M, K, group_size, mode);
+  const size_t need = dqmm_workspace(M, N, K, group_size, mode);
   if (need > 0 && tb::gemm_tc_ok(q, M, N, K) && (uintptr_t)x % 16 == 0) {
     if (arena) {
-      TB_TRY(arena_get(need, &ws));
+      TB_TRY(arena_get(0, need, &ws));
     } else {
       TB_REQUIRE(ws && ws_bytes >= need);
     }
@@ -145,9 +166,8 @@ tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale
 
 extern "C" size_t tb_dequant_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
                                                    tb_gemm_mode_t mode) {
-  (void)N;
-  if (M < 0 || K <= 0 || group_size < 0) return 0;
-  return dqmm_workspace(M, K, group_size, mode);
+  if (M < 0 || N < 0 || K <= 0 || group_size < 0) return 0;
+  return dqmm_workspace(M, N, K, group_size, mode);
 }
 
 extern "C" tb_status_t tb_dequant_matmul_i8f32_ws(float* out, const float* x, const int8_t* q, const float* scale,

@@ -1,0 +1,503 @@
+// gemv_tc.cu — the decode-regime quantized Linear (1 <= M <= 32) on the
+// 5th-generation tensor cores, for the microbench and C-ABI callers.
+//
+// out[M, N] = x[M, K] @ (q * scale)^T (+ resid), q int8 [N, K] as stored.
+//
+// x is split into three int8 digit rows per batch row,
+//   x[m] = s_m (d0 + d1 / 128 + d2 / 128^2),   s_m = max_k |x[m, k]| / 127,
+// and every digit row times the raw weight bytes is an exact s32 sum
+// (tcgen05.mma kind::i8).  The MMA runs "swapped": the weights are the
+// 128-row A operand and the 3M digit rows (padded to ND, a multiple of 16)
+// the N side, so a tile is 128 weight rows x ND digit columns in TMEM and the
+// weight stream — the only large operand — moves in 16 KB TMA boxes.
+//
+// Work split ("stream-K"): the tile-major space of (weight tile, 128-byte
+// K block) iterations is cut into gridDim.x equal contiguous ranges, one per
+// CTA (one CTA per SM), so every SM streams the same number of weight bytes
+// whatever N and K are.  A tile whose K blocks span several CTAs is summed in
+// the workspace with integer reductions (red.add: exact, order-free); the
+// last CTA to count itself in finishes the tile and zeroes its slots again.
+//
+// Warps: 0 = TMA producer, 1 = MMA issuer (4 x tcgen05.mma per 128-byte K
+// block into one of two TMEM accumulators), 2..5 = epilogue (one weight row
+// per thread: its TMEM lane).  For M <= 8 (kGvInlineM) four more warps turn
+// x into the digit tiles of each stage directly in shared memory (row maxima
+// first, then 128 columns per stage), so one kernel does the whole product;
+// for larger M a digit kernel writes the digit rows and the producer loads
+// them with TMA.  The producer starts the weight stream before the
+// programmatic-launch wait: weights never depend on the preceding kernel.
+#include <string.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+#include "tma_common.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kGvRows = 128;               // weight rows per tile (MMA M)
+constexpr int kGvBK = 128;                 // K bytes per stage
+constexpr int kGvWTile = kGvRows * kGvBK;  // 16 KB
+constexpr int kGvTmemCols = 256;           // two accumulators of up to 128 columns
+constexpr int kGvInlineM = 8;              // M up to which the kernel makes its own digits
+
+struct GvArgs {
+  float* out;
+  const float* x;       // inline digits: the activations
+  const float* srow;    // TMA digits: row scales written by the digit kernel
+  const float* scale;
+  const float* resid;
+  int* acc;             // [tiles][ND][128] s32 sums of split tiles (zero between launches)
+  unsigned int* count;  // [tiles] CTAs done with a split tile (zero between launches)
+  int M, N, K, ND, KB, total, stages;
+  int* err;
+};
+
+// CTA whose iteration range holds iteration `it` (ranges: floor(b T / G)).
+__device__ __forceinline__ int owner_of(long long it, long long total, long long grid) {
+  return (int)(((it + 1) * grid + total - 1) / total) - 1;
+}
+__device__ __forceinline__ int range_begin(long long b, long long total, long long grid) {
+  return (int)(b * total / grid);
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+__device__ __forceinline__ void cvt_sync() { asm volatile("bar.sync 3, 128;" ::: "memory"); }
+
+// byte offset of (row r, byte c) in a K-major tile with the 128-byte swizzle
+__device__ __forceinline__ int sw128_offset(int r, int c) {
+  return (r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 4) ^ (r & 7)) << 4) | (c & 15));
+}
+
+template <bool INL>
+__global__ void __launch_bounds__(INL ? 320 : 192, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GvArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  const int S = a.stages;
+  const int stage_bytes = kGvWTile + a.ND * kGvBK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* sready = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sready + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* srow_s = reinterpret_cast<float*>(tmem_slot + 2);  // [kGvInlineM]
+  float* cred = srow_s + kGvInlineM;                         // [4][kGvInlineM]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long T = a.total, G = gridDim.x;
+  const int b0 = range_begin(blockIdx.x, T, G), b1 = range_begin(blockIdx.x + 1, T, G);
+  const int KB = a.KB, M = a.M, ND = a.ND;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbarrier_init(&full[s], INL ? 2 : 1);  // + the arrival of the converter warp of the stage
+      mbarrier_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbarrier_init(&tfull[b], 1);
+      mbarrier_init(&tempty[b], 4);  // one arrival per epilogue warp
+    }
+    mbarrier_init(sready, 4);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    if (!INL) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, kGvTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer; with TMA digits, the digit boxes of the first stages go out
+      // after the programmatic-launch wait, behind the weight boxes
+      const int n = b1 - b0;
+      const int pre = n < S ? n : S;
+      for (int i = 0; i < pre; i++) {
+        const int it = b0 + i;
+        mbarrier_expect_tx(&full[i], (uint32_t)(INL ? kGvWTile : stage_bytes));
+        tma_load_2d(smem + (size_t)i * stage_bytes, &tmW, (it % KB) * kGvBK, (it / KB) * kGvRows, &full[i]);
+      }
+      if (!INL) {
+        pdl_wait();
+        for (int i = 0; i < pre; i++)
+          tma_load_2d(smem + (size_t)i * stage_bytes + kGvWTile, &tmX, ((b0 + i) % KB) * kGvBK, 0, &full[i]);
+      }
+      for (int i = pre; i < n; i++) {
+        const int s = i % S, use = i / S;
+        const int it = b0 + i, kb = it % KB;
+        mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), a.err);
+        unsigned char* st = smem + (size_t)s * stage_bytes;
+        mbarrier_expect_tx(&full[s], (uint32_t)(INL ? kGvWTile : stage_bytes));
+        tma_load_2d(st, &tmW, kb * kGvBK, (it / KB) * kGvRows, &full[s]);
+        if (!INL) tma_load_2d(st + kGvWTile, &tmX, kb * kGvBK, 0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: one accumulator per tile segment, alternating buffers
+      const uint32_t idesc = idesc_i8(kGvRows, ND);
+      int i = 0, seg = 0;
+      for (int it = b0; it < b1; seg++) {
+        const int seg_end = min(b1, (it / KB + 1) * KB);
+        const int buf = seg & 1;
+        if (seg >= 2) mbarrier_wait(&tempty[buf], (uint32_t)(((seg - 2) >> 1) & 1), a.err);
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * 128);
+        for (int first = 1; it < seg_end; it++, i++, first = 0) {
+          const int s = i % S, use = i / S;
+          mbarrier_wait(&full[s], (uint32_t)(use & 1), a.err);
+          tc_fence_after();
+          const uint32_t w0 = smem_addr(smem + (size_t)s * stage_bytes), x0 = w0 + kGvWTile;
+#pragma unroll
+          for (int kk = 0; kk < kGvBK / 32; kk++)
+            tc_mma_i8(d, sw128_desc(w0 + kk * 32), sw128_desc(x0 + kk * 32), idesc, !(first && kk == 0));
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&tfull[buf]);
+      }
+    }
+  } else if (warp < 6) {
+    // epilogue: thread = weight row (tile row 32 q + lane = its TMEM lane)
+    const int q = warp & 3;
+    const int rowt = q * 32 + lane;
+    if (INL) mbarrier_wait(sready, 0u, a.err);
+    const float* srow = INL ? srow_s : a.srow;
+    int seg = 0;
+    for (int it = b0; it < b1; seg++) {
+      const int tile = it / KB;
+      const int tstart = tile * KB, tend = tstart + KB;
+      const int seg_end = min(b1, tend);
+      const int buf = seg & 1;
+      mbarrier_wait(&tfull[buf], (uint32_t)((seg >> 1) & 1), a.err);
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 128);
+      const int n = tile * kGvRows + rowt;
+      const bool live = n < a.N;
+      const float sc = live ? a.scale[n] : 0.f;
+      if (owner_of(tstart, T, G) == owner_of(tend - 1, T, G)) {
+        // the whole tile is this CTA's: finish it from TMEM
+        for (int m = 0; m < M; m++) {
+          uint32_t c0 = tmem_ld1(tb + m), c1 = tmem_ld1(tb + M + m), c2 = tmem_ld1(tb + 2 * M + m);
+          tmem_wait_ld();
+          pin1(c0);
+          pin1(c1);
+          pin1(c2);
+          if (live) {
+            const float y = (INL ? srow[m] : __ldcg(srow + m)) *
+                            ((float)(int)c0 + (float)(int)c1 * (1.0f / 128.0f) + (float)(int)c2 * (1.0f / 16384.0f));
+            float o = y * sc;
+            if (a.resid) o += __ldcg(a.resid + (size_t)m * a.N + n);
+            a.out[(size_t)m * a.N + n] = o;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbarrier_arrive(&tempty[buf]);
+      } else {
+        // split tile: add this CTA's sums into the tile's slots, count in; the
+        // last CTA to count finishes the tile and zeroes the slots again
+        const int nc = owner_of(tend - 1, T, G) - owner_of(tstart, T, G) + 1;
+        int* acc = a.acc + (size_t)tile * ND * kGvRows + rowt;
+        for (int j0 = 0; j0 < ND; j0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tb + j0, v);
+          tmem_wait_ld();
+          pin16(v);
+#pragma unroll
+          for (int j = 0; j < 16; j++)
+            if (j0 + j < 3 * M) atomicAdd(acc + (size_t)(j0 + j) * kGvRows, (int)v[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbarrier_arrive(&tempty[buf]);
+        // the CTA barrier orders every thread's reductions before the counter's
+        // release; its acquire (and the barrier after it) orders the last
+        // CTA's reads after every other CTA's reductions
+        epi_sync();
+        if (threadIdx.x == 64) {
+          unsigned int prev;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.count + tile) : "memory");
+          *last_flag = prev == (unsigned int)(nc - 1) ? 1 : 0;
+        }
+        epi_sync();
+        if (*last_flag) {
+          for (int m0 = 0; m0 < M; m0 += 8) {
+            int d[3][8];
+#pragma unroll
+            for (int p = 0; p < 3; p++)
+#pragma unroll
+              for (int mm = 0; mm < 8; mm++)
+                d[p][mm] = (m0 + mm < M) ? __ldcg(acc + (size_t)(p * M + m0 + mm) * kGvRows) : 0;
+#pragma unroll
+            for (int p = 0; p < 3; p++)
+#pragma unroll
+              for (int mm = 0; mm < 8; mm++)
+                if (m0 + mm < M) acc[(size_t)(p * M + m0 + mm) * kGvRows] = 0;
+#pragma unroll
+            for (int mm = 0; mm < 8; mm++) {
+              const int m = m0 + mm;
+              if (m < M && live) {
+                const float y = (INL ? srow[m] : __ldcg(srow + m)) *
+                                ((float)d[0][mm] + (float)d[1][mm] * (1.0f / 128.0f) +
+                                 (float)d[2][mm] * (1.0f / 16384.0f));
+                float o = y * sc;
+                if (a.resid) o += __ldcg(a.resid + (size_t)m * a.N + n);
+                a.out[(size_t)m * a.N + n] = o;
+              }
+            }
+          }
+          if (threadIdx.x == 64) a.count[tile] = 0u;
+        }
+        epi_sync();
+      }
+      it = seg_end;
+    }
+  } else if (INL) {
+    // converters (warps 6..9): row scales, then the digit tiles; four stages
+    // are converted at once, one per warp (lane = 4-column group)
+    const int ct = threadIdx.x - 192;  // 0..127
+    const int cw = ct >> 5;
+    {
+      // zero every stage's digit tile once: rows >= 3M stay zero
+      const int xbytes = ND * kGvBK;
+      for (int off = ct * 16; off < S * xbytes; off += 128 * 16)
+        *reinterpret_cast<uint4*>(smem + (size_t)(off / xbytes) * stage_bytes + kGvWTile + off % xbytes) =
+            make_uint4(0u, 0u, 0u, 0u);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    pdl_wait();  // x may come from the preceding kernel
+    const int nv = a.K >> 2;
+    float mx[kGvInlineM];
+#pragma unroll
+    for (int m = 0; m < kGvInlineM; m++) mx[m] = 0.f;
+    for (int m = 0; m < M; m++) {
+      const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)m * a.K);
+      float am = 0.f;
+      for (int v0 = ct; v0 < nv; v0 += 128 * 8) {
+        float4 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          t[u] = (v0 + u * 128 < nv) ? __ldcg(xr + v0 + u * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          am = fmaxf(am, fmaxf(fmaxf(fabsf(t[u].x), fabsf(t[u].y)), fmaxf(fabsf(t[u].z), fabsf(t[u].w))));
+      }
+#pragma unroll
+      for (int mm = 0; mm < kGvInlineM; mm++)
+        if (mm == m) mx[mm] = am;
+    }
+#pragma unroll
+    for (int m = 0; m < kGvInlineM; m++) {
+      const float w = warp_max(mx[m]);
+      if (lane == 0) cred[cw * kGvInlineM + m] = w;
+    }
+    cvt_sync();  // also orders every converter's zeroing before any tile is released
+    float inv[kGvInlineM];
+#pragma unroll
+    for (int m = 0; m < kGvInlineM; m++) {
+      float am = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; w++) am = fmaxf(am, cred[w * kGvInlineM + m]);
+      const float sc = (am > 0.f && isfinite(am)) ? am / 127.0f : 1.0f;
+      inv[m] = 1.0f / sc;
+      if (ct == 0 && m < M) srow_s[m] = sc;
+    }
+    __syncwarp();
+    if (lane == 0) mbarrier_arrive(sready);
+    const int n = b1 - b0;
+    // Warp cw owns the stage slots s = cw (mod 4), so the uses of a slot are
+    // made in order by one warp and each wait on a slot's `empty` barrier is
+    // for the phase right after the last one this warp saw complete (a wait
+    // two phases ahead would alias on the parity).  Its stages are taken two
+    // at a time: all x loads first, then the tiles.
+    int i = -1;
+    auto next_mine = [&](int from) {
+      for (int j = from; j < n; j++)
+        if ((j % S) % 4 == cw) return j;
+      return n;
+    };
+    i = next_mine(0);
+    while (i < n) {
+      const int i2 = next_mine(i + 1);
+      const int ii_[2] = {i, i2};
+      float4 xv[2][kGvInlineM];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int ii = ii_[h];
+        const int kb = (b0 + ii) % KB;
+#pragma unroll
+        for (int m = 0; m < kGvInlineM; m++)
+          xv[h][m] = (ii < n && m < M) ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.K + kb * kGvBK) + lane)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int ii = ii_[h];
+        if (ii >= n) break;
+        const int s = ii % S, use = ii / S;
+        if (use > 0) mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), a.err);
+        unsigned char* xt = smem + (size_t)s * stage_bytes + kGvWTile;
+#pragma unroll
+        for (int m = 0; m < kGvInlineM; m++) {
+          if (m >= M) break;
+          const float vals[4] = {xv[h][m].x, xv[h][m].y, xv[h][m].z, xv[h][m].w};
+          uint32_t pk[3] = {0u, 0u, 0u};
+#pragma unroll
+          for (int t = 0; t < 4; t++) {
+            const float u = fminf(fmaxf(vals[t] * inv[m], -127.0f), 127.0f);
+            const float e0 = rintf(u);
+            const float r1 = (u - e0) * 128.0f;
+            const float e1 = rintf(r1);
+            const float e2 = rintf((r1 - e1) * 128.0f);
+            pk[0] |= ((uint32_t)__float2int_rn(e0) & 0xffu) << (8 * t);
+            pk[1] |= ((uint32_t)__float2int_rn(e1) & 0xffu) << (8 * t);
+            pk[2] |= ((uint32_t)__float2int_rn(e2) & 0xffu) << (8 * t);
+          }
+#pragma unroll
+          for (int p = 0; p < 3; p++)
+            *reinterpret_cast<uint32_t*>(xt + sw128_offset(p * M + m, 4 * lane)) = pk[p];
+        }
+        // the tensor core reads the tile through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbarrier_arrive(&full[s]);
+      }
+      i = i2 < n ? next_mine(i2 + 1) : n;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kGvTmemCols);
+}
+
+// Workspace: a zero-maintained part (per-tile counters and split-tile sums:
+// zero before a launch, zero again after it) and, for M > kGvInlineM, a
+// scratch part for the digit rows and row scales.
+struct GvLayout {
+  size_t count, acc, zeroed, dig, srow, scratch;
+};
+
+GvLayout gv_layout(int64_t M, int64_t N, int64_t K) {
+  const int64_t ND = ((3 * M + 15) / 16) * 16;
+  const int64_t tiles = (N + kGvRows - 1) / kGvRows;
+  GvLayout L;
+  L.count = 0;
+  L.acc = ((size_t)tiles * 4 + 255) & ~(size_t)255;
+  L.zeroed = L.acc + (((size_t)tiles * ND * kGvRows * 4 + 255) & ~(size_t)255);
+  L.dig = 0;
+  L.srow = (((size_t)(3 * M * K) + 255) & ~(size_t)255);
+  L.scratch = M <= kGvInlineM ? 0 : L.srow + (size_t)M * 4;
+  return L;
+}
+
+template <bool INL>
+tb_status_t set_gv_smem() {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(gemv_tc_kernel<INL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(gemv_tc)");
+  return TB_SUCCESS;
+}
+
+}  // namespace
+
+size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(M, N, K).zeroed; }
+size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(M, N, K).scratch; }
+
+bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K) {
+  return M >= 1 && M <= kGemvTcMaxM && gemm_tc_ok(q, M, N, K) && K % 128 == 0;
+}
+
+tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
+                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st) {
+  const GvLayout L = gv_layout(M, N, K);
+  unsigned char* z = static_cast<unsigned char*>(zeroed);
+  unsigned char* w = static_cast<unsigned char*>(scratch);
+  const bool inl = M <= kGvInlineM;
+  const int ND = ((3 * M + 15) / 16) * 16;
+  const int KB = K / kGvBK;
+  const int tiles = (N + kGvRows - 1) / kGvRows;
+  const int total = tiles * KB;
+  int grid = sm_count();
+  if (grid > total) grid = total;
+  const int stage_bytes = kGvWTile + ND * kGvBK;
+  int stages = (200 * 1024) / stage_bytes;  // as many weight boxes in flight as fit
+  if (stages > 16) stages = 16;
+  const size_t smem = (size_t)stages * stage_bytes + 1024 + 512;
+  if (inl && (uintptr_t)x % 16 != 0) return TB_ERROR_NOT_SUPPORTED;
+
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return TB_ERROR_NOT_SUPPORTED;
+  CUtensorMap tw, tx;
+  memset(&tx, 0, sizeof(tx));
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {kGvBK, kGvRows};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TB_ERROR_NOT_SUPPORTED;
+  }
+  int8_t* dig = inl ? nullptr : reinterpret_cast<int8_t*>(w + L.dig);
+  float* srow = inl ? nullptr : reinterpret_cast<float*>(w + L.srow);
+  if (zero_first) TB_CUDA(cudaMemsetAsync(z, 0, L.zeroed, st));
+  if (!inl) {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(3 * M)};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {kGvBK, (cuuint32_t)ND};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, dig, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TB_ERROR_NOT_SUPPORTED;
+    TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, nullptr, 0.f, st));
+  }
+  TB_TRY(inl ? set_gv_smem<true>() : set_gv_smem<false>());
+
+  GvArgs a{};
+  a.out = out;
+  a.x = x;
+  a.srow = srow;
+  a.scale = scale;
+  a.resid = resid;
+  a.acc = reinterpret_cast<int*>(z + L.acc);
+  a.count = reinterpret_cast<unsigned int*>(z + L.count);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ND = ND;
+  a.KB = KB;
+  a.total = total;
+  a.stages = stages;
+  a.err = wait_timeout_word();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(inl ? 320 : 192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (inl)
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true>, tw, tx, a));
+  else
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false>, tw, tx, a));
+  return TB_SUCCESS;
+}
+
+}  // namespace tb

@@ -157,6 +157,19 @@ tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const 
 tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, int planes, void* ws, cudaStream_t st);
 
+// gemv_tc.cu: the same product for 1 <= M <= kGemvTcMaxM on tcgen05 with the
+// weights as the 128-row MMA operand and the work split evenly over the SMs
+// by K blocks (split tiles finished by the last CTA to arrive).
+// `zeroed` (gemv_tc_zeroed_bytes) holds counters and split-tile sums and is
+// zero before and after each launch (zero_first: clear it first); `scratch`
+// (gemv_tc_scratch_bytes, 0 for M <= 8) holds the digit rows.
+constexpr int kGemvTcMaxM = 32;
+size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
+size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K);
+bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
+tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
+                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st);
+
 // gemm.cu: out[M, N] = x[M, K] @ (q * scale)^T (+ resid) on CUDA cores.
 tb_status_t gemm_simt_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
                          int M, int N, int K, int group, cudaStream_t st);

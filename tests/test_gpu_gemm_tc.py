@@ -102,3 +102,32 @@ def test_gemm_tc_per_group_takes_cuda_cores(oracle, be, cuda):
     _, q, s = oracle.quantize(w, g)
     got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(s, cuda), g))
     assert rel_err(got, oracle.dequant_matmul(x, q, s, g)) <= 1e-3
+
+
+# --- decode regime (1 <= M <= 32): the stream-K tcgen05 GEMV -----------------
+# (M, N, K): the microbench shapes, a down projection (K 11008), N tails (300:
+# one partial 128-row tile; 128: a single tile spread over many CTAs) and
+# several batch sizes.
+GEMV_SHAPES = [(1, 4096, 4096), (1, 11008, 4096), (1, 4096, 11008), (3, 300, 1024), (5, 128, 4096),
+               (8, 4096, 4096), (8, 11008, 4096), (17, 1408, 512), (32, 4096, 4096), (32, 11008, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMV_SHAPES)
+def test_gemv_tc_matches_oracle(oracle, be, cuda, M, N, K):
+    rng, x, q, s = _case(oracle, M, N, K, M * 131 + N + K)
+    got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(s, cuda), 0))
+    want = oracle.dequant_matmul(x, q, s, 0)
+    assert rel_err(got, want) <= TOL[0]
+
+
+def test_gemv_tc_split_tiles_are_deterministic(oracle, be, cuda):
+    """Tiles split over several CTAs are summed in integers: repeated calls
+    give identical bits."""
+    import torch
+
+    M, N, K = 4, 4096, 11008
+    _, x, q, s = _case(oracle, M, N, K, 9)
+    xd, qd, sd = _t(x, cuda), _t(q, cuda), _t(s, cuda)
+    a = be.DequantizeMatmul(xd, qd, sd, 0)
+    for _ in range(3):
+        assert torch.equal(a, be.DequantizeMatmul(xd, qd, sd, 0))

@@ -135,10 +135,11 @@ def test_argument_validation_needs_no_gpu(tb):
     assert L.tb_quantize_i8_f32(None, None, None, 4, 10, 3, None) == tb.TB_ERROR_INVALID_ARGUMENT
     assert L.tb_dequant_matmul_i8f32(None, None, None, None, -1, 4, 4, 0, None) == tb.TB_ERROR_INVALID_ARGUMENT
     assert L.tb_dequant_matmul_i8f32(None, None, None, None, 1, 4, 12, 5, None) == tb.TB_ERROR_INVALID_ARGUMENT
-    # the tensor-core GEMM's scratch: none for the GEMV, per-group or CUDA-core
-    # modes; digit rows + row scales otherwise; a short workspace is rejected
-    # before any launch
-    assert L.tb_dequant_matmul_workspace_size(32, 4096, 4096, 0, tb.TB_GEMM_I8X3) == 0
+    # the tensor-core paths' scratch: none for per-group or CUDA-core modes;
+    # digit rows + row scales (+ split-tile partial sums for M <= 32)
+    # otherwise; a short workspace is rejected before any launch
+    assert L.tb_dequant_matmul_workspace_size(32, 4096, 4096, 0, tb.TB_GEMM_I8X3) >= 3 * 32 * 4096 + 32 * 4
+    assert L.tb_dequant_matmul_workspace_size(1, 4096, 4000, 0, tb.TB_GEMM_I8X3) == 0  # K % 128: CUDA-core GEMV
     assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 128, tb.TB_GEMM_I8X3) == 0
     assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 0, tb.TB_GEMM_SIMT) == 0
     assert L.tb_dequant_matmul_workspace_size(33, 4096, 4096, 0, tb.TB_GEMM_I8X3) == 3 * 33 * 4096 + 33 * 4
