@@ -16,6 +16,16 @@ N > 1 runs N independent replicas (one process per GPU, no data-path
 collective): weak scaling.  `--impl reference` times the CPU restatement of
 tendo's path (the oracle) on the host cores for the same metric; under
 torchrun only rank 0 runs it.
+
+    python -m torch.distributed.run --nproc-per-node N bench.py --workload llama70b-tp --gpus N
+
+runs the Llama-70B shape tensor-parallel over the N ranks (N = 1 keeps the
+whole model on one GPU): 80 layers, d_model 8192, 64 query / 8 kv heads x
+128, SwiGLU 28672, vocab 32000, RoPE theta 5e5, batch 16, KV cache of 4096
+positions; one step = 32 greedy tokens per sequence from position 2048.  The
+2048-token prompts' KV state is left as zeros instead of prefilled (the
+decode kernels read the same bytes whatever they hold; a 70B prefill is not
+part of the decode metric), so this workload has no `e2e` or CPU leg.
 """
 from __future__ import annotations
 
@@ -48,6 +58,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
+    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "llama70b-tp"])
     return ap.parse_args()
 
 
@@ -409,9 +420,125 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Llama-70B shape, tensor parallel over the ranks
+# ---------------------------------------------------------------------------
+CFG70 = dict(vocab=32000, dim=8192, layers=80, heads=64, kv_heads=8, hidden=28672, max_seq=4096,
+             rope_base=500000.0, eps=1e-5)
+B70, PROMPT70, NEW70 = 16, 2048, 32
+METRIC70 = "int8 Llama-70B decode tok/s (batch 16, greedy, tensor parallel)"
+
+
+def step_bytes70(P):
+    """Algorithmic bytes of one decode step (16 tokens) of the whole model at
+    cache position P: int8 weights + scales, fp32 lm_head, the 16 sequences'
+    fp32 KV rows 0..P (summed over the tensor-parallel shards)."""
+    c = CFG70
+    d, H, Hkv, F, V, L = c["dim"], c["heads"], c["kv_heads"], c["hidden"], c["vocab"], c["layers"]
+    D = d // H
+    per_layer = (H + 2 * Hkv) * D * d + d * H * D + 2 * F * d + d * F
+    scales = (H + 2 * Hkv) * D + d + 2 * F + d
+    kv = 2 * Hkv * D * (P + 1) * 4 * B70
+    return L * (per_layer + 4 * scales + kv) + V * d * 4
+
+
+def run_70b_tp(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    import tendo_b200 as tb
+
+    comm = tb.Comm.from_process_group(local) if world > 1 else None
+    qm = tb.QuantizedModel(CFG70, batch=B70, device=local, comm=comm)
+    qm.init_synthetic(0)
+    stream = torch.cuda.ExternalStream(qm.stream_handle, device=dev)
+    start = tb.synth_tokens(B70, CFG70["vocab"], 11)
+
+    def step():
+        qm.set_position(PROMPT70)
+        qm.decode(NEW70, start_tokens=start)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    qm.sync()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    qm.sync()
+    barrier()
+    clk = clocks.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    toks = qm.tokens(NEW70 + 1)[:, 0]
+    tokens = args.steps * NEW70 * B70
+    value = tokens / (ms / 1000.0)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    ms_tok = ms / (args.steps * NEW70)
+    byts = statistics.mean(step_bytes70(PROMPT70 + i) for i in range(NEW70))
+    achieved = byts / (ms_tok / 1000.0) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC70, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": "llama70b-int8-tp-decode: 80 layers, d_model 8192, 64/8 heads x 128 (GQA), SwiGLU "
+                                   "28672, vocab 32000; batch 16; decode from position 2048 (prompt KV zeros); "
+                                   "32 greedy tokens per step; KV 4096 positions",
+                       "global_batch": B70, "seq_len": PROMPT70 + NEW70, "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2: 68 GB int8 weights + 21 GB KV per step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak * world, "unit": "GB/s",
+                         "frac": achieved / (hbm_peak * world), "traffic": None, "kernel": "whole decode step",
+                         "bytes_per_token_step": byts, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clk, "first_tokens": toks[:8].tolist(),
+            "note": "no e2e or CPU leg for this workload: see the module docstring",
+        }
+        print(json.dumps(line), flush=True)
+    qm.close()
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.workload == "llama70b-tp":
+        if args.impl == "reference":
+            if dist_env()[0] == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the 70B shape's CPU restatement needs "
+                                  "about 70 GB of host weights and minutes per token; the reference arm runs on the "
+                                  "default 7B workload"}), flush=True)
+            return
+        run_70b_tp(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

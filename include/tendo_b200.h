@@ -246,6 +246,35 @@ typedef struct tb_model tb_model;
 
 /* Allocates weights, KV cache and work buffers on `device`. */
 TB_API tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device);
+
+/* ---------------------------------------------------------------------------
+ * Tensor parallelism (the 70B shape over 2/4/8 GPUs)
+ * ------------------------------------------------------------------------- */
+
+/* A communicator over the ranks of one tensor-parallel group, one process (or
+ * thread) per GPU: NCCL, loaded at run time (libnccl.so.2).  Rank 0 makes the
+ * unique id, the caller distributes its bytes to every rank (any channel),
+ * and each rank creates its communicator with it.  The tb_comm_init /
+ * tb_allreduce_sum_f32 pair planned for the reference's cgo layer. */
+typedef struct tb_comm tb_comm;
+TB_API size_t tb_comm_unique_id_bytes(void);
+TB_API tb_status_t tb_comm_unique_id(void* id_out, size_t bytes);
+TB_API tb_status_t tb_comm_create(tb_comm** out, const void* id, size_t bytes, int rank, int nranks, int device);
+TB_API tb_status_t tb_comm_destroy(tb_comm* comm);
+/* In-place sum over the ranks on `stream` (ncclAllReduce, fp32). */
+TB_API tb_status_t tb_allreduce_sum_f32(tb_comm* comm, float* buf, int64_t n, tb_stream_t stream);
+
+/* The model's share on rank r of a tensor-parallel group of `nranks` GPUs
+ * (models/llama/quantized.go layers, sharded Megatron-style): column-parallel
+ * Wq/Wk/Wv (heads r H/n .. (r+1) H/n, kv heads likewise), Wgate/Wup (rows
+ * r F/n ..) and the fp32 lm_head (vocabulary rows r V/n ..); row-parallel Wo
+ * and Wdown (their input columns), followed by an allreduce of the residual
+ * stream; embedding and norms replicated.  Greedy tokens come from an
+ * allreduce (max) of packed (logit, index) keys, lowest index on ties as
+ * models/sampling.go:73-83.  Needs heads, kv_heads, hidden and vocab
+ * divisible by nranks.  Every rank calls the same model functions in the
+ * same order. */
+TB_API tb_status_t tb_model_create_tp(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm);
 TB_API tb_status_t tb_model_destroy(tb_model* m);
 /* Synthetic weights: N(0, 0.02) from (seed, stream = layer * 8 + matrix),
  * quantized per channel on the device; gains 1.0; embedding and lm_head fp32. */

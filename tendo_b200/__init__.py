@@ -67,6 +67,12 @@ SIGNATURES = [
      [_vp, _vp, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, _vp]),
     ("tb_synth_tokens_host", _st, [_vp, _i64, _i64, ctypes.c_uint64]),
     ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
+    ("tb_model_create_tp", _st, [_vp, _vp, ctypes.c_int, _vp]),
+    ("tb_comm_unique_id_bytes", ctypes.c_size_t, []),
+    ("tb_comm_unique_id", _st, [_vp, ctypes.c_size_t]),
+    ("tb_comm_create", _st, [_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("tb_comm_destroy", _st, [_vp]),
+    ("tb_allreduce_sum_f32", _st, [_vp, _vp, _i64, _vp]),
     ("tb_model_destroy", _st, [_vp]),
     ("tb_model_init_synthetic", _st, [_vp, ctypes.c_uint64]),
     ("tb_model_set_linear", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
@@ -397,17 +403,62 @@ class ModelConfig(ctypes.Structure):
     ]
 
 
-class QuantizedModel:
-    """QuantizedModel (models/llama/quantized.go) on one GPU, B sequences in lockstep."""
+class Comm:
+    """A tensor-parallel communicator (tb_comm_*: NCCL), one per rank.
 
-    def __init__(self, cfg: dict, batch: int = 1, device: int = 0):
+    ``Comm.from_process_group(device)`` builds it over an initialised
+    torch.distributed group: rank 0 makes the unique id and the group
+    broadcasts it (any backend, gloo included)."""
+
+    def __init__(self, uid: bytes, rank: int, nranks: int, device: int):
+        self.rank, self.nranks, self.device = rank, nranks, device
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(uid, len(uid))
+        check(lib.tb_comm_create(ctypes.byref(h), buf, len(uid), rank, nranks, device))
+        self.h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        n = int(lib.tb_comm_unique_id_bytes())
+        buf = ctypes.create_string_buffer(n)
+        check(lib.tb_comm_unique_id(buf, n))
+        return buf.raw
+
+    @classmethod
+    def from_process_group(cls, device: int):
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(), dist.get_world_size()
+        obj = [cls.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return cls(obj[0], rank, world, device)
+
+    def allreduce_sum(self, t, stream=None):
+        """In-place fp32 sum over the ranks (tb_allreduce_sum_f32)."""
+        check(lib.tb_allreduce_sum_f32(self.h, _ptr(t), t.numel(), _stream(stream)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib.tb_comm_destroy(self.h)
+            self.h = None
+
+
+class QuantizedModel:
+    """QuantizedModel (models/llama/quantized.go) on one GPU, B sequences in
+    lockstep; with ``comm``, this rank's tensor-parallel share of it."""
+
+    def __init__(self, cfg: dict, batch: int = 1, device: int = 0, comm: "Comm | None" = None):
         self.cfg = dict(cfg)
         self.B = batch
         self.device = device
+        self.comm = comm
         c = ModelConfig(cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"],
                         cfg["max_seq"], cfg["rope_base"], cfg["eps"], batch)
         h = ctypes.c_void_p()
-        check(lib.tb_model_create(ctypes.byref(h), ctypes.byref(c), device))
+        if comm is None:
+            check(lib.tb_model_create(ctypes.byref(h), ctypes.byref(c), device))
+        else:
+            check(lib.tb_model_create_tp(ctypes.byref(h), ctypes.byref(c), device, comm.h))
         self.h = h
 
     def close(self):

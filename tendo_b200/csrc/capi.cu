@@ -21,6 +21,11 @@ tb_status_t cuda_fail(cudaError_t e, const char* where) {
   return TB_ERROR_CUDA;
 }
 
+tb_status_t fail_message(const char* msg) {
+  g_last_cuda_error = msg;
+  return TB_ERROR_CUDA;
+}
+
 tb_status_t check_launch(const char* where) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, where);

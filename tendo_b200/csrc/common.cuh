@@ -12,6 +12,8 @@ namespace tb {
 // Records the CUDA error text for tb_get_last_cuda_error_string() and maps
 // the error onto a status.
 tb_status_t cuda_fail(cudaError_t e, const char* where);
+// Records `msg` as the last error text (tb_get_last_cuda_error_string) and returns TB_ERROR_CUDA.
+tb_status_t fail_message(const char* msg);
 
 // Status of the launch just issued (cudaGetLastError).
 tb_status_t check_launch(const char* where);

@@ -53,6 +53,10 @@ struct tb_model {
   unsigned int* head_done = nullptr;
   int* err_word = nullptr;
   uint64_t* trace = nullptr;  // [2 + 2 * (1 + 5 L + 1)] phase stamps of the last decode step
+  tb_comm* comm = nullptr;    // tensor-parallel group (null: the whole model on one GPU)
+  int tp = 1, tp_rank = 0;
+  int64_t Hg = 0, Hkvg = 0, Fg = 0, Vg = 0;  // unsharded heads, kv heads, hidden, vocabulary
+  int64_t v0 = 0;                            // vocabulary index of this rank's first lm_head row
   int8_t* tcdig = nullptr;    // digit rows of the prefill projections' activations (tcgen05 GEMM)
   float* tcs = nullptr;       // their row scales
   int trace_n = 0;
@@ -179,16 +183,21 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
       TB_TRY(tb::attn_prefill(m->attn, m->g, kcl, vcl, (int)m->B, (int)m->H, (int)m->Hkv, (int)S, P + S, (int)m->D,
                               (int)m->Ms, scale, st));
     }
-    // o projection + residual
+    // o projection + residual; row-parallel under tensor parallelism: each
+    // rank's partial product, the residual on rank 0 only, summed over ranks
+    const float* resid = m->tp_rank == 0 ? m->h : nullptr;
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, 0, (tb_stream_t)st));
+      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
       const int HD = (int)(m->H * m->D);
       TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->attn, (int)rows, HD, kTcPlanes, nullptr, 0.f, st));
-      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wo, so, m->h, (int)rows, (int)m->d, HD, kTcPlanes, st));
+      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wo, so, resid, (int)rows, (int)m->d, HD, kTcPlanes, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
     } else {
-      TB_TRY(tb::gemm_simt_i8(m->h, m->attn, wo, so, m->h, (int)rows, (int)m->d, (int)(m->H * m->D), 0, st));
+      TB_TRY(tb::gemm_simt_i8(m->h, m->attn, wo, so, resid, (int)rows, (int)m->d, (int)(m->H * m->D), 0, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
     }
     // MLP block (models/llama/quantized.go:206-219, :385-417)
     if (tc) {
@@ -204,12 +213,15 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     TB_TRY(tb::silu_mul(m->g, m->g, m->u, rows * m->F, st));
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, 0, (tb_stream_t)st));
+      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
       TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->g, (int)rows, (int)m->F, kTcPlanes, nullptr, 0.f, st));
-      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, kTcPlanes, st));
+      TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wd, sd, resid, (int)rows, (int)m->d, (int)m->F, kTcPlanes, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
     } else {
-      TB_TRY(tb::gemm_simt_i8(m->h, m->g, wd, sd, m->h, (int)rows, (int)m->d, (int)m->F, 0, st));
+      TB_TRY(tb::gemm_simt_i8(m->h, m->g, wd, sd, resid, (int)rows, (int)m->d, (int)m->F, 0, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
     }
   }
   return TB_SUCCESS;
@@ -222,6 +234,9 @@ tb_status_t finish_logits(tb_model* m, int64_t S) {
   // gather the last rows: h[b * S + S - 1] -> last[b]
   TB_CUDA(cudaMemcpy2DAsync(m->last, sizeof(float) * m->d, m->h + (S - 1) * m->d, sizeof(float) * m->d * S,
                             sizeof(float) * m->d, m->B, cudaMemcpyDeviceToDevice, st));
+  // greedy keys of this rank's vocabulary rows, max over the ranks, then the
+  // tail kernel turns them into tokens (it advances the position by one:
+  // pre-compensate)
   if (m->B <= 8 && tb::gemv_smem_bytes(8, (int)m->d) <= 200 * 1024) {
     tb::LmHeadArgs a{};
     a.h = m->last;
@@ -233,22 +248,18 @@ tb_status_t finish_logits(tb_model* m, int64_t S) {
     a.M = (int)m->B;
     a.d = (int)m->d;
     a.V = (int)m->V;
+    a.v0 = (int)m->v0;
     a.l2_prefetch = tb::l2_prefetch_enabled();
     TB_TRY(tb::gemv_lmhead(a, st, false));
-    // the tail kernel advances the position by one; pre-compensate
-    int64_t p = m->host_pos - 1;
-    TB_CUDA(cudaMemcpyAsync(m->pos, &p, sizeof(int64_t), cudaMemcpyHostToDevice, st));
-    TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, st, false));
   } else {
     TB_TRY(tb::rmsnorm(m->xn, nullptr, m->last, nullptr, m->final_norm, m->B, m->d, m->c.eps, st));
     TB_TRY(tb::gemm_f32_nt(m->logits, m->xn, m->lm_head, (int)m->B, (int)m->V, (int)m->d, st));
-    TB_TRY(tb::argmax_rows(m->tokens, m->logits, m->B, m->V, st));
-    if (m->host_step < m->hist_cap)
-      TB_CUDA(cudaMemcpyAsync(m->history + m->host_step * m->B, m->tokens, sizeof(int64_t) * m->B,
-                              cudaMemcpyDeviceToDevice, st));
-    int64_t s1 = m->host_step + 1;
-    TB_CUDA(cudaMemcpyAsync(m->step, &s1, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    TB_TRY(tb::argmax_keys(m->keys, m->logits, m->B, m->V, m->v0, st));
   }
+  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, st));
+  int64_t p = m->host_pos - 1;
+  TB_CUDA(cudaMemcpyAsync(m->pos, &p, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+  TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, st, false));
   m->host_step += 1;
   // cudaMemcpyAsync from pageable host memory is staged before returning, so
   // the stack values above may go out of scope; keep the stream ordered.
@@ -263,7 +274,7 @@ tb_status_t forward_tokens(tb_model* m, int64_t S) {
     const int64_t sc = S - s0 < m->chunk_s ? S - s0 : m->chunk_s;
     // embed rows b * sc + s of this chunk
     for (int64_t b = 0; b < m->B; b++)
-      TB_TRY(tb::embedding(m->h + b * sc * m->d, m->embed, m->ids + b * S + s0, sc, m->V, m->d, m->bad, st, false));
+      TB_TRY(tb::embedding(m->h + b * sc * m->d, m->embed, m->ids + b * S + s0, sc, m->Vg, m->d, m->bad, st, false));
     TB_TRY(forward_layers(m, sc));
     m->host_pos += sc;
     if (s0 + sc >= S) TB_TRY(finish_logits(m, sc));
@@ -303,7 +314,19 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     qa.Hkv = (int)m->Hkv;
     qa.D = (int)m->D;
     qa.max_seq = (int)m->Ms;
-    if (kind == 0) return tb::gemv_qkv_rope(qa, st, pdl);
+    if (kind == 0) {
+      // the fused kernels take up to 8 sequences: larger batches run in groups
+      for (int64_t b0 = 0; b0 < m->B; b0 += 8) {
+        tb::QkvArgs g = qa;
+        g.h = m->h + b0 * m->d;
+        g.qout = m->qbuf + b0 * m->H * m->D;
+        g.kcache = kcl + b0 * m->Hkv * m->Ms * m->D;
+        g.vcache = vcl + b0 * m->Hkv * m->Ms * m->D;
+        g.M = (int)(m->B - b0 < 8 ? m->B - b0 : 8);
+        TB_TRY(tb::gemv_qkv_rope(g, st, pdl));
+      }
+      return TB_SUCCESS;
+    }
     tb::AttnDecodeArgs aa{};
     aa.q = m->qbuf;
     aa.kcache = kcl;
@@ -319,8 +342,11 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     aa.nsplit = m->nsplit;
     aa.scale = scale;
     if (kind == 1) return tb::attn_decode(aa, st, pdl);
+    // row-parallel under tensor parallelism: the residual joins on rank 0 and
+    // the step sums the ranks' partial products after the kernel
+    const float* resid = m->tp_rank == 0 ? m->h : nullptr;
     if (kind == 2)
-      return tb::gemv_plain(m->h, m->attn, wo, so, m->h, (int)m->B, (int)m->d, (int)(m->H * m->D), nullptr, 0.f, st,
+      return tb::gemv_plain(m->h, m->attn, wo, so, resid, (int)m->B, (int)m->d, (int)(m->H * m->D), nullptr, 0.f, st,
                             pdl);
     tb::GateUpArgs ga{};
     ga.h = m->h;
@@ -334,9 +360,18 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     ga.M = (int)m->B;
     ga.d = (int)m->d;
     ga.F = (int)m->F;
-    if (kind == 3) return tb::gemv_gateup(ga, st, pdl);
+    if (kind == 3) {
+      for (int64_t b0 = 0; b0 < m->B; b0 += 8) {
+        tb::GateUpArgs g = ga;
+        g.h = m->h + b0 * m->d;
+        g.act = m->g + b0 * m->F;
+        g.M = (int)(m->B - b0 < 8 ? m->B - b0 : 8);
+        TB_TRY(tb::gemv_gateup(g, st, pdl));
+      }
+      return TB_SUCCESS;
+    }
     if (kind == 4)
-      return tb::gemv_plain(m->h, m->g, wd, sd, m->h, (int)m->B, (int)m->d, (int)m->F, nullptr, 0.f, st, pdl);
+      return tb::gemv_plain(m->h, m->g, wd, sd, resid, (int)m->B, (int)m->d, (int)m->F, nullptr, 0.f, st, pdl);
   }
   tb::LmHeadArgs la{};
   la.h = m->h;
@@ -348,18 +383,34 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
   la.M = (int)m->B;
   la.d = (int)m->d;
   la.V = (int)m->V;
+  la.v0 = (int)m->v0;
   la.l2_prefetch = tb::l2_prefetch_enabled();
-  if (kind == 5) return tb::gemv_lmhead(la, st, pdl);
+  if (kind == 5) {
+    for (int64_t b0 = 0; b0 < m->B; b0 += 8) {
+      tb::LmHeadArgs g = la;
+      g.h = m->h + b0 * m->d;
+      g.logits = m->logits + b0 * m->V;
+      g.argmax_keys = m->keys + b0;
+      g.M = (int)(m->B - b0 < 8 ? m->B - b0 : 8);
+      TB_TRY(tb::gemv_lmhead(g, st, pdl));
+    }
+    return TB_SUCCESS;
+  }
   return TB_ERROR_INVALID_ARGUMENT;
 }
 
 // One fused decode step (graph body).
 tb_status_t decode_step_fused(tb_model* m) {
   const bool pdl = m->pdl;
-  TB_TRY(tb::embedding(m->h, m->embed, m->tokens, m->B, m->V, m->d, m->bad, m->stream, pdl));
+  TB_TRY(tb::embedding(m->h, m->embed, m->tokens, m->B, m->Vg, m->d, m->bad, m->stream, pdl));
   for (int64_t l = 0; l < m->L; l++)
-    for (int kind = 0; kind < 5; kind++) TB_TRY(decode_kernel(m, kind, l, pdl));
+    for (int kind = 0; kind < 5; kind++) {
+      TB_TRY(decode_kernel(m, kind, l, pdl));
+      // tensor parallelism: sum the row-parallel o / down partial products
+      if (kind == 2 || kind == 4) TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(m->B * m->d), false, m->stream));
+    }
   TB_TRY(decode_kernel(m, 5, 0, pdl));
+  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, m->stream));
   TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, m->stream, pdl));
   return TB_SUCCESS;
 }
@@ -438,25 +489,36 @@ tb_status_t build_graph(tb_model* m) {
 
 }  // namespace
 
-extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device) {
-  TB_INJECT("tb_model_create");
+namespace {
+
+tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm) {
   TB_REQUIRE(out && cfg);
   *out = nullptr;
   TB_REQUIRE(cfg->vocab > 0 && cfg->dim > 0 && cfg->layers > 0 && cfg->heads > 0 && cfg->kv_heads > 0);
   TB_REQUIRE(cfg->dim % cfg->heads == 0 && cfg->heads % cfg->kv_heads == 0 && cfg->hidden > 0);
   TB_REQUIRE(cfg->max_seq > 0 && cfg->max_batch > 0);
   TB_REQUIRE((cfg->dim / cfg->heads) % 2 == 0);
+  const int tp = tb::comm_size(comm), rank = tb::comm_rank(comm);
+  TB_REQUIRE(cfg->heads % tp == 0 && cfg->kv_heads % tp == 0 && cfg->hidden % tp == 0 && cfg->vocab % tp == 0);
   DeviceGuard guard(device);
   TB_CUDA(cudaSetDevice(device));
   tb_model* m = new tb_model();
   m->c = *cfg;
   m->device = device;
+  m->comm = comm;
+  m->tp = tp;
+  m->tp_rank = rank;
+  m->Hg = cfg->heads;
+  m->Hkvg = cfg->kv_heads;
+  m->Fg = cfg->hidden;
+  m->Vg = cfg->vocab;
   m->d = cfg->dim;
-  m->H = cfg->heads;
-  m->Hkv = cfg->kv_heads;
+  m->H = cfg->heads / tp;
+  m->Hkv = cfg->kv_heads / tp;
   m->D = cfg->dim / cfg->heads;
-  m->F = cfg->hidden;
-  m->V = cfg->vocab;
+  m->F = cfg->hidden / tp;
+  m->V = cfg->vocab / tp;
+  m->v0 = (int64_t)rank * m->V;
   m->L = cfg->layers;
   m->Ms = cfg->max_seq;
   m->B = cfg->max_batch;
@@ -466,7 +528,7 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   if (m->chunk_s > m->Ms) m->chunk_s = m->Ms;
   m->rows_max = m->B * m->chunk_s;
   const size_t fused_smem = tb::gemv_smem_bytes(m->B <= 1 ? 1 : (m->B <= 2 ? 2 : (m->B <= 4 ? 4 : 8)), (int)m->d);
-  m->fused = m->B <= 8 && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
+  m->fused = m->B <= 16 && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
              (m->D == 64 || m->D == 128) && (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 ||
                                              m->H / m->Hkv == 8);
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
@@ -474,7 +536,7 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);
   {
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
-    m->mk = !(e && e[0] == '0') &&
+    m->mk = !(e && e[0] == '0') && tp == 1 &&
             tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
     int ns = tb::sm_count() / (int)m->Hkv;  // about one attention unit per SM
     if (ns < 1) ns = 1;
@@ -500,7 +562,7 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   A(dalloc(m, &m->attn_norm, L * m->d));
   A(dalloc(m, &m->mlp_norm, L * m->d));
   A(dalloc(m, &m->final_norm, (size_t)m->d));
-  A(dalloc(m, &m->embed, (size_t)m->V * m->d));
+  A(dalloc(m, &m->embed, (size_t)m->Vg * m->d));
   A(dalloc(m, &m->lm_head, (size_t)m->V * m->d));
   A(dalloc(m, &m->cos_t, (size_t)m->Ms * (m->D / 2)));
   A(dalloc(m, &m->sin_t, (size_t)m->Ms * (m->D / 2)));
@@ -566,6 +628,19 @@ extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cf
   return TB_SUCCESS;
 }
 
+}  // namespace
+
+extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device) {
+  TB_INJECT("tb_model_create");
+  return create_model(out, cfg, device, nullptr);
+}
+
+extern "C" tb_status_t tb_model_create_tp(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm) {
+  TB_INJECT("tb_model_create");
+  TB_REQUIRE(comm);
+  return create_model(out, cfg, device, comm);
+}
+
 extern "C" tb_status_t tb_model_destroy(tb_model* m) {
   if (!m) return TB_SUCCESS;
   DeviceGuard guard(m->device);
@@ -584,17 +659,32 @@ extern "C" tb_status_t tb_model_init_synthetic(tb_model* m, uint64_t seed) {
   TB_REQUIRE(m);
   DeviceGuard guard(m->device);
   tb_stream_t st = (tb_stream_t)m->stream;
+  // every rank draws its shard with the unsharded element indices, so the
+  // sharded model is the same model (column-parallel: rows row0..; row-
+  // parallel: columns col0.. of full rows, scales over the full row)
+  const int64_t r = m->tp_rank;
   for (int l = 0; l < m->L; l++) {
     for (int mat = 0; mat < 7; mat++) {
       int8_t* q;
       float* s;
       lin_ptr(m, l, mat, &q, &s);
-      TB_TRY(tb_synth_quantized_i8(q, s, (int64_t)lin_rows(m, mat), (int64_t)lin_cols(m, mat), seed,
-                                   (uint64_t)l * TS_MATS + (uint64_t)mat, 0.02, st));
+      const int64_t rows = (int64_t)lin_rows(m, mat), cols = (int64_t)lin_cols(m, mat);
+      int64_t row0 = 0, col0 = 0, K = cols;
+      switch (mat) {
+        case 0: row0 = r * m->H * m->D; break;
+        case 1:
+        case 2: row0 = r * m->Hkv * m->D; break;
+        case 3: col0 = r * m->H * m->D; K = m->Hg * m->D; break;
+        case 4:
+        case 5: row0 = r * m->F; break;
+        default: col0 = r * m->F; K = m->Fg; break;
+      }
+      TB_TRY(tb::synth_quant_shard(q, s, rows, K, row0, col0, cols, seed, (uint64_t)l * TS_MATS + (uint64_t)mat, 0.02,
+                                   m->stream));
     }
   }
-  TB_TRY(tb_synth_normal_f32(m->embed, m->V, m->d, seed, 0x7fff0001ull, 0.02, st));
-  TB_TRY(tb_synth_normal_f32(m->lm_head, m->V, m->d, seed, 0x7fff0002ull, 0.02, st));
+  TB_TRY(tb_synth_normal_f32(m->embed, m->Vg, m->d, seed, 0x7fff0001ull, 0.02, st));
+  TB_TRY(tb::synth_normal_rows(m->lm_head, m->V, m->d, m->v0, seed, 0x7fff0002ull, 0.02, m->stream));
   fill_kernel<<<256, 256, 0, m->stream>>>(m->attn_norm, m->L * m->d, 1.0f);
   fill_kernel<<<256, 256, 0, m->stream>>>(m->mlp_norm, m->L * m->d, 1.0f);
   fill_kernel<<<16, 256, 0, m->stream>>>(m->final_norm, m->d, 1.0f);
@@ -633,7 +723,7 @@ extern "C" tb_status_t tb_model_set_tensor(tb_model* m, int which, int layer, co
   float* dst = nullptr;
   size_t n = 0;
   switch (which) {
-    case 0: dst = m->embed; n = (size_t)m->V * m->d; break;
+    case 0: dst = m->embed; n = (size_t)m->Vg * m->d; break;
     case 1: dst = m->lm_head; n = (size_t)m->V * m->d; break;
     case 2: dst = m->final_norm; n = (size_t)m->d; break;
     case 3: TB_REQUIRE(layer >= 0 && layer < m->L); dst = m->attn_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
@@ -649,7 +739,7 @@ extern "C" tb_status_t tb_model_get_tensor(tb_model* m, int which, int layer, fl
   const float* src = nullptr;
   size_t n = 0;
   switch (which) {
-    case 0: src = m->embed; n = (size_t)m->V * m->d; break;
+    case 0: src = m->embed; n = (size_t)m->Vg * m->d; break;
     case 1: src = m->lm_head; n = (size_t)m->V * m->d; break;
     case 2: src = m->final_norm; n = (size_t)m->d; break;
     case 3: TB_REQUIRE(layer >= 0 && layer < m->L); src = m->attn_norm + (size_t)layer * m->d; n = (size_t)m->d; break;
@@ -751,7 +841,7 @@ extern "C" tb_status_t tb_model_forward(tb_model* m, const int64_t* tokens_host,
   TB_REQUIRE(m && tokens_host && B == m->B && S >= 1);
   TB_REQUIRE(m->host_pos + S <= m->Ms);  // nn/rope.go:109-111
   DeviceGuard guard(m->device);
-  for (int64_t i = 0; i < B * S; i++) TB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->V);
+  for (int64_t i = 0; i < B * S; i++) TB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->Vg);
   TB_CUDA(cudaMemcpyAsync(m->ids, tokens_host, sizeof(int64_t) * B * S, cudaMemcpyHostToDevice, m->stream));
   TB_TRY(forward_tokens(m, S));
   if (last_logits_host)
@@ -768,7 +858,7 @@ extern "C" tb_status_t tb_model_decode(tb_model* m, const int64_t* start_tokens_
   TB_REQUIRE(m->host_pos + n_steps <= m->Ms);
   DeviceGuard guard(m->device);
   if (start_tokens_host) {
-    for (int64_t i = 0; i < m->B; i++) TB_REQUIRE(start_tokens_host[i] >= 0 && start_tokens_host[i] < m->V);
+    for (int64_t i = 0; i < m->B; i++) TB_REQUIRE(start_tokens_host[i] >= 0 && start_tokens_host[i] < m->Vg);
     TB_CUDA(cudaMemcpyAsync(m->tokens, start_tokens_host, sizeof(int64_t) * m->B, cudaMemcpyHostToDevice, m->stream));
     TB_CUDA(cudaStreamSynchronize(m->stream));
   }

@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_lmhead_kernel(LmHeadArgs a)
       for (int m = 0; m < MT; m++) {
         if (m >= a.M) continue;
         if (lane == m && a.logits) a.logits[(size_t)m * N + n] = acc[r][m];
-        const unsigned long long k = argmax_key(acc[r][m], n);
+        const unsigned long long k = argmax_key(acc[r][m], n + a.v0);
         best[m] = k > best[m] ? k : best[m];
       }
     }

@@ -43,6 +43,7 @@ struct LmHeadArgs {
   float* logits;   // [M, V] (may be null)
   unsigned long long* argmax_keys;  // [M] (may be null)
   int M, d, V;
+  int v0;  // vocabulary index of row 0 (tensor-parallel shards)
   bool l2_prefetch;
 };
 
@@ -170,10 +171,23 @@ bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st);
 
+// comm.cu: in-place NCCL allreduce on `st` (fp32 sum, or uint64 max for the
+// packed greedy keys); a no-op without a communicator or with one rank.
+tb_status_t allreduce(tb_comm* c, void* buf, size_t count, bool u64_max, cudaStream_t st);
+int comm_rank(const tb_comm* c);
+int comm_size(const tb_comm* c);
+
 // gemm.cu: out[M, N] = x[M, K] @ (q * scale)^T (+ resid) on CUDA cores.
 tb_status_t gemm_simt_i8(float* out, const float* x, const int8_t* q, const float* scale, const float* resid,
                          int M, int N, int K, int group, cudaStream_t st);
 tb_status_t gemm_f32_nt(float* out, const float* a, const float* b, int M, int N, int K, cudaStream_t st);
+
+// quant.cu: shards of the synthetic weights (tensor parallelism): rows
+// row0.. of a K-column matrix (scales over the full row), columns col0..col0+cols.
+tb_status_t synth_quant_shard(int8_t* q, float* scale, int64_t rows, int64_t K, int64_t row0, int64_t col0,
+                              int64_t cols, uint64_t seed, uint64_t stream_id, double std_, cudaStream_t st);
+tb_status_t synth_normal_rows(float* w, int64_t rows, int64_t K, int64_t row0, uint64_t seed, uint64_t stream_id,
+                              double std_, cudaStream_t st);
 
 // ops.cu
 tb_status_t embedding(float* out, const float* table, const int64_t* ids, int64_t n, int64_t vocab, int64_t dim,
@@ -187,6 +201,10 @@ tb_status_t rope_rows(float* x, const float* cos_t, const float* sin_t, int64_t 
                       int64_t pos, int64_t ld, cudaStream_t st);
 tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, cudaStream_t st);
 tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st);
+// keys[r] = max(keys[r], packed (x[r][j], v0 + j)) over the row: the greedy
+// choice as one orderable word (larger logit first, lower index on ties).
+tb_status_t argmax_keys(unsigned long long* keys, const float* x, int64_t rows, int64_t n, int64_t v0,
+                        cudaStream_t st);
 // Decode-step tail: token[m] from the argmax key, history append, key reset, position + 1.
 tb_status_t finish_step(unsigned long long* keys, int64_t* tokens, int64_t* history, int64_t* step, int64_t* pos,
                         int M, int64_t hist_cap, cudaStream_t st, bool pdl);

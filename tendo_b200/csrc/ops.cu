@@ -125,6 +125,37 @@ __global__ void add_kernel(float* out, const float* a, const float* b, int64_t n
 }
 
 // One CTA per row; first index of the maximum (strict >, models/sampling.go:73-83).
+// Greedy choice of a row as one orderable word: the logit's bits mapped to
+// an order-preserving unsigned, then 2^32 - 1 - index, so the max over
+// words is the largest logit with the lowest index on ties
+// (models/sampling.go:73-83).
+__device__ __forceinline__ unsigned long long packed_key(float v, int64_t idx) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+__global__ void argmax_keys_kernel(unsigned long long* keys, const float* x, int64_t n, int64_t v0) {
+  __shared__ unsigned long long bk[8];
+  const float* r = x + blockIdx.x * n;
+  unsigned long long best = 0ull;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = packed_key(r[i], v0 + i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ok > best ? ok : best;
+  }
+  if ((threadIdx.x & 31) == 0) bk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = bk[w] > best ? bk[w] : best;
+    atomicMax(keys + blockIdx.x, best);
+  }
+}
+
 __global__ void argmax_kernel(int64_t* out, const float* x, int64_t n) {
   __shared__ float bv[32];
   __shared__ int64_t bi[32];
@@ -238,6 +269,14 @@ tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, c
   TB_REQUIRE(rows <= 0x7fffffff && n > 0);
   argmax_kernel<<<(unsigned)rows, 256, 0, st>>>(out, x, n);
   return check_launch("argmax_kernel");
+}
+
+tb_status_t argmax_keys(unsigned long long* keys, const float* x, int64_t rows, int64_t n, int64_t v0,
+                        cudaStream_t st) {
+  if (rows == 0) return TB_SUCCESS;
+  TB_REQUIRE(rows <= 0x7fffffff && n > 0 && v0 >= 0 && v0 + n <= 0x7fffffff);
+  argmax_keys_kernel<<<(unsigned)rows, 256, 0, st>>>(keys, x, n, v0);
+  return check_launch("argmax_keys_kernel");
 }
 
 tb_status_t finish_step(unsigned long long* keys, int64_t* tokens, int64_t* history, int64_t* step, int64_t* pos,

@@ -90,6 +90,32 @@ __global__ void __launch_bounds__(kQuantThreads) synth_quant_kernel(int8_t* __re
   for (int64_t i = threadIdx.x; i < K; i += kQuantThreads) q[n * K + i] = quant_one(ts_normal_f32(key, base + i, std_), s);
 }
 
+// A shard of a synthetic quantized matrix: local row n is global row
+// row0 + n, drawn over all K columns (the per-channel scale needs the whole
+// row) with the same element indices as the unsharded draw; columns
+// [col0, col0 + cols) are kept.
+__global__ void __launch_bounds__(kQuantThreads) synth_quant_shard_kernel(int8_t* __restrict__ q,
+                                                                          float* __restrict__ scale, int64_t K,
+                                                                          int64_t row0, int64_t col0, int64_t cols,
+                                                                          uint64_t key, double std_) {
+  __shared__ float red[kQuantThreads / 32];
+  const int64_t n = blockIdx.x;
+  const uint64_t base = (uint64_t)((row0 + n) * K);
+  float m = 0.0f;
+  for (int64_t i = threadIdx.x; i < K; i += kQuantThreads) m = fmaxf(m, fabsf(ts_normal_f32(key, base + i, std_)));
+  m = block_max_256(m, red);
+  const float s = scale_of(m);
+  if (threadIdx.x == 0) scale[n] = s;
+  for (int64_t i = threadIdx.x; i < cols; i += kQuantThreads)
+    q[n * cols + i] = quant_one(ts_normal_f32(key, base + col0 + i, std_), s);
+}
+
+__global__ void synth_normal_offset_kernel(float* __restrict__ w, int64_t total, uint64_t first, uint64_t key,
+                                           double std_) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    w[i] = ts_normal_f32(key, first + (uint64_t)i, std_);
+}
+
 unsigned grid_for(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
   int64_t cap = (int64_t)tb::sm_count() * 16;
@@ -156,6 +182,26 @@ extern "C" tb_status_t tb_synth_quantized_i8(int8_t* q, float* scale, int64_t N,
                                                                                std_);
   return tb::check_launch("synth_quant_kernel");
 }
+
+namespace tb {
+
+tb_status_t synth_quant_shard(int8_t* q, float* scale, int64_t rows, int64_t K, int64_t row0, int64_t col0,
+                              int64_t cols, uint64_t seed, uint64_t stream_id, double std_, cudaStream_t st) {
+  if (rows == 0) return TB_SUCCESS;
+  synth_quant_shard_kernel<<<(unsigned)rows, kQuantThreads, 0, st>>>(q, scale, K, row0, col0, cols,
+                                                                      ts_key(seed, stream_id), std_);
+  return check_launch("synth_quant_shard_kernel");
+}
+
+tb_status_t synth_normal_rows(float* w, int64_t rows, int64_t K, int64_t row0, uint64_t seed, uint64_t stream_id,
+                              double std_, cudaStream_t st) {
+  if (rows * K == 0) return TB_SUCCESS;
+  synth_normal_offset_kernel<<<grid_for(rows * K, 256), 256, 0, st>>>(w, rows * K, (uint64_t)(row0 * K),
+                                                                      ts_key(seed, stream_id), std_);
+  return check_launch("synth_normal_offset_kernel");
+}
+
+}  // namespace tb
 
 extern "C" tb_status_t tb_synth_tokens_host(int64_t* ids, int64_t n, int64_t vocab, uint64_t seed) {
   TB_REQUIRE(n >= 0 && vocab > 0 && vocab <= 0xffffffffLL);

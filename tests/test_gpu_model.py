@@ -73,9 +73,10 @@ GQA = dict(vocab=1000, dim=256, layers=3, heads=8, kv_heads=2, hidden=384, max_s
            eps=1e-5)
 
 
-@pytest.mark.parametrize("batch", [1, 3])
+@pytest.mark.parametrize("batch", [1, 3, 12, 16])
 def test_gqa_batched_greedy(oracle, tb, cuda, batch):
-    """GQA (8 query heads on 2 kv heads, the 70B grouping pattern) and a lockstep batch."""
+    """GQA (8 query heads on 2 kv heads, the 70B grouping pattern) and a
+    lockstep batch (12 and 16: the fused decode step in groups of 8 rows)."""
     m = tb.QuantizedModel(GQA, batch=batch, device=0)
     m.init_synthetic(5)
     ref = oracle.Model(GQA, batch, seed=5)
