@@ -26,6 +26,14 @@ positions; one step = 32 greedy tokens per sequence from position 2048.  The
 2048-token prompts' KV state is left as zeros instead of prefilled (the
 decode kernels read the same bytes whatever they hold; a 70B prefill is not
 part of the decode metric), so this workload has no `e2e` or CPU leg.
+
+    python -m torch.distributed.run --nproc-per-node N bench.py --workload llama7b-serving --gpus N
+
+is batched serving of the 7B shape as data-parallel replicas: 64 sequences in
+total, 64 / N per GPU, KV cache of 1280 positions, decode from position 1024
+(the 1024-token prompts' KV state left as zeros, as above); one step = 32
+greedy tokens per sequence; `value` = all ranks' tokens / the slowest rank's
+time ("strong" scaling: the 64 sequences are fixed).
 """
 from __future__ import annotations
 
@@ -58,7 +66,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "llama70b-tp"])
+    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "llama70b-tp", "llama7b-serving"])
     return ap.parse_args()
 
 
@@ -528,8 +536,121 @@ def run_70b_tp(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Llama-7B shape, batched serving as replicas
+# ---------------------------------------------------------------------------
+SERVE_SEQS, SERVE_PROMPT, SERVE_NEW, SERVE_KV = 64, 1024, 32, 1280
+METRIC_SERVE = "int8 Llama-7B batched serving decode tok/s (64 sequences, greedy, replicas)"
+
+
+def step_bytes_serve(P, seqs):
+    """Algorithmic bytes of one decode step of `seqs` sequences on one replica
+    at cache position P: the weights once, every sequence's KV rows 0..P."""
+    c = CFG
+    d, H, Hkv, F, V, L = c["dim"], c["heads"], c["kv_heads"], c["hidden"], c["vocab"], c["layers"]
+    D = d // H
+    w = L * ((H + 2 * Hkv) * D * d + d * H * D + 3 * F * d) + V * d * 4
+    kv = L * 2 * Hkv * D * (P + 1) * 4 * seqs
+    return w + kv
+
+
+def run_serving(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if SERVE_SEQS % world:
+        raise SystemExit(f"{SERVE_SEQS} sequences do not split over {world} replicas")
+    B = SERVE_SEQS // world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    import tendo_b200 as tb
+
+    qm = tb.QuantizedModel(dict(CFG, max_seq=SERVE_KV), batch=B, device=local)
+    qm.init_synthetic(0)
+    stream = torch.cuda.ExternalStream(qm.stream_handle, device=dev)
+    start = tb.synth_tokens(B, CFG["vocab"], 7 + rank)
+
+    def step():
+        qm.set_position(SERVE_PROMPT)
+        qm.decode(SERVE_NEW, start_tokens=start)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    qm.sync()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    qm.sync()
+    barrier()
+    clk = clocks.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = SERVE_SEQS * SERVE_NEW * args.steps / (ms / 1000.0)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    ms_tok = ms / (args.steps * SERVE_NEW)
+    per_gpu = statistics.mean(step_bytes_serve(SERVE_PROMPT + i, B) for i in range(SERVE_NEW))
+    achieved = per_gpu / (ms_tok / 1000.0) / 1e9
+    toks = qm.tokens(SERVE_NEW + 1)[:, 0]
+    if rank == 0:
+        line = {
+            "metric": METRIC_SERVE, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": f"llama7b-int8-serving: 64 sequences as {world} replicas of {B}; decode from "
+                                   "position 1024 (prompt KV zeros); 32 greedy tokens per step; KV 1280 positions",
+                       "global_batch": SERVE_SEQS, "seq_len": SERVE_PROMPT + SERVE_NEW,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2: 7 GB weights + KV per step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None, "kernel": "whole decode step, per GPU",
+                         "bytes_per_token_step_per_gpu": per_gpu,
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clk, "first_tokens": toks[:8].tolist(),
+            "note": "no e2e or CPU leg for this workload: see the module docstring",
+        }
+        print(json.dumps(line), flush=True)
+    qm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "llama7b-serving":
+        if args.impl == "reference":
+            if dist_env()[0] == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference arm runs on the default 7B "
+                                  "batch-1 workload; 64 sequences of the CPU restatement take minutes per token"}),
+                      flush=True)
+            return
+        run_serving(args)
+        return
     if args.workload == "llama70b-tp":
         if args.impl == "reference":
             if dist_env()[0] == 0:
