@@ -57,6 +57,9 @@ struct tb_model {
   int tp = 1, tp_rank = 0;
   int64_t Hg = 0, Hkvg = 0, Fg = 0, Vg = 0;  // unsharded heads, kv heads, hidden, vocabulary
   int64_t v0 = 0;                            // vocabulary index of this rank's first lm_head row
+  bool gv = false;            // decode projections of 9..32 sequences on the tcgen05 GEMV (one weight pass)
+  void* gv_zero = nullptr;    // its split-tile counters and sums (kept zero between launches)
+  void* gv_scratch = nullptr; // its digit rows
   int8_t* tcdig = nullptr;    // digit rows of the prefill projections' activations (tcgen05 GEMM)
   float* tcs = nullptr;       // their row scales
   int trace_n = 0;
@@ -314,6 +317,28 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     qa.Hkv = (int)m->Hkv;
     qa.D = (int)m->D;
     qa.max_seq = (int)m->Ms;
+    const float* resid = m->tp_rank == 0 ? m->h : nullptr;
+    if (m->gv && kind != 1) {
+      // 9..32 sequences: each projection streams its weights once (tcgen05
+      // GEMV, RMSNorm fused into the digit split), RoPE / KV append and
+      // SwiGLU as separate elementwise kernels
+      const int B = (int)m->B, d = (int)m->d, HD = (int)(m->H * m->D), F = (int)m->F;
+      if (kind == 0) {
+        TB_TRY(tb::gemv_tc(m->qkv, m->h, wq, sq, nullptr, B, (int)m->NQKV, d, m->gv_zero, false, m->gv_scratch, st,
+                           m->attn_norm + l * m->d, m->c.eps));
+        return tb::qkv_rope_append(m->qbuf, kcl, vcl, m->qkv, m->cos_t, m->sin_t, m->pos, m->B, m->H, m->Hkv, m->D,
+                                   m->Ms, st);
+      }
+      if (kind == 2) return tb::gemv_tc(m->h, m->attn, wo, so, resid, B, d, HD, m->gv_zero, false, m->gv_scratch, st);
+      if (kind == 3) {
+        TB_TRY(tb::gemv_tc(m->g, m->h, wg, sg, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
+                           m->mlp_norm + l * m->d, m->c.eps));
+        TB_TRY(tb::gemv_tc(m->u, m->h, wu, su, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
+                           m->mlp_norm + l * m->d, m->c.eps));
+        return tb::silu_mul(m->g, m->g, m->u, m->B * m->F, st);
+      }
+      if (kind == 4) return tb::gemv_tc(m->h, m->g, wd, sd, resid, B, d, F, m->gv_zero, false, m->gv_scratch, st);
+    }
     if (kind == 0) {
       // the fused kernels take up to 8 sequences: larger batches run in groups
       for (int64_t b0 = 0; b0 < m->B; b0 += 8) {
@@ -344,7 +369,6 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     if (kind == 1) return tb::attn_decode(aa, st, pdl);
     // row-parallel under tensor parallelism: the residual joins on rank 0 and
     // the step sums the ranks' partial products after the kernel
-    const float* resid = m->tp_rank == 0 ? m->h : nullptr;
     if (kind == 2)
       return tb::gemv_plain(m->h, m->attn, wo, so, resid, (int)m->B, (int)m->d, (int)(m->H * m->D), nullptr, 0.f, st,
                             pdl);
@@ -528,7 +552,16 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   if (m->chunk_s > m->Ms) m->chunk_s = m->Ms;
   m->rows_max = m->B * m->chunk_s;
   const size_t fused_smem = tb::gemv_smem_bytes(m->B <= 1 ? 1 : (m->B <= 2 ? 2 : (m->B <= 4 ? 4 : 8)), (int)m->d);
-  m->fused = m->B <= 16 && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
+  {
+    // 9..32 sequences: the decode projections run on the tcgen05 GEMV (needs
+    // K % 128 and an sm_100 device; probed with an aligned stand-in pointer)
+    const void* al = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+    const int64_t HD = m->H * m->D;
+    m->gv = m->B > 8 && m->B <= tb::kGemvTcMaxM && tb::gemv_tc_ok(al, m->B, m->NQKV, m->d) &&
+            tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, m->F, m->d) &&
+            tb::gemv_tc_ok(al, m->B, m->d, m->F);
+  }
+  m->fused = m->B <= (m->gv ? 32 : 16) && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
              (m->D == 64 || m->D == 128) && (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 ||
                                              m->H / m->Hkv == 8);
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
@@ -594,6 +627,22 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->trace_n = 1 + 2 + 19 * (int)m->L + 3;
   A(dalloc(m, &m->trace, (size_t)m->trace_n));
   A(dalloc(m, &m->err_word, 1));
+  if (m->gv) {
+    int64_t nmax = m->NQKV > m->d ? m->NQKV : m->d;
+    if (m->F > nmax) nmax = m->F;
+    int64_t kmax = m->d > m->H * m->D ? m->d : m->H * m->D;
+    if (m->F > kmax) kmax = m->F;
+    unsigned char* z = nullptr;
+    unsigned char* sc = nullptr;
+    A(dalloc(m, &z, tb::gemv_tc_zeroed_bytes(m->B, nmax, kmax)));
+    A(dalloc(m, &sc, tb::gemv_tc_scratch_bytes(m->B, nmax, kmax)));
+    m->gv_zero = z;
+    m->gv_scratch = sc;
+    if (z) {
+      const cudaError_t ez = cudaMemset(z, 0, tb::gemv_tc_zeroed_bytes(m->B, nmax, kmax));
+      if (ez != cudaSuccess) A(tb::cuda_fail(ez, "cudaMemset"));
+    }
+  }
   {
     int64_t kmax = m->d > m->H * m->D ? m->d : m->H * m->D;
     if (m->F > kmax) kmax = m->F;

@@ -420,7 +420,8 @@ bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K) {
 }
 
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
-                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st) {
+                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st, const float* norm_w,
+                    float eps) {
   const GvLayout L = gv_layout(M, N, K);
   unsigned char* z = static_cast<unsigned char*>(zeroed);
   unsigned char* w = static_cast<unsigned char*>(scratch);
@@ -435,7 +436,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   int stages = (200 * 1024) / stage_bytes;  // as many weight boxes in flight as fit
   if (stages > 16) stages = 16;
   const size_t smem = (size_t)stages * stage_bytes + 1024 + 512;
-  if (inl && (uintptr_t)x % 16 != 0) return TB_ERROR_NOT_SUPPORTED;
+  if (inl && ((uintptr_t)x % 16 != 0 || norm_w)) return TB_ERROR_NOT_SUPPORTED;
 
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return TB_ERROR_NOT_SUPPORTED;
@@ -463,7 +464,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return TB_ERROR_NOT_SUPPORTED;
-    TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, nullptr, 0.f, st));
+    TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, norm_w, eps, st));
   }
   TB_TRY(inl ? set_gv_smem<true>() : set_gv_smem<false>());
 

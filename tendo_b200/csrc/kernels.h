@@ -168,8 +168,10 @@ constexpr int kGemvTcMaxM = 32;
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K);
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
+// norm_w != null (M > 8 only): the product is of RMSNorm(x) * norm_w.
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
-                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st);
+                    int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st,
+                    const float* norm_w = nullptr, float eps = 0.f);
 
 // comm.cu: in-place NCCL allreduce on `st` (fp32 sum, or uint64 max for the
 // packed greedy keys); a no-op without a communicator or with one rank.
@@ -200,6 +202,12 @@ tb_status_t kv_append_rope(float* kc, float* vc, const float* k, const float* v,
 tb_status_t rope_rows(float* x, const float* cos_t, const float* sin_t, int64_t B, int64_t S, int64_t Hx, int64_t D,
                       int64_t pos, int64_t ld, cudaStream_t st);
 tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, cudaStream_t st);
+// Decode step, B rows of qkv [B][(H + 2 Hkv) D]: RoPE on the q and k heads at
+// the device position *pos; q heads to q [B][H][D], k and v heads to the
+// caches [B][Hkv][max_seq][D] at *pos (v unrotated).
+tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, const float* cos_t, const float* sin_t,
+                            const int64_t* pos, int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t max_seq,
+                            cudaStream_t st);
 tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st);
 // keys[r] = max(keys[r], packed (x[r][j], v0 + j)) over the row: the greedy
 // choice as one orderable word (larger logit first, lower index on ties).

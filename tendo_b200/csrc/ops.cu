@@ -107,6 +107,32 @@ __global__ void kv_append_rope_kernel(float* kc, float* vc, const float* __restr
   }
 }
 
+__global__ void qkv_rope_append_kernel(float* q, float* kc, float* vc, const float* __restrict__ qkv,
+                                       const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                       const int64_t* pos_p, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+                                       int64_t max_seq) {
+  const int64_t pos = *pos_p;
+  const int64_t half = D / 2, NH = H + 2 * Hkv;
+  const int64_t total = B * NH * half;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = t % half;
+    const int64_t hh = (t / half) % NH;
+    const int64_t b = t / (half * NH);
+    const float* src = qkv + (b * NH + hh) * D;
+    const float x0 = src[i], x1 = src[i + half];
+    if (hh < H + Hkv) {
+      const float c = cos_t[pos * half + i], sn = sin_t[pos * half + i];
+      float* d = hh < H ? q + (b * H + hh) * D : kc + ((b * Hkv + (hh - H)) * max_seq + pos) * D;
+      d[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      d[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    } else {
+      float* d = vc + ((b * Hkv + (hh - H - Hkv)) * max_seq + pos) * D;
+      d[i] = x0;
+      d[i + half] = x1;
+    }
+  }
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
 __global__ void silu_kernel(float* out, const float* in, int64_t n) {
@@ -269,6 +295,16 @@ tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, c
   TB_REQUIRE(rows <= 0x7fffffff && n > 0);
   argmax_kernel<<<(unsigned)rows, 256, 0, st>>>(out, x, n);
   return check_launch("argmax_kernel");
+}
+
+tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, const float* cos_t, const float* sin_t,
+                            const int64_t* pos, int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t max_seq,
+                            cudaStream_t st) {
+  const int64_t total = B * (H + 2 * Hkv) * (D / 2);
+  if (total == 0) return TB_SUCCESS;
+  const int64_t blocks = (total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096;
+  qkv_rope_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, kc, vc, qkv, cos_t, sin_t, pos, B, H, Hkv, D, max_seq);
+  return check_launch("qkv_rope_append_kernel");
 }
 
 tb_status_t argmax_keys(unsigned long long* keys, const float* x, int64_t rows, int64_t n, int64_t v0,

@@ -87,6 +87,24 @@ def test_gqa_batched_greedy(oracle, tb, cuda, batch):
     m.close()
 
 
+GQA64 = dict(vocab=1000, dim=512, layers=2, heads=8, kv_heads=2, hidden=768, max_seq=160, rope_base=500000.0,
+             eps=1e-5)
+
+
+@pytest.mark.parametrize("batch", [8, 12, 24, 32])
+def test_gqa64_batched_greedy(oracle, tb, cuda, batch):
+    """head_dim 64 (the captured fused decode step): batch 8 on the fused
+    kernels, 12 / 24 / 32 on the single-pass tcgen05 GEMV projections."""
+    m = tb.QuantizedModel(GQA64, batch=batch, device=0)
+    m.init_synthetic(5)
+    ref = oracle.Model(GQA64, batch, seed=5)
+    prompt = np.stack([oracle.synth_tokens(7 + b, 40, GQA64["vocab"]) for b in range(batch)])
+    want, margins = ref.generate_greedy(prompt, 24)
+    got = m.generate_greedy(prompt, 24)
+    np.testing.assert_array_equal(got, want)
+    m.close()
+
+
 def test_llama7b_shape_prefix(oracle, tb, cuda):
     """7B shape (32 layers, d 4096, 32 x 128, F 11008): 16-token prompt + 4
     greedy tokens == the oracle's, on the same device-generated weights."""
