@@ -58,6 +58,7 @@ struct tb_model {
   int64_t Hg = 0, Hkvg = 0, Fg = 0, Vg = 0;  // unsharded heads, kv heads, hidden, vocabulary
   int64_t v0 = 0;                            // vocabulary index of this rank's first lm_head row
   bool gv = false;            // decode projections of 9..32 sequences on the tcgen05 GEMV (one weight pass)
+  int lm_rows = 8;            // rows of x the fused lm_head GEMV stages in shared memory (0: none fit)
   void* gv_zero = nullptr;    // its split-tile counters and sums (kept zero between launches)
   void* gv_scratch = nullptr; // its digit rows
   int8_t* tcdig = nullptr;    // digit rows of the prefill projections' activations (tcgen05 GEMM)
@@ -409,13 +410,21 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
   la.V = (int)m->V;
   la.v0 = (int)m->v0;
   la.l2_prefetch = tb::l2_prefetch_enabled();
+  if (kind == 5 && !m->lm_rows) {
+    // d too wide for the fused kernel's staged rows: norm, fp32 GEMM, keys
+    TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->final_norm, m->B, m->d, m->c.eps, st));
+    TB_TRY(tb::gemm_f32_nt(m->logits, m->xn, m->lm_head, (int)m->B, (int)m->V, (int)m->d, st));
+    return tb::argmax_keys(m->keys, m->logits, m->B, m->V, m->v0, st);
+  }
   if (kind == 5) {
-    for (int64_t b0 = 0; b0 < m->B; b0 += 8) {
+    // groups of as many sequences as the kernel can stage (8, or fewer for wide d)
+    const int64_t gr = m->lm_rows;
+    for (int64_t b0 = 0; b0 < m->B; b0 += gr) {
       tb::LmHeadArgs g = la;
       g.h = m->h + b0 * m->d;
       g.logits = m->logits + b0 * m->V;
       g.argmax_keys = m->keys + b0;
-      g.M = (int)(m->B - b0 < 8 ? m->B - b0 : 8);
+      g.M = (int)(m->B - b0 < gr ? m->B - b0 : gr);
       TB_TRY(tb::gemv_lmhead(g, st, pdl));
     }
     return TB_SUCCESS;
@@ -561,9 +570,15 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
             tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, m->F, m->d) &&
             tb::gemv_tc_ok(al, m->B, m->d, m->F);
   }
-  m->fused = m->B <= (m->gv ? 32 : 16) && fused_smem <= 200 * 1024 && m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 &&
-             (m->D == 64 || m->D == 128) && (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 ||
-                                             m->H / m->Hkv == 8);
+  // the captured decode step: the attention kernel's head shapes, and either
+  // the tcgen05 GEMV projections (9..32 sequences) or the fused CUDA-core /
+  // IMMA kernels, which stage up to 8 rows of x in shared memory
+  m->lm_rows = 0;
+  for (int r = 8; r >= 1 && !m->lm_rows; r /= 2)
+    if (tb::gemv_smem_bytes(r, (int)m->d) <= 200 * 1024) m->lm_rows = r;
+  m->fused = m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 && (m->D == 64 || m->D == 128) &&
+             (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 || m->H / m->Hkv == 8) &&
+             (m->gv ? m->B <= 32 : (m->B <= 16 && fused_smem <= 200 * 1024));
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);

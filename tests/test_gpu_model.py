@@ -105,6 +105,24 @@ def test_gqa64_batched_greedy(oracle, tb, cuda, batch):
     m.close()
 
 
+# d_model 8192 as the 70B shape (64 query / 8 kv heads x 128): too wide for the
+# fused lm_head's staged rows, so the captured step takes the fp32 GEMM + key path
+WIDE = dict(vocab=1000, dim=8192, layers=1, heads=64, kv_heads=8, hidden=1024, max_seq=64, rope_base=500000.0,
+            eps=1e-5)
+
+
+def test_wide_model_batched_greedy(oracle, tb, cuda):
+    batch = 9
+    m = tb.QuantizedModel(WIDE, batch=batch, device=0)
+    m.init_synthetic(5)
+    ref = oracle.Model(WIDE, batch, seed=5)
+    prompt = np.stack([oracle.synth_tokens(7 + b, 16, WIDE["vocab"]) for b in range(batch)])
+    want, margins = ref.generate_greedy(prompt, 8)
+    got = m.generate_greedy(prompt, 8)
+    np.testing.assert_array_equal(got, want)
+    m.close()
+
+
 def test_llama7b_shape_prefix(oracle, tb, cuda):
     """7B shape (32 layers, d 4096, 32 x 128, F 11008): 16-token prompt + 4
     greedy tokens == the oracle's, on the same device-generated weights."""
