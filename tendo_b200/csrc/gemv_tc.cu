@@ -380,8 +380,8 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 }
 
 // Workspace: a zero-maintained part (per-tile counters and split-tile sums:
-// zero before a launch, zero again after it) and, for M > kGvInlineM, a
-// scratch part for the digit rows and row scales.
+// zero before a launch, zero again after it) and a scratch part for the
+// digit rows and row scales (unused when the kernel makes its own digits).
 struct GvLayout {
   size_t count, acc, zeroed, dig, srow, scratch;
 };
@@ -395,7 +395,7 @@ GvLayout gv_layout(int64_t M, int64_t N, int64_t K) {
   L.zeroed = L.acc + (((size_t)tiles * ND * kGvRows * 4 + 255) & ~(size_t)255);
   L.dig = 0;
   L.srow = (((size_t)(3 * M * K) + 255) & ~(size_t)255);
-  L.scratch = M <= kGvInlineM ? 0 : L.srow + (size_t)M * 4;
+  L.scratch = L.srow + (size_t)M * 4;
   return L;
 }
 
@@ -425,7 +425,9 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   const GvLayout L = gv_layout(M, N, K);
   unsigned char* z = static_cast<unsigned char*>(zeroed);
   unsigned char* w = static_cast<unsigned char*>(scratch);
-  const bool inl = M <= kGvInlineM;
+  // digit tiles made in the kernel for small M without a norm; otherwise the
+  // digit kernel (which also applies the RMSNorm) writes them for TMA
+  const bool inl = M <= kGvInlineM && !norm_w;
   const int ND = ((3 * M + 15) / 16) * 16;
   const int KB = K / kGvBK;
   const int tiles = (N + kGvRows - 1) / kGvRows;
@@ -436,7 +438,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   int stages = (200 * 1024) / stage_bytes;  // as many weight boxes in flight as fit
   if (stages > 16) stages = 16;
   const size_t smem = (size_t)stages * stage_bytes + 1024 + 512;
-  if (inl && ((uintptr_t)x % 16 != 0 || norm_w)) return TB_ERROR_NOT_SUPPORTED;
+  if (inl && (uintptr_t)x % 16 != 0) return TB_ERROR_NOT_SUPPORTED;
 
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return TB_ERROR_NOT_SUPPORTED;

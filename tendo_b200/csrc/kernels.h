@@ -163,12 +163,12 @@ tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* sc
 // by K blocks (split tiles finished by the last CTA to arrive).
 // `zeroed` (gemv_tc_zeroed_bytes) holds counters and split-tile sums and is
 // zero before and after each launch (zero_first: clear it first); `scratch`
-// (gemv_tc_scratch_bytes, 0 for M <= 8) holds the digit rows.
+// (gemv_tc_scratch_bytes) holds the digit rows.
 constexpr int kGemvTcMaxM = 32;
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K);
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
-// norm_w != null (M > 8 only): the product is of RMSNorm(x) * norm_w.
+// norm_w != null: the product is of RMSNorm(x) * norm_w (the digit kernel applies it).
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st,
                     const float* norm_w = nullptr, float eps = 0.f);
