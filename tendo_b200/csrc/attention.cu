@@ -19,8 +19,6 @@
 namespace tb {
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnWarps = kAttnThreads / 32;
 
 template <int VEC>
 struct VecT;
@@ -51,13 +49,17 @@ __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
 }
 
 // grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv
-// head.  Each warp takes tiles of U consecutive positions: U K rows and U V
-// rows are loaded at once (2 U 16-byte loads in flight per lane for D = 128),
-// the U scores reduced together, and the running softmax updated once per tile.
-template <int VEC, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArgs a) {
+// head; W warps (8 when G >= 4: the G running softmaxes take registers, so
+// fewer CTAs fit per SM and each needs more rows in flight).  Each warp takes
+// tiles of U consecutive positions: U K rows and U V rows are loaded at once
+// (2 U 16-byte loads in flight per lane for D = 128), the U scores reduced
+// together, and the running softmax updated once per tile.
+template <int VEC, int G, int W>
+__global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int D = VEC * 32;
   constexpr int U = 8;
+  constexpr int kAttnWarps = W;
+  constexpr int kAttnThreads = W * 32;
   __shared__ float sm_o[kAttnWarps][G][D];
   __shared__ float sm_ml[kAttnWarps][G][2];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnDecodeArg
   const int64_t end = min(start + chunk, sk);
   const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
   const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && a.l2_prefetch) {
     const int64_t pend = min(end, sk - 1);  // row sk - 1 comes from the preceding kernel
     if (pend > start) {
       prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
@@ -312,17 +314,21 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, co
 }
 
 template <int VEC, int G>
-tb_status_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
+  // the older rows are prefetched into L2 only while a layer's whole cache
+  // fits in it comfortably (a batch-1 step); larger caches stream directly
+  a.l2_prefetch = (double)a.B * a.Hkv * a.max_seq * (a.D * 8.0) <= 96e6;
+  constexpr int W = G >= 4 ? 8 : 4;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
-  cfg.blockDim = dim3(kAttnThreads);
+  cfg.blockDim = dim3(W * 32);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W>, a);
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
   const int warps = a.B * a.H;
   cfg.gridDim = dim3((warps + 3) / 4);

@@ -57,6 +57,7 @@ struct AttnDecodeArgs {
   int64_t sk;
   int B, H, Hkv, D, max_seq, nsplit;
   float scale;
+  bool l2_prefetch;  // set by the launcher
 };
 
 // decode_mk.cu: the whole batch-1 decode step as one persistent kernel.
