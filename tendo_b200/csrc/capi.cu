@@ -84,7 +84,7 @@ int gemm_planes(tb_gemm_mode_t mode) { return mode == TB_GEMM_I8X2 ? 2 : 3; }
 
 size_t dqmm_workspace(int64_t M, int64_t N, int64_t K, int64_t group_size, tb_gemm_mode_t mode) {
   if (group_size > 0 || mode == TB_GEMM_SIMT) return 0;
-  if (M <= tb::kGemvTcMaxM) {
+  if (M <= 32) {  // the decode regime of the C ABI
     if (K % 128 != 0) return 0;
     return tb::gemv_tc_zeroed_bytes(M, N, K) + tb::gemv_tc_scratch_bytes(M, N, K);
   }

@@ -57,7 +57,7 @@ struct tb_model {
   int tp = 1, tp_rank = 0;
   int64_t Hg = 0, Hkvg = 0, Fg = 0, Vg = 0;  // unsharded heads, kv heads, hidden, vocabulary
   int64_t v0 = 0;                            // vocabulary index of this rank's first lm_head row
-  bool gv = false;            // decode projections of 2..32 sequences on the tcgen05 GEMV (one weight pass)
+  bool gv = false;            // decode projections of 2..64 sequences on the tcgen05 GEMV (one weight pass)
   int lm_rows = 8;            // rows of x the fused lm_head GEMV stages in shared memory (0: none fit)
   void* gv_zero = nullptr;    // its split-tile counters and sums (kept zero between launches)
   void* gv_scratch = nullptr; // its digit rows
@@ -320,7 +320,7 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     qa.max_seq = (int)m->Ms;
     const float* resid = m->tp_rank == 0 ? m->h : nullptr;
     if (m->gv && kind != 1) {
-      // 2..32 sequences: each projection streams its weights once (tcgen05
+      // 2..64 sequences: each projection streams its weights once (tcgen05
       // GEMV, RMSNorm fused into the digit split), RoPE / KV append and
       // SwiGLU as separate elementwise kernels
       const int B = (int)m->B, d = (int)m->d, HD = (int)(m->H * m->D), F = (int)m->F;
@@ -562,7 +562,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->rows_max = m->B * m->chunk_s;
   const size_t fused_smem = tb::gemv_smem_bytes(m->B <= 1 ? 1 : (m->B <= 2 ? 2 : (m->B <= 4 ? 4 : 8)), (int)m->d);
   {
-    // 2..32 sequences: the decode projections run on the tcgen05 GEMV (needs
+    // 2..64 sequences: the decode projections run on the tcgen05 GEMV (needs
     // K % 128 and an sm_100 device; probed with an aligned stand-in pointer)
     const void* al = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
     const int64_t HD = m->H * m->D;
@@ -571,14 +571,14 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
             tb::gemv_tc_ok(al, m->B, m->d, m->F);
   }
   // the captured decode step: the attention kernel's head shapes, and either
-  // the tcgen05 GEMV projections (2..32 sequences) or the fused CUDA-core /
+  // the tcgen05 GEMV projections (2..64 sequences) or the fused CUDA-core /
   // IMMA kernels, which stage up to 8 rows of x in shared memory
   m->lm_rows = 0;
   for (int r = 8; r >= 1 && !m->lm_rows; r /= 2)
     if (tb::gemv_smem_bytes(r, (int)m->d) <= 200 * 1024) m->lm_rows = r;
   m->fused = m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 && (m->D == 64 || m->D == 128) &&
              (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 || m->H / m->Hkv == 8) &&
-             (m->gv ? m->B <= 32 : (m->B <= 16 && fused_smem <= 200 * 1024));
+             (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024));
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);

@@ -1,4 +1,4 @@
-// gemv_tc.cu — the decode-regime quantized Linear (1 <= M <= 32) on the
+// gemv_tc.cu — the decode-regime quantized Linear (1 <= M <= 64) on the
 // 5th-generation tensor cores, for the microbench and C-ABI callers.
 //
 // out[M, N] = x[M, K] @ (q * scale)^T (+ resid), q int8 [N, K] as stored.
@@ -41,7 +41,7 @@ namespace {
 constexpr int kGvRows = 128;               // weight rows per tile (MMA M)
 constexpr int kGvBK = 128;                 // K bytes per stage
 constexpr int kGvWTile = kGvRows * kGvBK;  // 16 KB
-constexpr int kGvTmemCols = 256;           // two accumulators of up to 128 columns
+constexpr int kGvTmemCols = 512;           // two accumulators of up to 256 columns (ND <= 192)
 constexpr int kGvInlineM = 8;              // M up to which the kernel makes its own digits
 
 struct GvArgs {
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
         const int buf = seg & 1;
         if (seg >= 2) mbarrier_wait(&tempty[buf], (uint32_t)(((seg - 2) >> 1) & 1), a.err);
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * 128);
+        const uint32_t d = tmem + (uint32_t)(buf * 256);
         for (int first = 1; it < seg_end; it++, i++, first = 0) {
           const int s = i % S, use = i / S;
           mbarrier_wait(&full[s], (uint32_t)(use & 1), a.err);
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
       mbarrier_wait(&tfull[buf], (uint32_t)((seg >> 1) & 1), a.err);
       __syncwarp();
       tc_fence_after();
-      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 128);
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
       const int n = tile * kGvRows + rowt;
       const bool live = n < a.N;
       const float sc = live ? a.scale[n] : 0.f;

@@ -165,7 +165,7 @@ tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* sc
 // `zeroed` (gemv_tc_zeroed_bytes) holds counters and split-tile sums and is
 // zero before and after each launch (zero_first: clear it first); `scratch`
 // (gemv_tc_scratch_bytes) holds the digit rows.
-constexpr int kGemvTcMaxM = 32;
+constexpr int kGemvTcMaxM = 64;
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K);
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);

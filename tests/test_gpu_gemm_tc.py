@@ -112,6 +112,7 @@ GEMV_SHAPES = [(1, 4096, 4096), (1, 11008, 4096), (1, 4096, 11008), (3, 300, 102
                (8, 4096, 4096), (8, 11008, 4096), (17, 1408, 512), (32, 4096, 4096), (32, 11008, 4096)]
 
 
+
 @pytest.mark.parametrize("M,N,K", GEMV_SHAPES)
 def test_gemv_tc_matches_oracle(oracle, be, cuda, M, N, K):
     rng, x, q, s = _case(oracle, M, N, K, M * 131 + N + K)

@@ -91,7 +91,7 @@ GQA64 = dict(vocab=1000, dim=512, layers=2, heads=8, kv_heads=2, hidden=768, max
              eps=1e-5)
 
 
-@pytest.mark.parametrize("batch", [2, 8, 12, 24, 32])
+@pytest.mark.parametrize("batch", [2, 8, 12, 24, 32, 64])
 def test_gqa64_batched_greedy(oracle, tb, cuda, batch):
     """head_dim 64 (the captured decode step) on the single-pass tcgen05 GEMV
     projections (RMSNorm fused into the digit kernel)."""
