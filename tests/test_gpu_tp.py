@@ -40,3 +40,28 @@ def test_tp2_greedy_matches_unsharded_oracle(oracle, tb, cuda, tmp_path, cfg, ba
     mp.start_processes(tp_worker.run, args=(2, _free_port(), cfg, batch, 5, prompt, 24, out), nprocs=2,
                        join=True, start_method="spawn")
     np.testing.assert_array_equal(np.load(out), want)
+
+
+def test_tp2_loads_its_shard_of_a_checkpoint(oracle, tb, cuda, tmp_path):
+    """An unsharded pre-quantized checkpoint loaded by two tensor-parallel ranks."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    import tp_worker
+    from tendo_b200 import checkpoint as ck
+
+    cfg, batch = GQA64, 3
+    src = tb.QuantizedModel(cfg, batch=1, device=0)
+    src.init_synthetic(5)
+    path = str(tmp_path / "m.safetensors")
+    ck.export_model(src, path)
+    src.close()
+    ref = oracle.Model(cfg, batch, seed=5)
+    prompt = np.stack([oracle.synth_tokens(7 + b, 40, cfg["vocab"]) for b in range(batch)])
+    want, _ = ref.generate_greedy(prompt, 24)
+    out = str(tmp_path / "tokens.npy")
+    mp.start_processes(tp_worker.run, args=(2, _free_port(), cfg, batch, 5, prompt, 24, out, path), nprocs=2,
+                       join=True, start_method="spawn")
+    np.testing.assert_array_equal(np.load(out), want)

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 
 
-def run(rank, world, port, cfg, batch, seed, prompt, steps, out_path):
+def run(rank, world, port, cfg, batch, seed, prompt, steps, out_path, ckpt=None):
     import torch
     import torch.distributed as dist
 
@@ -23,7 +23,12 @@ def run(rank, world, port, cfg, batch, seed, prompt, steps, out_path):
 
     comm = tb.Comm.from_process_group(rank)
     m = tb.QuantizedModel(cfg, batch=batch, device=rank, comm=comm)
-    m.init_synthetic(seed)
+    if ckpt:
+        from tendo_b200 import checkpoint
+
+        checkpoint.load_model(m, ckpt)  # this rank's shard of the unsharded checkpoint
+    else:
+        m.init_synthetic(seed)
     toks = m.generate_greedy(np.asarray(prompt, dtype=np.int64), steps)
     m.close()
     dist.barrier()
