@@ -339,3 +339,59 @@ TINY = dict(vocab=32000, dim=512, layers=8, heads=8, kv_heads=8, hidden=1408, ma
             rope_base=10000.0, eps=1e-5)
 LLAMA7B = dict(vocab=32000, dim=4096, layers=32, heads=32, kv_heads=32, hidden=11008, max_seq=2048,
                rope_base=10000.0, eps=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# Sampler.Sample (models/sampling.go:47-70, :99-161), restated with float32
+# scalars for every operation, loops in the reference's order.  The uniform
+# draw r (the reference's rng.Float32()) is an argument.
+# ---------------------------------------------------------------------------
+def _softmax_ref(x):
+    """models/sampling.go:140-161: max from x[0], float32(exp(float64(v - max))),
+    fp32 sum in index order, division."""
+    import math
+
+    f32 = np.float32
+    m = x[0]
+    for v in x[1:]:
+        if v > m:
+            m = v
+    e = [f32(math.exp(float(f32(v - m)))) if np.isfinite(f32(v - m)) else f32(0.0 if f32(v - m) < 0 else np.nan)
+         for v in x]
+    s = f32(0.0)
+    for p in e:
+        s = f32(s + p)
+    return [f32(p / s) for p in e]
+
+
+def sample(logits, temperature=1.0, top_k=0, top_p=0.0, r=0.5):
+    f32 = np.float32
+    x = [f32(v) for v in np.asarray(logits, np.float32)]
+    V = len(x)
+    T = f32(temperature)
+    if T != f32(1.0) and T > 0:
+        x = [f32(v / T) for v in x]
+    if 0 < top_k < V:
+        thr = sorted(x, reverse=True)[top_k - 1]  # findKthLargest: the k-th largest value
+        x = [f32(-np.inf) if v < thr else v for v in x]
+    if 0 < top_p < 1.0:
+        probs = _softmax_ref(x)
+        order = sorted(range(V), key=lambda i: (-probs[i], i))  # stable insertion sort, descending
+        cs, cut = f32(0.0), 0
+        for n, i in enumerate(order):
+            cs = f32(cs + probs[i])
+            if cs >= f32(top_p):
+                cut = n + 1
+                break
+        for i in order[cut:]:
+            x[i] = f32(-np.inf)
+    if all(v == -np.inf for v in x):
+        return V - 1
+    probs = _softmax_ref(x)
+    cs = f32(0.0)
+    r = f32(r)
+    for i, p in enumerate(probs):
+        cs = f32(cs + p)
+        if r < cs:
+            return i
+    return V - 1

@@ -68,6 +68,7 @@ SIGNATURES = [
     ("tb_synth_tokens_host", _st, [_vp, _i64, _i64, ctypes.c_uint64]),
     ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
     ("tb_model_create_tp", _st, [_vp, _vp, ctypes.c_int, _vp]),
+    ("tb_sample_f32", _st, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float, _vp, _vp]),
     ("tb_comm_unique_id_bytes", ctypes.c_size_t, []),
     ("tb_comm_unique_id", _st, [_vp, ctypes.c_size_t]),
     ("tb_comm_create", _st, [_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
@@ -231,6 +232,19 @@ class Backend:
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
         check(lib.tb_dequant_matmul_i8f32_ws(_ptr(out), _ptr(x), _ptr(qweight), _ptr(scale), M, N, K, group_size,
                                              mode, _ptr(ws) if ws is not None else None, ws_bytes, _stream()))
+        return out
+
+    # models.Sampler.Sample (models/sampling.go:47-70), one row per sequence
+    def Sample(self, logits, uniforms, temperature: float = 1.0, top_k: int = 0, top_p: float = 0.0):
+        torch = _torch()
+        _need_cuda(logits, uniforms)
+        B, V = logits.shape
+        out = torch.empty(B, dtype=torch.int64, device=logits.device)
+        bad = torch.zeros(1, dtype=torch.int32, device=logits.device)
+        check(lib.tb_sample_f32(_ptr(out), _ptr(logits), _ptr(uniforms), B, V, float(temperature), int(top_k),
+                                float(top_p), _ptr(bad), _stream()))
+        if int(bad.item()):
+            raise ShapeError(f"{int(bad.item())} rows keep more than 4096 tokens for top-p")
         return out
 
     def MatMulNT(self, a, b):

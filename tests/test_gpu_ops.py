@@ -236,3 +236,25 @@ def test_attention(oracle, be, cuda, B, H, Hkv, D, Sq, sk):
     got = _np(be.Attention(_t(q, cuda), _t(kc, cuda), _t(vc, cuda), sk))
     want = _attn_ref(oracle, q, kc, vc, sk)
     assert rel_err(got, want) <= 1e-4
+
+
+# --- Sampler.Sample on the device (models/sampling.go:47-70) ----------------
+@pytest.mark.parametrize("V,T,K,P", [(32000, 1.0, 0, 0.0), (32000, 0.7, 50, 0.0), (32000, 1.3, 40, 0.9),
+                                     (4000, 1.0, 0, 0.9), (32000, 1.0, 1, 0.0), (1000, 0.5, 999, 0.95)])
+def test_sample_matches_oracle(oracle, be, cuda, V, T, K, P):
+    rng = np.random.default_rng(V + K)
+    B = 6
+    logits = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    logits[1, :10] = logits[1].max() + 1.0  # ties at the top
+    r = np.array([0.0, 0.5, 0.999999, 0.25, 0.75, 0.1], np.float32)
+    got = _np(be.Sample(_t(logits, cuda), _t(r, cuda), T, K, P))
+    want = [oracle.sample(logits[b], T, K, P, float(r[b])) for b in range(B)]
+    np.testing.assert_array_equal(got, np.array(want))
+
+
+def test_sample_top_p_without_top_k_over_a_large_vocab_is_reported(be, cuda):
+    import tendo_b200 as tb
+
+    logits = np.zeros((1, 32000), np.float32)
+    with pytest.raises(tb.ShapeError):
+        be.Sample(_t(logits, cuda), _t(np.array([0.5], np.float32), cuda), 1.0, 0, 0.9)

@@ -253,3 +253,25 @@ def test_oracle_reproduces_golden_fixture(oracle):
     assert prompt.tolist() == g["prompt"]
     toks, _ = m.generate_greedy(prompt, 16)
     assert toks[0].tolist() == g["tokens"][:16]
+
+
+# --- Sampler.Sample (models/sampling.go:47-70): the restatement on cases with
+# hand-computed answers ------------------------------------------------------
+def test_sampler_restatement_known_answers(oracle):
+    import math
+
+    s = oracle.sample
+    assert s([0.0, 0.0], r=0.25) == 0 and s([0.0, 0.0], r=0.75) == 1
+    # top-k keeps every value tied with the k-th largest (findKthLargest is by value)
+    assert s([1.0, 3.0, 3.0, 2.0], top_k=1, r=0.6) == 2
+    assert s([1.0, 3.0, 3.0, 2.0], top_k=1, r=0.4) == 1
+    # top-p: probabilities 0.5, 0.3, 0.2; P = 0.7 keeps the first two (0.5 + 0.3 >= 0.7),
+    # renormalised to 0.625 / 0.375
+    lg = [math.log(0.5), math.log(0.3), math.log(0.2)]
+    assert s(lg, top_p=0.7, r=0.6) == 0 and s(lg, top_p=0.7, r=0.7) == 1
+    assert s(lg, top_p=0.7, r=0.99) == 1  # the masked token is never drawn
+    # temperature 2 flattens [0, ln 4] to [0, ln 2]: probabilities 1/3, 2/3
+    assert s([0.0, math.log(4.0)], temperature=2.0, r=0.3) == 0
+    assert s([0.0, math.log(4.0)], temperature=2.0, r=0.34) == 1
+    # r at the very top of [0, 1) still lands on a token
+    assert s([5.0, 1.0, 0.0], r=0.9999999) == 2
