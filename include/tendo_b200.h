@@ -310,6 +310,15 @@ TB_API int64_t tb_model_position(const tb_model* m);
 TB_API tb_status_t tb_model_forward(tb_model* m, const int64_t* tokens_host, int64_t B, int64_t S,
                              float* last_logits_host, int64_t* next_host);
 
+/* QuantizedModel.Generate with the Sampler (models/llama/quantized.go:422-477,
+ * models/sampling.go:47-70): the prompt, then n_new tokens per sequence, each
+ * drawn on the device (tb_sample_f32) from the step's logits with the uniform
+ * draw (seed, step * B + row) of the library's counter generator, so no
+ * logits leave the GPU.  One GPU (not tensor parallel). */
+TB_API tb_status_t tb_model_generate_sample(tb_model* m, const int64_t* prompt_host, int64_t B, int64_t S,
+                                            int64_t n_new, float temperature, int64_t top_k, float top_p,
+                                            uint64_t seed, int64_t* out_tokens_host);
+
 /* GenerateGreedy (models/llama/generate.go:99-150): reset, prefill with
  * prompt[B, S] (HOST), then n_new greedy tokens into out_tokens_host[B, n_new].
  * Each decode step is one CUDA-graph launch that reads the token and position

@@ -195,4 +195,12 @@ TS_HD uint32_t ts_uniform_int(uint64_t key, uint64_t index, uint32_t n) {
   return (uint32_t)((b * (uint64_t)n) >> 32);
 }
 
+/* Uniform float in [0, 1): the top 24 bits of the draw times 2^-24 (exact in
+ * fp32, identical on host and device). */
+TS_HD float ts_uniform_f32(uint64_t key, uint64_t index) {
+  return (float)(uint32_t)(ts_bits(key, index) >> 40) * (1.0f / 16777216.0f);
+}
+
+#define TS_STREAM_SAMPLE 0x7fff0006ull /* the sampler's uniforms: index = step * B + row */
+
 #endif /* TENDO_SYNTH_H */

@@ -296,6 +296,12 @@ int or_embedding(const float* table, int64_t V, int64_t d, const int64_t* ids, i
   return 0;
 }
 
+/* The sampler's uniform draws (ts_uniform_f32): index offset .. offset + n - 1. */
+void or_synth_uniform(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float* out) {
+  const uint64_t key = ts_key(seed, stream);
+  for (int64_t i = 0; i < n; i++) out[i] = ts_uniform_f32(key, offset + (uint64_t)i);
+}
+
 void or_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, double std_, float* out) {
   uint64_t key = ts_key(seed, stream);
 #pragma omp parallel for schedule(static)

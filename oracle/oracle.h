@@ -76,6 +76,7 @@ int or_embedding(const float* table, int64_t V, int64_t d, const int64_t* ids, i
 
 /* Synthetic inputs (include/tendo_synth.h): out[i] = N(0, std) draw
  * `offset + i` of (seed, stream); tokens uniform in [0, vocab). */
+void or_synth_uniform(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float* out);
 void or_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, double std_, float* out);
 void or_synth_tokens(uint64_t seed, int64_t n, int64_t vocab, int64_t* out);
 

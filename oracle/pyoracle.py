@@ -69,6 +69,7 @@ def lib():
         L.or_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_double,
                                       _f32p]
         L.or_synth_tokens.argtypes = [ctypes.c_uint64, _i64, _i64, _i64p]
+        L.or_synth_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _i64, _f32p]
         L.or_model_create.argtypes = [ctypes.POINTER(Config), ctypes.c_int, ctypes.c_uint64, ctypes.c_int]
         L.or_model_create.restype = ctypes.c_void_p
         L.or_model_free.argtypes = [ctypes.c_void_p]
@@ -395,3 +396,30 @@ def sample(logits, temperature=1.0, top_k=0, top_p=0.0, r=0.5):
         if r < cs:
             return i
     return V - 1
+
+
+STREAM_SAMPLE = 0x7FFF0006
+
+
+def synth_uniform(seed: int, stream: int, n: int, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().or_synth_uniform(seed, stream, offset, n, _p(out, _f32p))
+    return out
+
+
+def generate_sample(model, prompt, n_new, temperature, top_k, top_p, seed):
+    """QuantizedModel.Generate with the Sampler (models/llama/quantized.go:422-477,
+    models/sampling.go:47-70): forward the prompt, then per step sample every
+    row's last logits with the uniform draw (seed, step * B + row) and feed the
+    tokens back."""
+    prompt = np.ascontiguousarray(prompt, dtype=np.int64).reshape(model.B, -1)
+    B = model.B
+    _, last, _ = model.forward(prompt, want_logits=False)
+    out = np.empty((B, n_new), np.int64)
+    for j in range(n_new):
+        u = synth_uniform(seed, STREAM_SAMPLE, B, offset=j * B)
+        toks = np.array([sample(last[b], temperature, top_k, top_p, float(u[b])) for b in range(B)], np.int64)
+        out[:, j] = toks
+        if j + 1 < n_new:
+            _, last, _ = model.forward(toks[:, None], want_logits=False)
+    return out

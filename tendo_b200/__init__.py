@@ -69,6 +69,8 @@ SIGNATURES = [
     ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
     ("tb_model_create_tp", _st, [_vp, _vp, ctypes.c_int, _vp]),
     ("tb_sample_f32", _st, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float, _vp, _vp]),
+    ("tb_model_generate_sample", _st, [_vp, _vp, _i64, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float,
+                                       ctypes.c_uint64, _vp]),
     ("tb_comm_unique_id_bytes", ctypes.c_size_t, []),
     ("tb_comm_unique_id", _st, [_vp, ctypes.c_size_t]),
     ("tb_comm_create", _st, [_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
@@ -553,6 +555,17 @@ class QuantizedModel:
         p = np.ascontiguousarray(prompt, dtype=np.int64).reshape(self.B, -1)
         out = np.empty((self.B, n_new), np.int64)
         check(lib.tb_model_generate_greedy(self.h, p.ctypes.data, self.B, p.shape[1], n_new, out.ctypes.data))
+        return out
+
+    def generate_sample(self, prompt, n_new: int, temperature: float = 1.0, top_k: int = 0, top_p: float = 0.0,
+                        seed: int = 0):
+        """Generate with the Sampler, drawn on the device (tb_model_generate_sample)."""
+        import numpy as np
+
+        p = np.ascontiguousarray(prompt, dtype=np.int64).reshape(self.B, -1)
+        out = np.empty((self.B, n_new), np.int64)
+        check(lib.tb_model_generate_sample(self.h, p.ctypes.data, self.B, p.shape[1], n_new, float(temperature),
+                                           int(top_k), float(top_p), seed, out.ctypes.data))
         return out
 
     def decode(self, n_steps: int, start_tokens=None):

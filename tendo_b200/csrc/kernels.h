@@ -210,6 +210,11 @@ tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, co
                             const int64_t* pos, int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t max_seq,
                             cudaStream_t st);
 tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st);
+// The sampler's uniforms for the token the last step generated, and the
+// history entry of that step set to the (sampled) tokens.
+tb_status_t sample_uniforms(float* u, const int64_t* step, int64_t B, uint64_t seed, cudaStream_t st);
+tb_status_t history_set(int64_t* history, const int64_t* tokens, const int64_t* step, int64_t B, int64_t hist_cap,
+                        cudaStream_t st);
 // keys[r] = max(keys[r], packed (x[r][j], v0 + j)) over the row: the greedy
 // choice as one orderable word (larger logit first, lower index on ties).
 tb_status_t argmax_keys(unsigned long long* keys, const float* x, int64_t rows, int64_t n, int64_t v0,

@@ -5,6 +5,7 @@
 
 #include <vector>
 
+#include "../../include/tendo_synth.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -305,6 +306,32 @@ tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, co
   const int64_t blocks = (total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096;
   qkv_rope_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, kc, vc, qkv, cos_t, sin_t, pos, B, H, Hkv, D, max_seq);
   return check_launch("qkv_rope_append_kernel");
+}
+
+// The sampler's draws for the token just generated (device step s counts it):
+// u[b] = uniform(key, (s - 1) B + b).
+__global__ void sample_uniforms_kernel(float* u, const int64_t* step, int64_t B, uint64_t key) {
+  const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (b < B) u[b] = ts_uniform_f32(key, (uint64_t)((*step - 1) * B + b));
+}
+
+// The sampled tokens replace the step's greedy choice in the history.
+__global__ void history_set_kernel(int64_t* history, const int64_t* tokens, const int64_t* step, int64_t B,
+                                   int64_t hist_cap) {
+  const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t s = *step - 1;
+  if (b < B && s >= 0 && s < hist_cap) history[s * B + b] = tokens[b];
+}
+
+tb_status_t sample_uniforms(float* u, const int64_t* step, int64_t B, uint64_t seed, cudaStream_t st) {
+  sample_uniforms_kernel<<<(unsigned)((B + 127) / 128), 128, 0, st>>>(u, step, B, ts_key(seed, TS_STREAM_SAMPLE));
+  return check_launch("sample_uniforms_kernel");
+}
+
+tb_status_t history_set(int64_t* history, const int64_t* tokens, const int64_t* step, int64_t B, int64_t hist_cap,
+                        cudaStream_t st) {
+  history_set_kernel<<<(unsigned)((B + 127) / 128), 128, 0, st>>>(history, tokens, step, B, hist_cap);
+  return check_launch("history_set_kernel");
 }
 
 tb_status_t argmax_keys(unsigned long long* keys, const float* x, int64_t rows, int64_t n, int64_t v0,

@@ -146,3 +146,21 @@ def test_llama7b_shape_prefix(oracle, tb, cuda):
     got = m.generate_greedy(prompt[None, :], 4)
     np.testing.assert_array_equal(got, want)
     m.close()
+
+
+@pytest.mark.parametrize("batch,T,K,P", [(1, 0.8, 20, 0.9), (3, 1.2, 0, 0.0), (12, 0.7, 40, 0.0)])
+def test_sampled_generation_matches_oracle(oracle, tb, cuda, batch, T, K, P):
+    """QuantizedModel.Generate with the Sampler: the device sampler draws every
+    token from the step's logits with the counter generator's uniforms; the
+    oracle does the same with the restated Sampler.  Batch 1 runs the
+    persistent decode kernel, 3 and 12 the captured multi-kernel step."""
+    cfg = GQA64 if batch > 1 else dict(GQA64, heads=8, kv_heads=8)
+    m = tb.QuantizedModel(cfg, batch=batch, device=0)
+    m.init_synthetic(5)
+    ref_w = oracle.Model(cfg, batch, seed=5)
+    prompt = np.stack([oracle.synth_tokens(7 + b, 24, cfg["vocab"]) for b in range(batch)])
+    want = oracle.generate_sample(ref_w, prompt, 16, T, K, P, seed=3)
+    got = m.generate_sample(prompt, 16, T, K, P, seed=3)
+    np.testing.assert_array_equal(got, want)
+    m.close()
+    ref_w.close()
