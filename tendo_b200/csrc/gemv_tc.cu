@@ -39,8 +39,8 @@ namespace tb {
 namespace {
 
 constexpr int kGvRows = 128;               // weight rows per tile (MMA M)
-constexpr int kGvBK = 128;                 // K bytes per stage
-constexpr int kGvWTile = kGvRows * kGvBK;  // 16 KB
+constexpr int kGvSub = 128;                // K bytes of one 128-byte-swizzled sub-tile
+constexpr int kGvWSub = kGvRows * kGvSub;  // 16 KB: 128 weight rows x 128 bytes
 constexpr int kGvTmemCols = 512;           // two accumulators of up to 256 columns (ND <= 192)
 constexpr int kGvInlineM = 8;              // M up to which the kernel makes its own digits
 
@@ -72,9 +72,13 @@ __device__ __forceinline__ int sw128_offset(int r, int c) {
   return (r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 4) ^ (r & 7)) << 4) | (c & 15));
 }
 
-template <bool INL>
+// GKB 128-byte K sub-tiles per stage (one 3-D TMA box of 128 rows x GKB x 128
+// bytes for the weights: longer runs per row, fewer copies).
+template <bool INL, int GKB>
 __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GvArgs a) {
+  constexpr int kGvBK = kGvSub * GKB;     // K bytes per stage
+  constexpr int kGvWTile = kGvWSub * GKB;  // weight bytes per stage
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int S = a.stages;
@@ -123,12 +127,14 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
       for (int i = 0; i < pre; i++) {
         const int it = b0 + i;
         mbarrier_expect_tx(&full[i], (uint32_t)(INL ? kGvWTile : stage_bytes));
-        tma_load_2d(smem + (size_t)i * stage_bytes, &tmW, (it % KB) * kGvBK, (it / KB) * kGvRows, &full[i]);
+        tma_load_3d(smem + (size_t)i * stage_bytes, &tmW, 0, (it / KB) * kGvRows, (it % KB) * GKB, &full[i]);
       }
       if (!INL) {
         pdl_wait();
         for (int i = 0; i < pre; i++)
-          tma_load_2d(smem + (size_t)i * stage_bytes + kGvWTile, &tmX, ((b0 + i) % KB) * kGvBK, 0, &full[i]);
+          for (int g = 0; g < GKB; g++)
+            tma_load_2d(smem + (size_t)i * stage_bytes + kGvWTile + g * ND * kGvSub, &tmX,
+                        ((b0 + i) % KB) * kGvBK + g * kGvSub, 0, &full[i]);
       }
       for (int i = pre; i < n; i++) {
         const int s = i % S, use = i / S;
@@ -136,8 +142,10 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
         mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), a.err);
         unsigned char* st = smem + (size_t)s * stage_bytes;
         mbarrier_expect_tx(&full[s], (uint32_t)(INL ? kGvWTile : stage_bytes));
-        tma_load_2d(st, &tmW, kb * kGvBK, (it / KB) * kGvRows, &full[s]);
-        if (!INL) tma_load_2d(st + kGvWTile, &tmX, kb * kGvBK, 0, &full[s]);
+        tma_load_3d(st, &tmW, 0, (it / KB) * kGvRows, kb * GKB, &full[s]);
+        if (!INL)
+          for (int g = 0; g < GKB; g++)
+            tma_load_2d(st + kGvWTile + g * ND * kGvSub, &tmX, kb * kGvBK + g * kGvSub, 0, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -157,8 +165,11 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
           tc_fence_after();
           const uint32_t w0 = smem_addr(smem + (size_t)s * stage_bytes), x0 = w0 + kGvWTile;
 #pragma unroll
-          for (int kk = 0; kk < kGvBK / 32; kk++)
-            tc_mma_i8(d, sw128_desc(w0 + kk * 32), sw128_desc(x0 + kk * 32), idesc, !(first && kk == 0));
+          for (int g = 0; g < GKB; g++)
+#pragma unroll
+            for (int kk = 0; kk < kGvSub / 32; kk++)
+              tc_mma_i8(d, sw128_desc(w0 + g * kGvRows * kGvSub + kk * 32), sw128_desc(x0 + g * ND * kGvSub + kk * 32),
+                        idesc, !(first && g == 0 && kk == 0));
           tc_commit(&empty[s]);
         }
         tc_commit(&tfull[buf]);
@@ -268,7 +279,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     const int cw = ct >> 5;
     {
       // zero every stage's digit tile once: rows >= 3M stay zero
-      const int xbytes = ND * kGvBK;
+      const int xbytes = ND * kGvBK;  // GKB sub-tiles of ND rows x 128 bytes
       for (int off = ct * 16; off < S * xbytes; off += 128 * 16)
         *reinterpret_cast<uint4*>(smem + (size_t)(off / xbytes) * stage_bytes + kGvWTile + off % xbytes) =
             make_uint4(0u, 0u, 0u, 0u);
@@ -329,15 +340,17 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     while (i < n) {
       const int i2 = next_mine(i + 1);
       const int ii_[2] = {i, i2};
-      float4 xv[2][kGvInlineM];
+      float4 xv[2][kGvInlineM][GKB];
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         const int ii = ii_[h];
         const int kb = (b0 + ii) % KB;
 #pragma unroll
         for (int m = 0; m < kGvInlineM; m++)
-          xv[h][m] = (ii < n && m < M) ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.K + kb * kGvBK) + lane)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int g = 0; g < GKB; g++)
+            xv[h][m][g] = (ii < n && m < M)
+                              ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.K + kb * kGvBK + g * kGvSub) + lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int h = 0; h < 2; h++) {
@@ -349,7 +362,8 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 #pragma unroll
         for (int m = 0; m < kGvInlineM; m++) {
           if (m >= M) break;
-          const float vals[4] = {xv[h][m].x, xv[h][m].y, xv[h][m].z, xv[h][m].w};
+          for (int g = 0; g < GKB; g++) {
+          const float vals[4] = {xv[h][m][g].x, xv[h][m][g].y, xv[h][m][g].z, xv[h][m][g].w};
           uint32_t pk[3] = {0u, 0u, 0u};
 #pragma unroll
           for (int t = 0; t < 4; t++) {
@@ -364,7 +378,8 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
           }
 #pragma unroll
           for (int p = 0; p < 3; p++)
-            *reinterpret_cast<uint32_t*>(xt + sw128_offset(p * M + m, 4 * lane)) = pk[p];
+            *reinterpret_cast<uint32_t*>(xt + g * ND * kGvSub + sw128_offset(p * M + m, 4 * lane)) = pk[p];
+          }
         }
         // the tensor core reads the tile through the async proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -399,12 +414,12 @@ GvLayout gv_layout(int64_t M, int64_t N, int64_t K) {
   return L;
 }
 
-template <bool INL>
+template <bool INL, int GKB>
 tb_status_t set_gv_smem() {
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
-    err = cudaFuncSetAttribute(gemv_tc_kernel<INL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    err = cudaFuncSetAttribute(gemv_tc_kernel<INL, GKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(gemv_tc)");
   return TB_SUCCESS;
@@ -416,7 +431,7 @@ size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(M, N, K).scratch; }
 
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K) {
-  return M >= 1 && M <= kGemvTcMaxM && gemm_tc_ok(q, M, N, K) && K % 128 == 0;
+  return M >= 1 && M <= kGemvTcMaxM && gemm_tc_ok(q, M, N, K) && K % kGvSub == 0;
 }
 
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
@@ -429,6 +444,11 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   // digit kernel (which also applies the RMSNorm) writes them for TMA
   const bool inl = M <= kGvInlineM && !norm_w;
   const int ND = ((3 * M + 15) / 16) * 16;
+  // two 128-byte sub-tiles per stage where K allows (halves the copies and
+  // doubles the contiguous run per weight row)
+  const int G = K % (2 * kGvSub) == 0 ? 2 : 1;
+  const int kGvBK = kGvSub * G;
+  const int kGvWTile = kGvWSub * G;
   const int KB = K / kGvBK;
   const int tiles = (N + kGvRows - 1) / kGvRows;
   const int total = tiles * KB;
@@ -445,11 +465,11 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   CUtensorMap tw, tx;
   memset(&tx, 0, sizeof(tx));
   {
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
-    const cuuint64_t strides[1] = {(cuuint64_t)K};
-    const cuuint32_t box[2] = {kGvBK, kGvRows};
-    const cuuint32_t es[2] = {1, 1};
-    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, es,
+    const cuuint64_t dims[3] = {(cuuint64_t)kGvSub, (cuuint64_t)N, (cuuint64_t)(K / kGvSub)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)kGvSub};
+    const cuuint32_t box[3] = {kGvSub, kGvRows, (cuuint32_t)G};
+    const cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(q), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return TB_ERROR_NOT_SUPPORTED;
@@ -460,7 +480,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   if (!inl) {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(3 * M)};
     const cuuint64_t strides[1] = {(cuuint64_t)K};
-    const cuuint32_t box[2] = {kGvBK, (cuuint32_t)ND};
+    const cuuint32_t box[2] = {kGvSub, (cuuint32_t)ND};
     const cuuint32_t es[2] = {1, 1};
     if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, dig, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -468,7 +488,8 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
       return TB_ERROR_NOT_SUPPORTED;
     TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, norm_w, eps, st));
   }
-  TB_TRY(inl ? set_gv_smem<true>() : set_gv_smem<false>());
+  TB_TRY(inl ? (G == 2 ? set_gv_smem<true, 2>() : set_gv_smem<true, 1>())
+             : (G == 2 ? set_gv_smem<false, 2>() : set_gv_smem<false, 1>()));
 
   GvArgs a{};
   a.out = out;
@@ -496,10 +517,14 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (inl)
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true>, tw, tx, a));
+  if (inl && G == 2)
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 2>, tw, tx, a));
+  else if (inl)
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 1>, tw, tx, a));
+  else if (G == 2)
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 2>, tw, tx, a));
   else
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false>, tw, tx, a));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 1>, tw, tx, a));
   return TB_SUCCESS;
 }
 
