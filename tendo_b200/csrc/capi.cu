@@ -83,11 +83,12 @@ namespace {
 int gemm_planes(tb_gemm_mode_t mode) { return mode == TB_GEMM_I8X2 ? 2 : 3; }
 
 size_t dqmm_workspace(int64_t M, int64_t N, int64_t K, int64_t group_size, tb_gemm_mode_t mode) {
-  if (group_size > 0 || mode == TB_GEMM_SIMT) return 0;
-  if (M <= 32) {  // the decode regime of the C ABI
-    if (K % 128 != 0) return 0;
-    return tb::gemv_tc_zeroed_bytes(M, N, K) + tb::gemv_tc_scratch_bytes(M, N, K);
+  if (mode == TB_GEMM_SIMT) return 0;
+  if (M <= 32) {  // the decode regime of the C ABI (per-group: groups of a multiple of 128)
+    if (K % 128 != 0 || (group_size > 0 && group_size % 128 != 0)) return 0;
+    return tb::gemv_tc_zeroed_bytes(M, N, K) + tb::gemv_tc_scratch_bytes(M, N, K, group_size);
   }
+  if (group_size > 0) return 0;
   return tb::gemm_tc_workspace(M, K, gemm_planes(mode));
 }
 
@@ -128,8 +129,8 @@ tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale
                  int64_t group_size, tb_gemm_mode_t mode, void* ws, size_t ws_bytes, bool arena, cudaStream_t st) {
   if (M <= 32) {
     const size_t gneed = dqmm_workspace(M, N, K, group_size, mode);
-    if (gneed > 0 && tb::gemv_tc_ok(q, M, N, K) && (uintptr_t)x % 16 == 0) {
-      const size_t zb = tb::gemv_tc_zeroed_bytes(M, N, K), sb = tb::gemv_tc_scratch_bytes(M, N, K);
+    if (gneed > 0 && tb::gemv_tc_ok(q, M, N, K, group_size) && (uintptr_t)x % 16 == 0) {
+      const size_t zb = tb::gemv_tc_zeroed_bytes(M, N, K), sb = tb::gemv_tc_scratch_bytes(M, N, K, group_size);
       void *zero = nullptr, *scratch = nullptr;
       if (arena) {
         TB_TRY(arena_get(1, zb, &zero));
@@ -139,7 +140,8 @@ tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale
         zero = ws;
         scratch = static_cast<unsigned char*>(ws) + zb;
       }
-      return tb::gemv_tc(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, zero, !arena, scratch, st);
+      return tb::gemv_tc(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, zero, !arena, scratch, st, nullptr, 0.f,
+                         (int)group_size);
     }
     if (!arena && gneed > 0) TB_REQUIRE(ws && ws_bytes >= gneed);
     if (group_size == 0 && tb::gemv_fast_ok(x, q, K))

@@ -52,7 +52,9 @@ struct GvArgs {
   const float* resid;
   int* acc;             // [tiles][ND][128] s32 sums of split tiles (zero between launches)
   unsigned int* count;  // [tiles] CTAs done with a split tile (zero between launches)
+  float* part;          // per-group scales: [grid][2][M][128] fp32 partial rows of split tiles
   int M, N, K, ND, KB, total, stages;
+  int gs, ngroups;      // per-group scales: 128-byte sub-tiles per group, groups per row
   int* err;
 };
 
@@ -74,7 +76,15 @@ __device__ __forceinline__ int sw128_offset(int r, int c) {
 
 // GKB 128-byte K sub-tiles per stage (one 3-D TMA box of 128 rows x GKB x 128
 // bytes for the weights: longer runs per row, fewer copies).
-template <bool INL, int GKB>
+//
+// GRP: per-group scales [N, K / group] (group a multiple of 128).  The MMA
+// hands an accumulator to the epilogue at every group boundary (and at the
+// end of a tile segment, which may cut a group: the scale is linear), the
+// epilogue scales each group's exact s32 sums by scale[n, group] and adds them
+// into fp32 rows in shared memory.  A split tile's fp32 partial rows go to the
+// CTA's own workspace slots; the last CTA to count in adds them in CTA order,
+// so the sum does not depend on arrival order.
+template <bool INL, int GKB, bool GRP>
 __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GvArgs a) {
   constexpr int kGvBK = kGvSub * GKB;     // K bytes per stage
@@ -92,6 +102,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* srow_s = reinterpret_cast<float*>(tmem_slot + 2);  // [kGvInlineM]
   float* cred = srow_s + kGvInlineM;                         // [4][kGvInlineM]
+  float* accs = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes + 512);  // GRP: [ND][128]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long T = a.total, G = gridDim.x;
   const int b0 = range_begin(blockIdx.x, T, G), b1 = range_begin(blockIdx.x + 1, T, G);
@@ -149,7 +160,46 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (GRP && lane == 0) {
+      // MMA issuer, per-group scales: one accumulator per (group, segment)
+      // piece, alternating buffers; h counts the hand-offs
+      const uint32_t idesc = idesc_i8(kGvRows, ND);
+      int i = 0, h = 0;
+      for (int it = b0; it < b1;) {
+        const int tstart = (it / KB) * KB;
+        const int seg_end = min(b1, tstart + KB);
+        int j = (it - tstart) * GKB;  // 128-byte sub-tile within the tile
+        bool open = false;
+        uint32_t d = tmem;
+        for (; it < seg_end; it++, i++) {
+          const int s = i % S, use = i / S;
+          mbarrier_wait(&full[s], (uint32_t)(use & 1), a.err);
+          tc_fence_after();
+          const uint32_t w0 = smem_addr(smem + (size_t)s * stage_bytes), x0 = w0 + kGvWTile;
+#pragma unroll
+          for (int g = 0; g < GKB; g++, j++) {
+            const bool first = !open;
+            if (!open) {
+              const int buf = h & 1;
+              if (h >= 2) mbarrier_wait(&tempty[buf], (uint32_t)(((h - 2) >> 1) & 1), a.err);
+              tc_fence_after();
+              d = tmem + (uint32_t)(buf * 256);
+              open = true;
+            }
+#pragma unroll
+            for (int kk = 0; kk < kGvSub / 32; kk++)
+              tc_mma_i8(d, sw128_desc(w0 + g * kGvRows * kGvSub + kk * 32), sw128_desc(x0 + g * ND * kGvSub + kk * 32),
+                        idesc, !(first && kk == 0));
+            if ((j + 1) % a.gs == 0 || (it + 1 == seg_end && g == GKB - 1)) {
+              tc_commit(&tfull[h & 1]);
+              h++;
+              open = false;
+            }
+          }
+          tc_commit(&empty[s]);
+        }
+      }
+    } else if (lane == 0) {
       // MMA issuer: one accumulator per tile segment, alternating buffers
       const uint32_t idesc = idesc_i8(kGvRows, ND);
       int i = 0, seg = 0;
@@ -181,6 +231,121 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     const int rowt = q * 32 + lane;
     if (INL) mbarrier_wait(sready, 0u, a.err);
     const float* srow = INL ? srow_s : a.srow;
+    if (GRP) {
+      // fp32 sums per accumulator column (digit row p M + m) of this thread's
+      // weight row; distinct columns, so a 16-column chunk is read, updated
+      // and written back as a batch
+      float* acc_r = accs + rowt;  // [ND][128]
+      for (int c = 0; c < ND; c++) acc_r[c * kGvRows] = 0.f;
+      const int nd3 = 3 * M, ncol = (nd3 + 15) & ~15;
+      // the scale of each hand-off is loaded one hand-off ahead
+      auto scale_of = [&](int tile_, int grp_) {
+        const int nn = tile_ * kGvRows + rowt;
+        return nn < a.N ? __ldg(a.scale + (size_t)nn * a.ngroups + grp_) : 0.f;
+      };
+      // out[m, n] = srow[m] y[m] (+ resid) for rows m0 .. m0 + 7
+      auto emit = [&](int m0, const float* y, int n) {
+        float sr[8], rs[8];
+#pragma unroll
+        for (int mm = 0; mm < 8; mm++) {
+          const int m = m0 + mm < M ? m0 + mm : M - 1;
+          sr[mm] = INL ? srow[m] : __ldcg(srow + m);
+          rs[mm] = a.resid ? __ldcg(a.resid + (size_t)m * a.N + n) : 0.f;
+        }
+#pragma unroll
+        for (int mm = 0; mm < 8; mm++)
+          if (m0 + mm < M) a.out[(size_t)(m0 + mm) * a.N + n] = a.resid ? sr[mm] * y[mm] + rs[mm] : sr[mm] * y[mm];
+      };
+      float sg_next = scale_of(b0 / KB, ((b0 % KB) * GKB) / a.gs);
+      int h = 0;
+      for (int it = b0; it < b1;) {
+        const int tile = it / KB;
+        const int tstart = tile * KB, tend = tstart + KB;
+        const int seg_end = min(b1, tend);
+        const int n = tile * kGvRows + rowt;
+        const bool live = n < a.N;
+        for (int j = (it - tstart) * GKB, je = (seg_end - tstart) * GKB; j < je; h++) {
+          const int grp = j / a.gs;
+          const int jn = min(je, (grp + 1) * a.gs);
+          const int buf = h & 1;
+          const float sg = sg_next;
+          if (jn < je)
+            sg_next = scale_of(tile, jn / a.gs);
+          else if (seg_end < b1)
+            sg_next = scale_of(tile + 1, 0);
+          mbarrier_wait(&tfull[buf], (uint32_t)((h >> 1) & 1), a.err);
+          __syncwarp();
+          tc_fence_after();
+          const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+          for (int j0 = 0; j0 < ncol; j0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tb + j0, v);
+            tmem_wait_ld();
+            pin16(v);
+            float* ac = acc_r + j0 * kGvRows;
+            float t[16];
+#pragma unroll
+            for (int c = 0; c < 16; c++) t[c] = ac[c * kGvRows];
+#pragma unroll
+            for (int c = 0; c < 16; c++) ac[c * kGvRows] = __fmaf_rn((float)(int)v[c], sg, t[c]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbarrier_arrive(&tempty[buf]);
+          j = jn;
+        }
+        // y[m] = a0 + a1 / 128 + a2 / 128^2 over this segment; columns re-zeroed
+        auto seg_sum = [&](int m) {
+          const float y = acc_r[m * kGvRows] + acc_r[(M + m) * kGvRows] * (1.0f / 128.0f) +
+                          acc_r[(2 * M + m) * kGvRows] * (1.0f / 16384.0f);
+          return y;
+        };
+        const int c0 = owner_of(tstart, T, G), c1 = owner_of(tend - 1, T, G);
+        if (c0 == c1) {
+          for (int m0 = 0; m0 < M; m0 += 8) {
+            float y[8];
+#pragma unroll
+            for (int mm = 0; mm < 8; mm++) y[mm] = m0 + mm < M ? seg_sum(m0 + mm) : 0.f;
+            if (live) emit(m0, y, n);
+          }
+        } else {
+          // split tile: this CTA's slot 0 is its first segment, slot 1 its last
+          const int slot = tile == b0 / KB ? 0 : 1;
+          float* ps = a.part + ((size_t)(blockIdx.x * 2 + slot) * M) * kGvRows + rowt;
+          for (int m = 0; m < M; m++) ps[(size_t)m * kGvRows] = seg_sum(m);
+          epi_sync();
+          if (threadIdx.x == 64) {
+            unsigned int prev;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.count + tile) : "memory");
+            *last_flag = prev == (unsigned int)(c1 - c0) ? 1 : 0;
+          }
+          epi_sync();
+          if (*last_flag) {
+            // the contributors' partial rows, added in CTA order
+            for (int m0 = 0; m0 < M; m0 += 8) {
+              float y[8];
+#pragma unroll
+              for (int mm = 0; mm < 8; mm++) y[mm] = 0.f;
+#pragma unroll 4
+              for (int c = c0; c <= c1; c++) {
+                const int sl = tile == range_begin(c, T, G) / KB ? 0 : 1;
+                const float* pc = a.part + ((size_t)(c * 2 + sl) * M + m0) * kGvRows + rowt;
+                float v[8];
+#pragma unroll
+                for (int mm = 0; mm < 8; mm++) v[mm] = m0 + mm < M ? __ldcg(pc + (size_t)mm * kGvRows) : 0.f;
+#pragma unroll
+                for (int mm = 0; mm < 8; mm++) y[mm] += v[mm];
+              }
+              if (live) emit(m0, y, n);
+            }
+            if (threadIdx.x == 64) a.count[tile] = 0u;
+          }
+          epi_sync();
+        }
+        for (int c = 0; c < ncol; c++) acc_r[c * kGvRows] = 0.f;
+        it = seg_end;
+      }
+    } else {
     int seg = 0;
     for (int it = b0; it < b1; seg++) {
       const int tile = it / KB;
@@ -271,6 +436,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
         epi_sync();
       }
       it = seg_end;
+    }
     }
   } else if (INL) {
     // converters (warps 6..9): row scales, then the digit tiles; four stages
@@ -398,10 +564,12 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 // zero before a launch, zero again after it) and a scratch part for the
 // digit rows and row scales (unused when the kernel makes its own digits).
 struct GvLayout {
-  size_t count, acc, zeroed, dig, srow, scratch;
+  size_t count, acc, zeroed, dig, srow, part, scratch;
 };
 
-GvLayout gv_layout(int64_t M, int64_t N, int64_t K) {
+// per-group scales add the split tiles' fp32 partial rows: two slots of
+// M x 128 per CTA (at most one CTA per SM)
+GvLayout gv_layout(int64_t M, int64_t N, int64_t K, int64_t group = 0) {
   const int64_t ND = ((3 * M + 15) / 16) * 16;
   const int64_t tiles = (N + kGvRows - 1) / kGvRows;
   GvLayout L;
@@ -410,16 +578,17 @@ GvLayout gv_layout(int64_t M, int64_t N, int64_t K) {
   L.zeroed = L.acc + (((size_t)tiles * ND * kGvRows * 4 + 255) & ~(size_t)255);
   L.dig = 0;
   L.srow = (((size_t)(3 * M * K) + 255) & ~(size_t)255);
-  L.scratch = L.srow + (size_t)M * 4;
+  L.part = (L.srow + (size_t)M * 4 + 255) & ~(size_t)255;
+  L.scratch = group > 0 ? L.part + (size_t)sm_count() * 2 * M * kGvRows * 4 : L.srow + (size_t)M * 4;
   return L;
 }
 
-template <bool INL, int GKB>
+template <bool INL, int GKB, bool GRP>
 tb_status_t set_gv_smem() {
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
-    err = cudaFuncSetAttribute(gemv_tc_kernel<INL, GKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    err = cudaFuncSetAttribute(gemv_tc_kernel<INL, GKB, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(gemv_tc)");
   return TB_SUCCESS;
@@ -428,25 +597,52 @@ tb_status_t set_gv_smem() {
 }  // namespace
 
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(M, N, K).zeroed; }
-size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K) { return gv_layout(M, N, K).scratch; }
-
-bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K) {
-  return M >= 1 && M <= kGemvTcMaxM && gemm_tc_ok(q, M, N, K) && K % kGvSub == 0;
+size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K, int64_t group) {
+  return gv_layout(M, N, K, group).scratch;
 }
+
+bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group) {
+  return M >= 1 && M <= kGemvTcMaxM && gemm_tc_ok(q, M, N, K) && K % kGvSub == 0 &&
+         (group == 0 || (group > 0 && group % kGvSub == 0 && K % group == 0));
+}
+
+namespace {
+template <bool GRP>
+tb_status_t launch_gv(const cudaLaunchConfig_t& cfg, bool inl, int G, const CUtensorMap& tw, const CUtensorMap& tx,
+                      const GvArgs& a) {
+  if (inl && G == 2) {
+    TB_TRY((set_gv_smem<true, 2, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 2, GRP>, tw, tx, a));
+  } else if (inl) {
+    TB_TRY((set_gv_smem<true, 1, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 1, GRP>, tw, tx, a));
+  } else if (G == 2) {
+    TB_TRY((set_gv_smem<false, 2, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 2, GRP>, tw, tx, a));
+  } else {
+    TB_TRY((set_gv_smem<false, 1, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 1, GRP>, tw, tx, a));
+  }
+  return TB_SUCCESS;
+}
+}  // namespace
 
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st, const float* norm_w,
-                    float eps) {
-  const GvLayout L = gv_layout(M, N, K);
+                    float eps, int group) {
+  const GvLayout L = gv_layout(M, N, K, group);
   unsigned char* z = static_cast<unsigned char*>(zeroed);
   unsigned char* w = static_cast<unsigned char*>(scratch);
   // digit tiles made in the kernel for small M without a norm; otherwise the
   // digit kernel (which also applies the RMSNorm) writes them for TMA
   const bool inl = M <= kGvInlineM && !norm_w;
   const int ND = ((3 * M + 15) / 16) * 16;
+  const int acc_bytes = group > 0 ? ND * kGvRows * 4 : 0;  // per-group: fp32 column sums
   // two 128-byte sub-tiles per stage where K allows (halves the copies and
-  // doubles the contiguous run per weight row)
-  const int G = K % (2 * kGvSub) == 0 ? 2 : 1;
+  // doubles the contiguous run per weight row), unless the per-group column
+  // sums would leave fewer than three such stages
+  int G = K % (2 * kGvSub) == 0 ? 2 : 1;
+  if (G == 2 && group > 0 && (200 * 1024 - acc_bytes) / (2 * (kGvWSub + ND * kGvSub)) < 3) G = 1;
   const int kGvBK = kGvSub * G;
   const int kGvWTile = kGvWSub * G;
   const int KB = K / kGvBK;
@@ -455,9 +651,9 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   int grid = sm_count();
   if (grid > total) grid = total;
   const int stage_bytes = kGvWTile + ND * kGvBK;
-  int stages = (200 * 1024) / stage_bytes;  // as many weight boxes in flight as fit
+  int stages = (200 * 1024 - acc_bytes) / stage_bytes;  // as many weight boxes in flight as fit
   if (stages > 16) stages = 16;
-  const size_t smem = (size_t)stages * stage_bytes + 1024 + 512;
+  const size_t smem = (size_t)stages * stage_bytes + 1024 + 512 + acc_bytes;
   if (inl && (uintptr_t)x % 16 != 0) return TB_ERROR_NOT_SUPPORTED;
 
   EncodeTiledFn enc = encode_tiled();
@@ -488,8 +684,6 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
       return TB_ERROR_NOT_SUPPORTED;
     TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, norm_w, eps, st));
   }
-  TB_TRY(inl ? (G == 2 ? set_gv_smem<true, 2>() : set_gv_smem<true, 1>())
-             : (G == 2 ? set_gv_smem<false, 2>() : set_gv_smem<false, 1>()));
 
   GvArgs a{};
   a.out = out;
@@ -506,6 +700,9 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   a.KB = KB;
   a.total = total;
   a.stages = stages;
+  a.part = group > 0 ? reinterpret_cast<float*>(w + L.part) : nullptr;
+  a.gs = group > 0 ? group / kGvSub : 0;
+  a.ngroups = group > 0 ? K / group : 0;
   a.err = wait_timeout_word();
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
@@ -517,15 +714,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (inl && G == 2)
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 2>, tw, tx, a));
-  else if (inl)
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 1>, tw, tx, a));
-  else if (G == 2)
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 2>, tw, tx, a));
-  else
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 1>, tw, tx, a));
-  return TB_SUCCESS;
+  return group > 0 ? launch_gv<true>(cfg, inl, G, tw, tx, a) : launch_gv<false>(cfg, inl, G, tw, tx, a);
 }
 
 }  // namespace tb

@@ -164,15 +164,17 @@ tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* sc
 // by K blocks (split tiles finished by the last CTA to arrive).
 // `zeroed` (gemv_tc_zeroed_bytes) holds counters and split-tile sums and is
 // zero before and after each launch (zero_first: clear it first); `scratch`
-// (gemv_tc_scratch_bytes) holds the digit rows.
+// (gemv_tc_scratch_bytes) holds the digit rows (and, for per-group scales,
+// the split tiles' fp32 partial rows).  group > 0: scale is [N, K / group],
+// group a multiple of 128.
 constexpr int kGemvTcMaxM = 64;
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
-size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K);
-bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K);
+size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K, int64_t group = 0);
+bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group = 0);
 // norm_w != null: the product is of RMSNorm(x) * norm_w (the digit kernel applies it).
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st,
-                    const float* norm_w = nullptr, float eps = 0.f);
+                    const float* norm_w = nullptr, float eps = 0.f, int group = 0);
 
 // comm.cu: in-place NCCL allreduce on `st` (fp32 sum, or uint64 max for the
 // packed greedy keys); a no-op without a communicator or with one rank.

@@ -1,13 +1,15 @@
 """Quantized Linear microbench: tb_dequant_matmul_i8f32 on one GPU.
 
-    python -m tendo_b200.microbench [--M 1 8 32 128 2048] [--N 4096 11008] [--K 4096] [--iters 20]
+    python -m tendo_b200.microbench [--M 1 8 32 128 2048] [--N 4096 11008] [--K 4096] [--iters 20] [--group G]
     python -m tendo_b200.microbench --decode-layers 8 [--tokens 4]
 
 W [N, K] is drawn N(0, 0.02) (seed 42) and int8-quantized per output channel
-on the device; X [M, K] is N(0, 1) (seed 42).  Enough weight copies are
+on the device (per group of G input columns with --group G: scales [N, K/G]);
+X [M, K] is N(0, 1) (seed 42).  Enough weight copies are
 rotated that every launch streams its weights from HBM, not L2 (126 MB).
 Prints one JSON line per (M, N): microseconds per launch (CUDA events),
-achieved GB/s over the algorithmic bytes N*K + 4N + 4MK + 4MN (the M <= 32
+achieved GB/s over the algorithmic bytes N*K + 4N + 4MK + 4MN (4N*K/G for the
+scales of --group G; the M <= 32
 regime is HBM-bound) and TFLOP/s over 2MNK.
 
 --decode-layers L runs the batch-1 decode step of a Llama-7B-width model cut
@@ -27,17 +29,17 @@ import torch
 import tendo_b200 as tb
 
 
-def linear_bytes(M, N, K):
-    return N * K + 4 * N + 4 * M * K + 4 * M * N
+def linear_bytes(M, N, K, group=0):
+    return N * K + 4 * N * (K // group if group else 1) + 4 * M * K + 4 * M * N
 
 
-def run(Ms, Ns, K, iters, mode):
+def run(Ms, Ns, K, iters, mode, group=0):
     be = tb.Backend(0)
     dev = torch.device("cuda:0")
     rows = []
     for N in Ns:
         w = be.SynthNormal(N, K, 42, tb.STREAM_W, 0.02)
-        qt = be.Quantize(w, 0)
+        qt = be.Quantize(w, group)
         del w
         copies = max(2, math.ceil(400e6 / (N * K)))
         qs = [qt.data] + [qt.data.clone() for _ in range(copies - 1)]
@@ -50,7 +52,7 @@ def run(Ms, Ns, K, iters, mode):
             def launch(i):
                 nonlocal sh
                 tb.check(tb.lib.tb_dequant_matmul_i8f32_mode(out.data_ptr(), x.data_ptr(), qs[i % copies].data_ptr(),
-                                                             qt.scale.data_ptr(), M, N, K, 0, mode, sh))
+                                                             qt.scale.data_ptr(), M, N, K, group, mode, sh))
 
             for i in range(3):
                 launch(i)
@@ -70,8 +72,8 @@ def run(Ms, Ns, K, iters, mode):
             b.record(st)
             torch.cuda.synchronize()
             us = a.elapsed_time(b) * 1000.0 / iters
-            byts = linear_bytes(M, N, K)
-            row = {"M": M, "N": N, "K": K, "us": us, "GB_s": byts / (us * 1e-6) / 1e9,
+            byts = linear_bytes(M, N, K, group)
+            row = {"M": M, "N": N, "K": K, "group": group, "us": us, "GB_s": byts / (us * 1e-6) / 1e9,
                    "TFLOP_s": 2.0 * M * N * K / (us * 1e-6) / 1e12, "bytes": byts,
                    "regime": "gemv" if M <= 32 else "gemm", "weight_copies": copies}
             rows.append(row)
@@ -104,11 +106,12 @@ def main():
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--mode", type=int, default=tb.TB_GEMM_I8X3)
+    ap.add_argument("--group", type=int, default=0)
     a = ap.parse_args()
     if a.decode_layers > 0:
         decode_small(a.decode_layers, a.tokens)
     else:
-        run(a.M, a.N, a.K, a.iters, a.mode)
+        run(a.M, a.N, a.K, a.iters, a.mode, a.group)
 
 
 if __name__ == "__main__":

@@ -132,3 +132,58 @@ def test_gemv_tc_split_tiles_are_deterministic(oracle, be, cuda):
     a = be.DequantizeMatmul(xd, qd, sd, 0)
     for _ in range(3):
         assert torch.equal(a, be.DequantizeMatmul(xd, qd, sd, 0))
+
+
+# per-group scales (nn/quantize.go:126-187) on the same GEMV: (M, N, K, group)
+# with one group per 128-byte sub-tile (two per stage), groups spanning
+# stages (512, 1024), a stage of one sub-tile (K 384: group 384 = three
+# stages), N tails and a single tile spread over many CTAs (128 rows), the
+# digit-kernel path (M 17, 32).
+GEMV_GROUP_SHAPES = [(1, 4096, 4096, 128), (1, 11008, 4096, 128), (1, 4096, 11008, 128), (3, 300, 1024, 256),
+                     (5, 128, 4096, 512), (8, 4096, 4096, 1024), (1, 4096, 384, 384), (17, 1408, 512, 128),
+                     (32, 4096, 4096, 128), (2, 11008, 4096, 4096)]
+
+
+def _group_case(oracle, M, N, K, g, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    w[:, :g] *= 8.0  # the first group's scales differ from the rest
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    _, q, s = oracle.quantize(w, g)
+    return x, q, s
+
+
+@pytest.mark.parametrize("M,N,K,g", GEMV_GROUP_SHAPES)
+def test_gemv_tc_per_group_matches_oracle(oracle, tb, be, cuda, M, N, K, g):
+    assert tb.lib.tb_dequant_matmul_workspace_size(M, N, K, g, tb.TB_GEMM_I8X3) > 0  # the tensor-core path
+    x, q, s = _group_case(oracle, M, N, K, g, M * 17 + N + K + g)
+    got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(s, cuda), g))
+    want = oracle.dequant_matmul(x, q, s, g)
+    assert rel_err(got, want) <= TOL[0]
+
+
+def test_gemv_tc_per_group_is_deterministic_and_library_scratch_agrees(oracle, tb, be, cuda):
+    """Split tiles add their fp32 partial rows in CTA order: repeated calls,
+    and the library-scratch entry point, give identical bits."""
+    import torch
+
+    M, N, K, g = 4, 4096, 11008, 128
+    x, q, s = _group_case(oracle, M, N, K, g, 21)
+    xd, qd, sd = _t(x, cuda), _t(q, cuda), _t(s, cuda)
+    a = be.DequantizeMatmul(xd, qd, sd, g)
+    for _ in range(3):
+        assert torch.equal(a, be.DequantizeMatmul(xd, qd, sd, g))
+    b = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    tb.check(tb.lib.tb_dequant_matmul_i8f32(b.data_ptr(), xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), M, N, K, g,
+                                            tb._stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_gemv_per_group_below_128_takes_cuda_cores(oracle, tb, be, cuda):
+    """Groups that are not a multiple of 128 bytes run the CUDA-core GEMV."""
+    M, N, K, g = 3, 512, 1024, 64
+    assert tb.lib.tb_dequant_matmul_workspace_size(M, N, K, g, tb.TB_GEMM_I8X3) == 0
+    x, q, s = _group_case(oracle, M, N, K, g, 5)
+    got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(s, cuda), g))
+    assert rel_err(got, oracle.dequant_matmul(x, q, s, g)) <= 1e-4
