@@ -109,8 +109,9 @@ TB_API tb_status_t tb_dequant_matmul_i8f32_mode(float* out, const float* x, cons
                                          tb_gemm_mode_t mode, tb_stream_t stream);
 
 /* Scratch bytes tb_dequant_matmul_i8f32_ws needs for these sizes and mode
- * (0 when no scratch is used: TB_GEMM_SIMT, K not a multiple of 128,
- * per-group scales with M > 32 or a group that is not a multiple of 128). */
+ * (0 when no scratch is used: TB_GEMM_SIMT, M <= 32 with K not a multiple
+ * of 128, per-group scales with a group that is not a multiple of 128 or,
+ * for M > 32, more than 128 groups per row). */
 TB_API size_t tb_dequant_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
                                                tb_gemm_mode_t mode);
 

@@ -88,7 +88,8 @@ size_t dqmm_workspace(int64_t M, int64_t N, int64_t K, int64_t group_size, tb_ge
     if (K % 128 != 0 || (group_size > 0 && group_size % 128 != 0)) return 0;
     return tb::gemv_tc_zeroed_bytes(M, N, K) + tb::gemv_tc_scratch_bytes(M, N, K, group_size);
   }
-  if (group_size > 0) return 0;
+  // per-group: groups of a multiple of 128 and at most 128 groups per row
+  if (group_size > 0 && (group_size % 128 != 0 || K % group_size != 0 || K / group_size > 128)) return 0;
   return tb::gemm_tc_workspace(M, K, gemm_planes(mode));
 }
 
@@ -149,12 +150,16 @@ tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale
     return tb::gemv_generic(out, x, q, scale, (int)M, (int)N, (int)K, group_size > 0 ? (int)group_size : (int)K, st);
   }
   const size_t need = dqmm_workspace(M, N, K, group_size, mode);
-  if (need > 0 && tb::gemm_tc_ok(q, M, N, K) && (uintptr_t)x % 16 == 0) {
+  const bool tc = group_size > 0 ? tb::gemm_tc_grp_ok(q, M, N, K, group_size) : tb::gemm_tc_ok(q, M, N, K);
+  if (need > 0 && tc && (uintptr_t)x % 16 == 0) {
     if (arena) {
       TB_TRY(arena_get(0, need, &ws));
     } else {
       TB_REQUIRE(ws && ws_bytes >= need);
     }
+    if (group_size > 0)
+      return tb::gemm_tc_grp(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, (int)group_size, gemm_planes(mode), ws,
+                             st);
     return tb::gemm_tc(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, gemm_planes(mode), ws, st);
   }
   if (!arena && need > 0) TB_REQUIRE(ws && ws_bytes >= need);

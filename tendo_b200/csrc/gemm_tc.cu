@@ -239,6 +239,178 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, C::kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// per-group scales [N, K / group] (group a multiple of 128): the same digit
+// planes and MMAs on a 128 x 64 tile, with an accumulator hand-off per group.
+//   warp 0 lane 0: TMA producer (NP digit tiles + a 64-row weight tile per
+//     128-byte K block);
+//   warp 1 lane 0: MMA issuer — a group's NP plane accumulators (NP x 64
+//     columns) go to one of two TMEM buffers, committed to the epilogue at
+//     the group's last K block;
+//   warps 2..5: epilogue — thread = output row (its TMEM lane); per group,
+//     y = D0 + D1 / 128 (+ D2 / 128^2) per column, times scale[n, group]
+//     (staged in shared memory for the tile's 64 rows), added into 64 fp32
+//     registers; out = s_m * sum (+ resid) at the end.
+// ---------------------------------------------------------------------------
+constexpr int kGgBN = 64;                          // weight rows per tile (MMA N)
+constexpr int kGgWTile = kGgBN * kTcBK;            // 8 KB
+constexpr int kGgStages = 3;
+constexpr int kGgThreads = 192;
+constexpr int kGgMaxScales = 8192;                 // 64 rows x up to 128 groups
+template <int NP>
+struct GgCfg {
+  static constexpr int kStageBytes = NP * kTcTile + kGgWTile;
+  static constexpr size_t kSmem = (size_t)kGgStages * kStageBytes + 1024 + 256 + kGgMaxScales * 4;
+};
+
+template <int NP>
+__global__ void __launch_bounds__(kGgThreads, 1)
+    gemm_tc_grp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       float* out, const float* __restrict__ srow, const float* __restrict__ scale,
+                       const float* resid, int M, int N, int K, int gs, int ng, int vec_ok, int* err) {
+  using C = GgCfg<NP>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kGgStages * C::kStageBytes);
+  uint64_t* empty = full + kGgStages;
+  uint64_t* tfull = empty + kGgStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  float* sc_s = reinterpret_cast<float*>(smem + (size_t)kGgStages * C::kStageBytes + 256);  // [64][ng]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kTcBM, n0 = blockIdx.y * kGgBN;
+  const int nk = K / kTcBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGgStages; s++) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbarrier_init(&tfull[b], 1);
+      mbarrier_init(&tempty[b], 4);  // one arrival per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % kGgStages, use = kb / kGgStages;
+        if (use > 0) mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), err);
+        unsigned char* st = smem + (size_t)s * C::kStageBytes;
+        mbarrier_expect_tx(&full[s], (uint32_t)C::kStageBytes);
+#pragma unroll
+        for (int p = 0; p < NP; p++) tma_load_3d(st + p * kTcTile, &tmA, kb * kTcBK, m0, p, &full[s]);
+        tma_load_2d(st + NP * kTcTile, &tmB, kb * kTcBK, n0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(kTcBM, kGgBN);
+      int h = 0;
+      uint32_t d = tmem;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % kGgStages, use = kb / kGgStages;
+        const bool first = kb % gs == 0;
+        if (first) {
+          const int buf = h & 1;
+          if (h >= 2) mbarrier_wait(&tempty[buf], (uint32_t)(((h - 2) >> 1) & 1), err);
+          d = tmem + (uint32_t)(buf * 256);
+        }
+        mbarrier_wait(&full[s], (uint32_t)(use & 1), err);
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(smem + (size_t)s * C::kStageBytes);
+        const uint32_t b0 = a0 + NP * kTcTile;
+#pragma unroll
+        for (int kk = 0; kk < kTcBK / 32; kk++) {
+#pragma unroll
+          for (int p = 0; p < NP; p++)
+            tc_mma_i8(d + p * kGgBN, sw128_desc(a0 + p * kTcTile + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                      !(first && kk == 0));
+        }
+        tc_commit(&empty[s]);
+        if ((kb + 1) % gs == 0) {
+          tc_commit(&tfull[h & 1]);
+          h++;
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;  // 0..127
+    // the tile's scales, [64 rows][ng groups]
+    for (int i = et; i < kGgBN * ng; i += 128) {
+      const int j = i / ng, n = n0 + j;
+      sc_s[i] = n < N ? __ldg(scale + (size_t)n * ng + (i - j * ng)) : 0.f;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    float acc[kGgBN];
+#pragma unroll
+    for (int j = 0; j < kGgBN; j++) acc[j] = 0.f;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    for (int g = 0; g < ng; g++) {
+      const int buf = g & 1;
+      mbarrier_wait(&tfull[buf], (uint32_t)((g >> 1) & 1), err);
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kGgBN; c += 32) {
+        uint32_t v[NP][32];
+#pragma unroll
+        for (int p = 0; p < NP; p++) tmem_ld32(lane_base + (uint32_t)(buf * 256 + p * kGgBN + c), v[p]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int p = 0; p < NP; p++) pin32(v[p]);
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          float y = (float)(int)v[0][e] + (float)(int)v[1][e] * (1.0f / 128.0f);
+          if (NP == 3) y += (float)(int)v[NP - 1][e] * (1.0f / 16384.0f);
+          acc[c + e] = __fmaf_rn(y, sc_s[(c + e) * ng + g], acc[c + e]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbarrier_arrive(&tempty[buf]);
+    }
+    const int row = m0 + q * 32 + lane;
+    if (row < M) {
+      const float sr = srow[row];
+      float* orow = out + (size_t)row * N;
+      const float* rrow = resid ? resid + (size_t)row * N : nullptr;
+#pragma unroll
+      for (int j = 0; j < kGgBN; j += 4) {
+        const int n = n0 + j;
+        if (vec_ok && n + 3 < N) {
+          float4 o = make_float4(sr * acc[j], sr * acc[j + 1], sr * acc[j + 2], sr * acc[j + 3]);
+          if (rrow) {
+            const float4 r = *reinterpret_cast<const float4*>(rrow + n);
+            o.x += r.x;
+            o.y += r.y;
+            o.z += r.z;
+            o.w += r.w;
+          }
+          *reinterpret_cast<float4*>(orow + n) = o;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; e++)
+            if (n + e < N) orow[n + e] = rrow ? sr * acc[j + e] + rrow[n + e] : sr * acc[j + e];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 template <int NP>
 tb_status_t launch_tc(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
                       const float* resid, int M, int N, int K, cudaStream_t st) {
@@ -281,6 +453,47 @@ tb_status_t launch_tc(float* out, const int8_t* dig, const float* srow, const in
   return check_launch("gemm_tc_kernel");
 }
 
+template <int NP>
+tb_status_t launch_tc_grp(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
+                          const float* resid, int M, int N, int K, int group, cudaStream_t st) {
+  using C = GgCfg<NP>;
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return TB_ERROR_NOT_SUPPORTED;
+  CUtensorMap ta, tbm;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, (cuuint64_t)NP};
+    const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)M * (cuuint64_t)K};
+    const cuuint32_t box[3] = {kTcBK, kTcBM, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(dig), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TB_ERROR_NOT_SUPPORTED;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {kTcBK, kGgBN};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TB_ERROR_NOT_SUPPORTED;
+  }
+  static std::once_flag once[2];
+  static cudaError_t attr_err[2];
+  std::call_once(once[NP - 2], [] {
+    attr_err[NP - 2] =
+        cudaFuncSetAttribute(gemm_tc_grp_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+  });
+  if (attr_err[NP - 2] != cudaSuccess) return cuda_fail(attr_err[NP - 2], "cudaFuncSetAttribute(gemm_tc_grp)");
+  const int vec_ok = (N % 4 == 0) && ((uintptr_t)out % 16 == 0) && (!resid || (uintptr_t)resid % 16 == 0);
+  const dim3 grid((M + kTcBM - 1) / kTcBM, (N + kGgBN - 1) / kGgBN);
+  gemm_tc_grp_kernel<NP><<<grid, kGgThreads, C::kSmem, st>>>(ta, tbm, out, srow, scale, resid, M, N, K,
+                                                             group / kTcBK, K / group, vec_ok, wait_timeout_word());
+  return check_launch("gemm_tc_grp_kernel");
+}
+
 }  // namespace
 
 size_t gemm_tc_workspace(int64_t M, int64_t K, int planes) {
@@ -311,6 +524,22 @@ tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const 
   if (M <= 0 || N <= 0) return TB_SUCCESS;
   if (planes == 3) return launch_tc<3>(out, dig, srow, q, scale, resid, M, N, K, st);
   return launch_tc<2>(out, dig, srow, q, scale, resid, M, N, K, st);
+}
+
+bool gemm_tc_grp_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group) {
+  return group > 0 && group % kTcBK == 0 && K % group == 0 && (K / group) * kGgBN <= kGgMaxScales &&
+         gemm_tc_ok(q, M, N, K) && N <= 65535 * kGgBN;
+}
+
+tb_status_t gemm_tc_grp(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                        int N, int K, int group, int planes, void* ws, cudaStream_t st) {
+  int8_t* dig = static_cast<int8_t*>(ws);
+  float* srow = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + gemm_tc_workspace(M, K, planes) -
+                                         (size_t)M * sizeof(float));
+  if (M <= 0 || N <= 0) return TB_SUCCESS;
+  TB_TRY(gemm_tc_digits(dig, srow, x, M, K, planes, nullptr, 0.f, st));
+  if (planes == 3) return launch_tc_grp<3>(out, dig, srow, q, scale, resid, M, N, K, group, st);
+  return launch_tc_grp<2>(out, dig, srow, q, scale, resid, M, N, K, group, st);
 }
 
 tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,

@@ -158,6 +158,11 @@ tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const 
 // digits + GEMM with the digit rows in `ws` (gemm_tc_workspace bytes).
 tb_status_t gemm_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, int planes, void* ws, cudaStream_t st);
+// per-group scales [N, K / group] (group a multiple of 128, K / group <= 128):
+// digits + the grouped GEMM, digit rows in `ws` (gemm_tc_workspace bytes).
+bool gemm_tc_grp_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group);
+tb_status_t gemm_tc_grp(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                        int N, int K, int group, int planes, void* ws, cudaStream_t st);
 
 // gemv_tc.cu: the same product for 1 <= M <= kGemvTcMaxM on tcgen05 with the
 // weights as the 128-row MMA operand and the work split evenly over the SMs

@@ -93,9 +93,31 @@ def test_gemm_tc_zero_and_extreme_rows(oracle, be, cuda):
             assert rel_err(got[r:r + 1], want) <= TOL[0]
 
 
-def test_gemm_tc_per_group_takes_cuda_cores(oracle, be, cuda):
-    """group_size > 0 (nn/quantize.go:126-187) runs the CUDA-core GEMM."""
-    M, N, K, g = 64, 256, 512, 128
+# per-group scales (nn/quantize.go:126-187) on the tensor-core GEMM, 128 x 64
+# tiles with a hand-off per group: M and N tails, groups of one and several
+# K blocks, the 7B prefill shapes (86 groups per row at K 11008).
+GEMM_GROUP_SHAPES = [(33, 128, 512, 128), (129, 300, 1024, 256), (300, 1408, 512, 512), (512, 4096, 4096, 128),
+                     (512, 11008, 4096, 128), (512, 4096, 11008, 128), (200, 4096, 4096, 4096)]
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("M,N,K,g", GEMM_GROUP_SHAPES)
+def test_gemm_tc_per_group_matches_oracle(oracle, tb, be, cuda, M, N, K, g, mode):
+    assert tb.lib.tb_dequant_matmul_workspace_size(M, N, K, g, mode) > 0  # the tensor-core path
+    rng = np.random.default_rng(M + N + K + g)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    w[:, :g] *= 8.0
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    _, q, s = oracle.quantize(w, g)
+    got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(s, cuda), g, mode=mode))
+    rows = sorted(set([0, M // 2, M - 1] + [int(r) for r in rng.integers(0, M, 5)]))
+    assert rel_err(got[rows], oracle.dequant_matmul(x[rows], q, s, g)) <= TOL[mode]
+
+
+def test_gemm_per_group_below_128_takes_cuda_cores(oracle, tb, be, cuda):
+    """Groups that are not a multiple of 128 bytes run the CUDA-core GEMM."""
+    M, N, K, g = 64, 256, 512, 64
+    assert tb.lib.tb_dequant_matmul_workspace_size(M, N, K, g, tb.TB_GEMM_I8X3) == 0
     rng = np.random.default_rng(3)
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     x = rng.standard_normal((M, K)).astype(np.float32)

@@ -140,7 +140,9 @@ def test_argument_validation_needs_no_gpu(tb):
     # otherwise; a short workspace is rejected before any launch
     assert L.tb_dequant_matmul_workspace_size(32, 4096, 4096, 0, tb.TB_GEMM_I8X3) >= 3 * 32 * 4096 + 32 * 4
     assert L.tb_dequant_matmul_workspace_size(1, 4096, 4000, 0, tb.TB_GEMM_I8X3) == 0  # K % 128: CUDA-core GEMV
-    assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 128, tb.TB_GEMM_I8X3) == 0  # per-group GEMM: CUDA cores
+    # per-group GEMM: the digit rows of the tensor-core path, unless a row has more than 128 groups
+    assert L.tb_dequant_matmul_workspace_size(64, 4096, 4096, 128, tb.TB_GEMM_I8X3) == 3 * 64 * 4096 + 64 * 4
+    assert L.tb_dequant_matmul_workspace_size(64, 4096, 32768, 128, tb.TB_GEMM_I8X3) == 0
     # per-group decode regime: the tensor-core GEMV adds fp32 partial-row slots
     assert L.tb_dequant_matmul_workspace_size(8, 4096, 4096, 128, tb.TB_GEMM_I8X3) > \
         L.tb_dequant_matmul_workspace_size(8, 4096, 4096, 0, tb.TB_GEMM_I8X3)
