@@ -288,6 +288,17 @@ TB_API tb_status_t tb_allreduce_sum_f32(tb_comm* comm, float* buf, int64_t n, tb
  * divisible by nranks.  Every rank calls the same model functions in the
  * same order. */
 TB_API tb_status_t tb_model_create_tp(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm);
+
+/* Model options for tb_model_create_ex. */
+#define TB_MODEL_KV_BF16 1u /* KV cache in bf16 (rounded to nearest even when
+                             * appended): half the cache bytes; a numerics
+                             * change against the reference's fp32 cache.
+                             * Decodes through the tcgen05 GEMV path (batch
+                             * <= 64) or the per-step kernels. */
+
+/* tb_model_create / tb_model_create_tp (comm may be null) with options. */
+TB_API tb_status_t tb_model_create_ex(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm,
+                                      uint32_t flags);
 TB_API tb_status_t tb_model_destroy(tb_model* m);
 /* Synthetic weights: N(0, 0.02) from (seed, stream = layer * 8 + matrix),
  * quantized per channel on the device; gains 1.0; embedding and lm_head fp32. */

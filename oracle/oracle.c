@@ -331,6 +331,7 @@ struct or_model {
   float* lm_head; /* [V][d] */
   float* kc;      /* [layers][B][Hkv][max_seq][D] */
   float* vc;
+  int kv_bf16;    /* values rounded to bf16 as they are appended */
   float* cos_t;
   float* sin_t;
 };
@@ -440,6 +441,31 @@ float* or_model_kcache(or_model* m, int layer) { return m->kc + layer * kv_layer
 float* or_model_vcache(or_model* m, int layer) { return m->vc + layer * kv_layer_elems(m); }
 void or_model_reset(or_model* m) { m->pos = 0; }
 void or_model_set_pos(or_model* m, int64_t pos) { m->pos = pos; }
+void or_model_set_kv_bf16(or_model* m, int on) { m->kv_bf16 = on != 0; }
+
+/* Round to nearest even at bit 16 of the fp32 pattern: the bf16 value with the
+ * upper 16 bits (NaN stays NaN). */
+float or_round_bf16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) {
+    u |= 0x00400000u;
+  } else {
+    u += 0x7FFFu + ((u >> 16) & 1u);
+  }
+  u &= 0xFFFF0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+/* dst[0..n) = src, rounded to bf16 when the model keeps a bf16 cache */
+static void kv_store(const or_model* m, float* dst, const float* src, int64_t n) {
+  if (!m->kv_bf16) {
+    memcpy(dst, src, sizeof(float) * (size_t)n);
+    return;
+  }
+  for (int64_t i = 0; i < n; i++) dst[i] = or_round_bf16(src[i]);
+}
 int64_t or_model_pos(const or_model* m) { return m->pos; }
 
 /* models/llama/quantized.go:229-382 for one layer, batch-major activations
@@ -474,9 +500,8 @@ static void attention_layer(or_model* m, int l, const float* xn, int64_t S, floa
   for (int64_t b = 0; b < B; b++)
     for (int64_t h = 0; h < Hkv; h++)
       for (int64_t s = 0; s < S; s++) {
-        memcpy(kc + ((b * Hkv + h) * Ms + P + s) * D, kh + ((b * Hkv + h) * S + s) * D, sizeof(float) * (size_t)D);
-        memcpy(vc + ((b * Hkv + h) * Ms + P + s) * D, scratch_v + (b * S + s) * Hkv * D + h * D,
-               sizeof(float) * (size_t)D);
+        kv_store(m, kc + ((b * Hkv + h) * Ms + P + s) * D, kh + ((b * Hkv + h) * S + s) * D, D);
+        kv_store(m, vc + ((b * Hkv + h) * Ms + P + s) * D, scratch_v + (b * S + s) * Hkv * D + h * D, D);
       }
   float scale = 1.0f / (float)sqrt((double)D);
   int64_t rep = H / Hkv;

@@ -108,6 +108,10 @@ float* or_model_vcache(or_model* m, int layer);
 
 void or_model_reset(or_model* m); /* empties the KV cache */
 void or_model_set_pos(or_model* m, int64_t pos); /* cache length (timing samples) */
+/* on != 0: K and V are rounded to bf16 (nearest even) as they are appended,
+ * the restatement of a bf16 KV cache; off (default): the reference's fp32 cache. */
+void or_model_set_kv_bf16(or_model* m, int on);
+float or_round_bf16(float x); /* fp32 -> nearest-even bf16 value, as fp32 */
 int64_t or_model_pos(const or_model* m);
 
 /* QuantizedModel.Forward (models/llama/quantized.go:125-178) over tokens[B, S]

@@ -89,6 +89,9 @@ def lib():
         L.or_model_vcache.restype = _f32p
         L.or_model_reset.argtypes = [ctypes.c_void_p]
         L.or_model_set_pos.argtypes = [ctypes.c_void_p, _i64]
+        L.or_model_set_kv_bf16.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.or_round_bf16.argtypes = [ctypes.c_float]
+        L.or_round_bf16.restype = ctypes.c_float
         L.or_model_pos.argtypes = [ctypes.c_void_p]
         L.or_model_pos.restype = _i64
         L.or_model_forward.argtypes = [ctypes.c_void_p, _i64p, _i64, _f32p, _f32p, _f32p]
@@ -297,6 +300,10 @@ class Model:
 
     def set_pos(self, pos: int):
         lib().or_model_set_pos(self.h, pos)
+
+    def set_kv_bf16(self, on: bool = True):
+        """K and V rounded to bf16 as they are appended (a bf16 KV cache)."""
+        lib().or_model_set_kv_bf16(self.h, 1 if on else 0)
 
     @property
     def pos(self) -> int:

@@ -29,6 +29,8 @@ TB_GEMM_I8X3 = 0
 TB_GEMM_I8X2 = 1
 TB_GEMM_SIMT = 2
 
+TB_MODEL_KV_BF16 = 1
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -68,6 +70,7 @@ SIGNATURES = [
     ("tb_synth_tokens_host", _st, [_vp, _i64, _i64, ctypes.c_uint64]),
     ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
     ("tb_model_create_tp", _st, [_vp, _vp, ctypes.c_int, _vp]),
+    ("tb_model_create_ex", _st, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_uint32]),
     ("tb_sample_f32", _st, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float, _vp, _vp]),
     ("tb_model_generate_sample", _st, [_vp, _vp, _i64, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float,
                                        ctypes.c_uint64, _vp]),
@@ -461,17 +464,24 @@ class Comm:
 
 class QuantizedModel:
     """QuantizedModel (models/llama/quantized.go) on one GPU, B sequences in
-    lockstep; with ``comm``, this rank's tensor-parallel share of it."""
+    lockstep; with ``comm``, this rank's tensor-parallel share of it.
+    ``kv_bf16``: the KV cache in bf16 (TB_MODEL_KV_BF16), half the cache bytes,
+    values rounded to nearest even as they are appended."""
 
-    def __init__(self, cfg: dict, batch: int = 1, device: int = 0, comm: "Comm | None" = None):
+    def __init__(self, cfg: dict, batch: int = 1, device: int = 0, comm: "Comm | None" = None,
+                 kv_bf16: bool = False):
         self.cfg = dict(cfg)
         self.B = batch
         self.device = device
         self.comm = comm
+        self.kv_bf16 = kv_bf16
         c = ModelConfig(cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"],
                         cfg["max_seq"], cfg["rope_base"], cfg["eps"], batch)
         h = ctypes.c_void_p()
-        if comm is None:
+        if kv_bf16:
+            check(lib.tb_model_create_ex(ctypes.byref(h), ctypes.byref(c), device, comm.h if comm else None,
+                                         TB_MODEL_KV_BF16))
+        elif comm is None:
             check(lib.tb_model_create(ctypes.byref(h), ctypes.byref(c), device))
         else:
             check(lib.tb_model_create_tp(ctypes.byref(h), ctypes.byref(c), device, comm.h))

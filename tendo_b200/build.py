@@ -1,6 +1,6 @@
 """Builds libtendo_b200.so in-tree with nvcc for sm_100a.
 
-    python -m tendo_b200.build          # or: python tendo_b200/build.py
+    python tendo_b200/build.py   (loads no library: works before the first build)
 
 Each .cu under csrc/ is compiled to an object in tendo_b200/_build/ (rebuilt
 when it or a header is newer), then linked into tendo_b200/libtendo_b200.so

@@ -4,7 +4,8 @@
 // over keys, P . V; GQA reads kv head h / (H / Hkv) directly
 // (models/llama/forward.go:345-370) instead of materialising the repeat.
 //
-// Decode (Sq = 1) is HBM-bound on the fp32 cache: split-K over positions,
+// Decode (Sq = 1) is HBM-bound on the cache (fp32 as the reference stores
+// it, or bf16 as a model option): split-K over positions,
 // one CTA per (split, kv head, sequence) serving all H / Hkv query heads of
 // that kv head (each K/V row is read once), online softmax per warp, then a
 // combine kernel merges the splits.  Prefill is a tiled (flash-style) fp32
@@ -47,6 +48,20 @@ __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
     r[0] = t.x; r[1] = t.y;
   }
 }
+// bf16 cache rows: VEC consecutive elements widened to fp32 (exact)
+template <int VEC>
+__device__ __forceinline__ void load_vec(float (&r)[VEC], const __nv_bfloat16* p) {
+  if constexpr (VEC == 4) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    r[0] = __uint_as_float(t.x << 16); r[1] = __uint_as_float(t.x & 0xffff0000u);
+    r[2] = __uint_as_float(t.y << 16); r[3] = __uint_as_float(t.y & 0xffff0000u);
+  } else if constexpr (VEC == 2) {
+    const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
+    r[0] = __uint_as_float(t << 16); r[1] = __uint_as_float(t & 0xffff0000u);
+  } else {
+    r[0] = __bfloat162float(*p);
+  }
+}
 
 // grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv
 // head; W warps (8 when G >= 4: the G running softmaxes take registers, so
@@ -54,7 +69,7 @@ __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
 // tiles of U consecutive positions: U K rows and U V rows are loaded at once
 // (2 U 16-byte loads in flight per lane for D = 128), the U scores reduced
 // together, and the running softmax updated once per tile.
-template <int VEC, int G, int W>
+template <int VEC, int G, int W, typename KT>
 __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int D = VEC * 32;
   constexpr int U = 8;
@@ -73,13 +88,13 @@ __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
   chunk = (chunk + U - 1) / U * U;
   const int64_t start = (int64_t)split * chunk;
   const int64_t end = min(start + chunk, sk);
-  const float* kb = a.kcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  const float* vb = a.vcache + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const KT* kb = static_cast<const KT*>(a.kcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const KT* vb = static_cast<const KT*>(a.vcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
   if (threadIdx.x == 0 && a.l2_prefetch) {
     const int64_t pend = min(end, sk - 1);  // row sk - 1 comes from the preceding kernel
     if (pend > start) {
-      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
-      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
+      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(KT)));
+      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * sizeof(KT)));
     }
   }
   pdl_wait();
@@ -225,10 +240,10 @@ __global__ void attn_combine_kernel(float* out, const float* partial, int B, int
 // ---------------------------------------------------------------------------
 constexpr int BQ = 32, BK = 16, KU = BK / 8, kPfThreads = 256;
 
-template <int D>
+template <int D, typename KT>
 __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, const float* __restrict__ q,
-                                                                   const float* __restrict__ kc,
-                                                                   const float* __restrict__ vc, int H, int Hkv,
+                                                                   const KT* __restrict__ kc,
+                                                                   const KT* __restrict__ vc, int H, int Hkv,
                                                                    int Sq, int64_t Sk, int max_seq, float scale) {
   __shared__ float Qs[BQ][D + 1];
   __shared__ float Ks[BK][D + 1];
@@ -245,8 +260,8 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, co
     const int qq = q0 + r;
     Qs[r][e] = qq < Sq ? q[(((size_t)b * Sq + qq) * H + h) * D + e] : 0.f;
   }
-  const float* kb = kc + ((size_t)b * Hkv + kvh) * max_seq * D;
-  const float* vb = vc + ((size_t)b * Hkv + kvh) * max_seq * D;
+  const KT* kb = kc + ((size_t)b * Hkv + kvh) * max_seq * D;
+  const KT* vb = vc + ((size_t)b * Hkv + kvh) * max_seq * D;
   constexpr int OV = D / 8;
   float o[OV];
 #pragma unroll
@@ -260,8 +275,8 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, co
       const int r = i / D, e = i - r * D;
       const int64_t kk = k0 + r;
       const bool ok = kk < Sk;
-      Ks[r][e] = ok ? kb[kk * D + e] : 0.f;
-      Vs[r][e] = ok ? vb[kk * D + e] : 0.f;
+      Ks[r][e] = ok ? kv_get(kb + kk * D + e) : 0.f;
+      Vs[r][e] = ok ? kv_get(vb + kk * D + e) : 0.f;
     }
     __syncthreads();
     float s[KU];
@@ -317,7 +332,7 @@ template <int VEC, int G>
 tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
   // the older rows are prefetched into L2 only while a layer's whole cache
   // fits in it comfortably (a batch-1 step); larger caches stream directly
-  a.l2_prefetch = (double)a.B * a.Hkv * a.max_seq * (a.D * 8.0) <= 96e6;
+  a.l2_prefetch = (double)a.B * a.Hkv * a.max_seq * (a.D * (a.kv_bf16 ? 4.0 : 8.0)) <= 96e6;
   constexpr int W = G >= 4 ? 8 : 4;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
@@ -328,7 +343,8 @@ tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W>, a);
+  cudaError_t e = a.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W, __nv_bfloat16>, a)
+                            : cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W, float>, a);
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
   const int warps = a.B * a.H;
   cfg.gridDim = dim3((warps + 3) / 4);
@@ -374,20 +390,30 @@ tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   return TB_ERROR_NOT_SUPPORTED;
 }
 
-tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const float* vcache, int B, int H,
-                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st) {
-  TB_REQUIRE(Hkv > 0 && H % Hkv == 0 && Sq >= 1 && Sk >= Sq);
+template <typename KT>
+tb_status_t launch_prefill(float* out, const float* q, const KT* kc, const KT* vc, int B, int H, int Hkv, int Sq,
+                           int64_t Sk, int D, int max_seq, float scale, cudaStream_t st) {
   dim3 grid((Sq + BQ - 1) / BQ, H, B);
-  if (D == 128) {
-    attn_prefill_kernel<128><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
-  } else if (D == 64) {
-    attn_prefill_kernel<64><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
-  } else if (D == 32) {
-    attn_prefill_kernel<32><<<grid, kPfThreads, 0, st>>>(out, q, kcache, vcache, H, Hkv, Sq, Sk, max_seq, scale);
-  } else {
+  if (D == 128)
+    attn_prefill_kernel<128, KT><<<grid, kPfThreads, 0, st>>>(out, q, kc, vc, H, Hkv, Sq, Sk, max_seq, scale);
+  else if (D == 64)
+    attn_prefill_kernel<64, KT><<<grid, kPfThreads, 0, st>>>(out, q, kc, vc, H, Hkv, Sq, Sk, max_seq, scale);
+  else if (D == 32)
+    attn_prefill_kernel<32, KT><<<grid, kPfThreads, 0, st>>>(out, q, kc, vc, H, Hkv, Sq, Sk, max_seq, scale);
+  else
     return TB_ERROR_NOT_SUPPORTED;
-  }
   return check_launch("attn_prefill_kernel");
+}
+
+tb_status_t attn_prefill(float* out, const float* q, const void* kcache, const void* vcache, int B, int H,
+                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st,
+                         bool kv_bf16) {
+  TB_REQUIRE(Hkv > 0 && H % Hkv == 0 && Sq >= 1 && Sk >= Sq);
+  if (kv_bf16)
+    return launch_prefill(out, q, static_cast<const __nv_bfloat16*>(kcache), static_cast<const __nv_bfloat16*>(vcache),
+                          B, H, Hkv, Sq, Sk, D, max_seq, scale, st);
+  return launch_prefill(out, q, static_cast<const float*>(kcache), static_cast<const float*>(vcache), B, H, Hkv, Sq,
+                        Sk, D, max_seq, scale, st);
 }
 
 }  // namespace tb

@@ -2,6 +2,7 @@
 // checks, host-side fault injection, small device utilities).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -28,6 +29,13 @@ int sm_count();
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 inline unsigned ceil_div(int64_t a, int64_t b) { return (unsigned)((a + b - 1) / b); }
+
+// KV cache elements: fp32 (the reference's cache) or bf16 (a model option;
+// rounded to nearest even on the way in, widened exactly on the way out).
+__device__ __forceinline__ void kv_put(float* p, float v) { *p = v; }
+__device__ __forceinline__ void kv_put(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ float kv_get(const float* p) { return *p; }
+__device__ __forceinline__ float kv_get(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 }  // namespace tb
 

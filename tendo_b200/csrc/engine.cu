@@ -37,7 +37,8 @@ struct tb_model {
   float *sqkv = nullptr, *so = nullptr, *sgate = nullptr, *sup = nullptr, *sdown = nullptr;
   float *attn_norm = nullptr, *mlp_norm = nullptr, *final_norm = nullptr;
   float *embed = nullptr, *lm_head = nullptr, *cos_t = nullptr, *sin_t = nullptr;
-  float *kc = nullptr, *vc = nullptr;
+  void *kc = nullptr, *vc = nullptr;  // fp32, or bf16 with kv16
+  bool kv16 = false;                   // bf16 KV cache (TB_MODEL_KV_BF16)
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *u = nullptr;
   float *qbuf = nullptr, *partial = nullptr, *logits = nullptr, *last = nullptr;
   unsigned long long* keys = nullptr;
@@ -84,6 +85,12 @@ tb_status_t dalloc(tb_model* m, T** p, size_t count) {
   m->allocs.push_back(v);
   *p = (T*)v;
   return TB_SUCCESS;
+}
+
+// layer l's slice of a KV cache [L][B][Hkv][max_seq][D] of either element type
+void* kv_layer(const tb_model* m, void* base, int64_t l) {
+  const size_t elems = (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+  return static_cast<unsigned char*>(base) + elems * (m->kv16 ? 2 : 4);
 }
 
 __global__ void fill_kernel(float* p, int64_t n, float v) {
@@ -150,8 +157,8 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     lin_ptr(m, (int)l, 4, &wg, &sg);
     lin_ptr(m, (int)l, 5, &wu, &su);
     lin_ptr(m, (int)l, 6, &wd, &sd);
-    float* kcl = m->kc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
-    float* vcl = m->vc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    void* kcl = kv_layer(m, m->kc, l);
+    void* vcl = kv_layer(m, m->vc, l);
     // attention block (models/llama/quantized.go:186-199)
     if (tc) {
       TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->h, (int)rows, (int)m->d, kTcPlanes, m->attn_norm + l * m->d,
@@ -164,7 +171,7 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     }
     TB_TRY(tb::rope_rows(m->qkv, m->cos_t, m->sin_t, m->B, S, m->H, m->D, P, m->NQKV, st));
     TB_TRY(tb::kv_append_rope(kcl, vcl, m->qkv + m->H * m->D, m->qkv + (m->H + m->Hkv) * m->D, m->cos_t, m->sin_t,
-                              m->B, m->Hkv, S, m->D, P, m->Ms, m->NQKV, st));
+                              m->B, m->Hkv, S, m->D, P, m->Ms, m->NQKV, st, m->kv16));
     // q rows have stride NQKV; the attention kernels take [B, S, H, D] rows of H * D
     TB_CUDA(cudaMemcpy2DAsync(m->g, sizeof(float) * m->H * m->D, m->qkv, sizeof(float) * m->NQKV,
                               sizeof(float) * m->H * m->D, rows, cudaMemcpyDeviceToDevice, st));
@@ -184,10 +191,11 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
       a.max_seq = (int)m->Ms;
       a.nsplit = m->nsplit;
       a.scale = scale;
+      a.kv_bf16 = m->kv16;
       TB_TRY(tb::attn_decode(a, st, false));
     } else {
       TB_TRY(tb::attn_prefill(m->attn, m->g, kcl, vcl, (int)m->B, (int)m->H, (int)m->Hkv, (int)S, P + S, (int)m->D,
-                              (int)m->Ms, scale, st));
+                              (int)m->Ms, scale, st, m->kv16));
     }
     // o projection + residual; row-parallel under tensor parallelism: each
     // rank's partial product, the residual on rank 0 only, summed over ranks
@@ -300,8 +308,8 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     lin_ptr(m, (int)l, 4, &wg, &sg);
     lin_ptr(m, (int)l, 5, &wu, &su);
     lin_ptr(m, (int)l, 6, &wd, &sd);
-    float* kcl = m->kc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
-    float* vcl = m->vc + (size_t)l * m->B * m->Hkv * m->Ms * m->D;
+    void* kcl = kv_layer(m, m->kc, l);
+    void* vcl = kv_layer(m, m->vc, l);
     tb::QkvArgs qa{};
     qa.h = m->h;
     qa.norm_w = m->attn_norm + l * m->d;
@@ -312,8 +320,8 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     qa.sin_t = m->sin_t;
     qa.pos = m->pos;
     qa.qout = m->qbuf;
-    qa.kcache = kcl;
-    qa.vcache = vcl;
+    qa.kcache = static_cast<float*>(kcl);  // the fused QKV kernels: fp32 caches only
+    qa.vcache = static_cast<float*>(vcl);
     qa.M = (int)m->B;
     qa.d = (int)m->d;
     qa.H = (int)m->H;
@@ -330,7 +338,7 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
         TB_TRY(tb::gemv_tc(m->qkv, m->h, wq, sq, nullptr, B, (int)m->NQKV, d, m->gv_zero, false, m->gv_scratch, st,
                            m->attn_norm + l * m->d, m->c.eps));
         return tb::qkv_rope_append(m->qbuf, kcl, vcl, m->qkv, m->cos_t, m->sin_t, m->pos, m->B, m->H, m->Hkv, m->D,
-                                   m->Ms, st);
+                                   m->Ms, st, m->kv16);
       }
       if (kind == 2) return tb::gemv_tc(m->h, m->attn, wo, so, resid, B, d, HD, m->gv_zero, false, m->gv_scratch, st);
       if (kind == 3) {
@@ -348,8 +356,8 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
         tb::QkvArgs g = qa;
         g.h = m->h + b0 * m->d;
         g.qout = m->qbuf + b0 * m->H * m->D;
-        g.kcache = kcl + b0 * m->Hkv * m->Ms * m->D;
-        g.vcache = vcl + b0 * m->Hkv * m->Ms * m->D;
+        g.kcache = qa.kcache + b0 * m->Hkv * m->Ms * m->D;
+        g.vcache = qa.vcache + b0 * m->Hkv * m->Ms * m->D;
         g.M = (int)(m->B - b0 < 8 ? m->B - b0 : 8);
         TB_TRY(tb::gemv_qkv_rope(g, st, pdl));
       }
@@ -369,6 +377,7 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     aa.max_seq = (int)m->Ms;
     aa.nsplit = m->nsplit;
     aa.scale = scale;
+    aa.kv_bf16 = m->kv16;
     if (kind == 1) return tb::attn_decode(aa, st, pdl);
     // row-parallel under tensor parallelism: the residual joins on rank 0 and
     // the step sums the ranks' partial products after the kernel
@@ -481,8 +490,8 @@ tb::MkArgs mk_args(tb_model* m) {
   a.lm_head = m->lm_head;
   a.cos_t = m->cos_t;
   a.sin_t = m->sin_t;
-  a.kc = m->kc;
-  a.vc = m->vc;
+  a.kc = static_cast<float*>(m->kc);  // the persistent kernel runs fp32 caches only
+  a.vc = static_cast<float*>(m->vc);
   a.h = m->h;
   a.q = m->qbuf;
   a.partial = m->partial;
@@ -526,8 +535,9 @@ tb_status_t build_graph(tb_model* m) {
 
 namespace {
 
-tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm) {
+tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm, uint32_t flags) {
   TB_REQUIRE(out && cfg);
+  TB_REQUIRE((flags & ~(uint32_t)TB_MODEL_KV_BF16) == 0);
   *out = nullptr;
   TB_REQUIRE(cfg->vocab > 0 && cfg->dim > 0 && cfg->layers > 0 && cfg->heads > 0 && cfg->kv_heads > 0);
   TB_REQUIRE(cfg->dim % cfg->heads == 0 && cfg->heads % cfg->kv_heads == 0 && cfg->hidden > 0);
@@ -541,6 +551,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->c = *cfg;
   m->device = device;
   m->comm = comm;
+  m->kv16 = (flags & TB_MODEL_KV_BF16) != 0;
   m->tp = tp;
   m->tp_rank = rank;
   m->Hg = cfg->heads;
@@ -568,7 +579,9 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     // K % 128 and an sm_100 device; probed with an aligned stand-in pointer)
     const void* al = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
     const int64_t HD = m->H * m->D;
-    m->gv = m->B > 1 && m->B <= tb::kGemvTcMaxM && tb::gemv_tc_ok(al, m->B, m->NQKV, m->d) &&
+    // (a bf16 cache takes this path at batch 1 too: its RoPE / append kernel
+    // writes either cache type)
+    m->gv = (m->B > 1 || m->kv16) && m->B <= tb::kGemvTcMaxM && tb::gemv_tc_ok(al, m->B, m->NQKV, m->d) &&
             tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, m->F, m->d) &&
             tb::gemv_tc_ok(al, m->B, m->d, m->F);
   }
@@ -580,13 +593,13 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     if (tb::gemv_smem_bytes(r, (int)m->d) <= 200 * 1024) m->lm_rows = r;
   m->fused = m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 && (m->D == 64 || m->D == 128) &&
              (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 || m->H / m->Hkv == 8) &&
-             (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024));
+             (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024 && !m->kv16));
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);
   {
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
-    m->mk = !(e && e[0] == '0') && tp == 1 &&
+    m->mk = !(e && e[0] == '0') && tp == 1 && !m->kv16 &&
             tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
     int ns = tb::sm_count() / (int)m->Hkv;  // about one attention unit per SM
     if (ns < 1) ns = 1;
@@ -616,9 +629,14 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->lm_head, (size_t)m->V * m->d));
   A(dalloc(m, &m->cos_t, (size_t)m->Ms * (m->D / 2)));
   A(dalloc(m, &m->sin_t, (size_t)m->Ms * (m->D / 2)));
-  const size_t kv = L * m->B * m->Hkv * m->Ms * m->D;
-  A(dalloc(m, &m->kc, kv));
-  A(dalloc(m, &m->vc, kv));
+  const size_t kv = L * m->B * m->Hkv * m->Ms * m->D * (m->kv16 ? 2 : 4);  // bytes
+  {
+    unsigned char *kc = nullptr, *vc = nullptr;
+    A(dalloc(m, &kc, kv));
+    A(dalloc(m, &vc, kv));
+    m->kc = kc;
+    m->vc = vc;
+  }
   const size_t R = (size_t)m->rows_max;
   A(dalloc(m, &m->h, R * m->d));
   A(dalloc(m, &m->xn, R * m->d));
@@ -678,8 +696,8 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     cudaError_t e = cudaMemcpy(m->cos_t, ct.data(), ct.size() * sizeof(float), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(m->sin_t, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(m->keys, 0, sizeof(unsigned long long) * m->B);
-    if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv * sizeof(float));
-    if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv);
+    if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv);
     if (e == cudaSuccess) e = cudaMemset(m->pos, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->step, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->bad, 0, sizeof(int32_t));
@@ -700,13 +718,19 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
 
 extern "C" tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, int device) {
   TB_INJECT("tb_model_create");
-  return create_model(out, cfg, device, nullptr);
+  return create_model(out, cfg, device, nullptr, 0);
 }
 
 extern "C" tb_status_t tb_model_create_tp(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm) {
   TB_INJECT("tb_model_create");
   TB_REQUIRE(comm);
-  return create_model(out, cfg, device, comm);
+  return create_model(out, cfg, device, comm, 0);
+}
+
+extern "C" tb_status_t tb_model_create_ex(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm,
+                                          uint32_t flags) {
+  TB_INJECT("tb_model_create");
+  return create_model(out, cfg, device, comm, flags);
 }
 
 extern "C" tb_status_t tb_model_destroy(tb_model* m) {

@@ -49,8 +49,8 @@ struct LmHeadArgs {
 
 struct AttnDecodeArgs {
   const float* q;       // [B, H, D]
-  const float* kcache;  // [B, Hkv, max_seq, D]
-  const float* vcache;
+  const void* kcache;   // [B, Hkv, max_seq, D] fp32 (bf16 with kv_bf16)
+  const void* vcache;
   float* out;           // [B, H, D]
   float* partial;       // [B, H, nsplit, D + 2] workspace
   const int64_t* pos;   // device position of the newest key (Sk = *pos + 1); null: use sk
@@ -58,6 +58,7 @@ struct AttnDecodeArgs {
   int B, H, Hkv, D, max_seq, nsplit;
   float scale;
   bool l2_prefetch;  // set by the launcher
+  bool kv_bf16;
 };
 
 // decode_mk.cu: the whole batch-1 decode step as one persistent kernel.
@@ -141,8 +142,9 @@ bool l2_prefetch_enabled();
 int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq);
 size_t attn_decode_workspace(int B, int H, int D, int nsplit);
 tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
-tb_status_t attn_prefill(float* out, const float* q, const float* kcache, const float* vcache, int B, int H,
-                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st);
+tb_status_t attn_prefill(float* out, const float* q, const void* kcache, const void* vcache, int B, int H,
+                         int Hkv, int Sq, int64_t Sk, int D, int max_seq, float scale, cudaStream_t st,
+                         bool kv_bf16 = false);
 
 // gemm_tc.cu: the prefill-regime quantized Linear on the 5th-generation
 // tensor cores.  x rows are split into `planes` int8 digit rows
@@ -204,18 +206,19 @@ tb_status_t embedding(float* out, const float* table, const int64_t* ids, int64_
                       int32_t* bad, cudaStream_t st, bool pdl);
 tb_status_t rmsnorm(float* out, float* resid_out, const float* in, const float* resid, const float* w, int64_t rows,
                     int64_t d, float eps, cudaStream_t st);
-tb_status_t kv_append_rope(float* kc, float* vc, const float* k, const float* v, const float* cos_t,
+// kc, vc: fp32 caches, or bf16 ones with kv_bf16
+tb_status_t kv_append_rope(void* kc, void* vc, const float* k, const float* v, const float* cos_t,
                            const float* sin_t, int64_t B, int64_t Hkv, int64_t S, int64_t D, int64_t pos,
-                           int64_t max_seq, int64_t ld, cudaStream_t st);
+                           int64_t max_seq, int64_t ld, cudaStream_t st, bool kv_bf16 = false);
 tb_status_t rope_rows(float* x, const float* cos_t, const float* sin_t, int64_t B, int64_t S, int64_t Hx, int64_t D,
                       int64_t pos, int64_t ld, cudaStream_t st);
 tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, cudaStream_t st);
 // Decode step, B rows of qkv [B][(H + 2 Hkv) D]: RoPE on the q and k heads at
 // the device position *pos; q heads to q [B][H][D], k and v heads to the
-// caches [B][Hkv][max_seq][D] at *pos (v unrotated).
-tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, const float* cos_t, const float* sin_t,
+// caches [B][Hkv][max_seq][D] at *pos (v unrotated; fp32, or bf16 with kv_bf16).
+tb_status_t qkv_rope_append(float* q, void* kc, void* vc, const float* qkv, const float* cos_t, const float* sin_t,
                             const int64_t* pos, int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t max_seq,
-                            cudaStream_t st);
+                            cudaStream_t st, bool kv_bf16 = false);
 tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st);
 // The sampler's uniforms for the token the last step generated, and the
 // history entry of that step set to the (sampled) tokens.

@@ -83,11 +83,11 @@ __global__ void rope_rows_kernel(float* x, const float* __restrict__ cos_t, cons
 }
 
 // k, v [B, S, Hkv, D] (row stride ld) -> caches [B, Hkv, max_seq, D] at
-// positions pos..pos+S-1, RoPE applied to k on the way.
-__global__ void kv_append_rope_kernel(float* kc, float* vc, const float* __restrict__ k,
-                                      const float* __restrict__ v, const float* __restrict__ cos_t,
-                                      const float* __restrict__ sin_t, int64_t B, int64_t Hkv, int64_t S, int64_t D,
-                                      int64_t pos, int64_t max_seq, int64_t ld) {
+// positions pos..pos+S-1, RoPE applied to k on the way; KT is the cache element.
+template <typename KT>
+__global__ void kv_append_rope_kernel(KT* kc, KT* vc, const float* __restrict__ k, const float* __restrict__ v,
+                                      const float* __restrict__ cos_t, const float* __restrict__ sin_t, int64_t B,
+                                      int64_t Hkv, int64_t S, int64_t D, int64_t pos, int64_t max_seq, int64_t ld) {
   const int64_t half = D / 2;
   const int64_t total = B * S * Hkv * half;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -97,18 +97,19 @@ __global__ void kv_append_rope_kernel(float* kc, float* vc, const float* __restr
     const int64_t b = t / (half * Hkv * S);
     const float* ks = k + (b * S + s) * ld + hh * D;
     const float* vs = v + (b * S + s) * ld + hh * D;
-    float* kd = kc + ((b * Hkv + hh) * max_seq + pos + s) * D;
-    float* vd = vc + ((b * Hkv + hh) * max_seq + pos + s) * D;
+    KT* kd = kc + ((b * Hkv + hh) * max_seq + pos + s) * D;
+    KT* vd = vc + ((b * Hkv + hh) * max_seq + pos + s) * D;
     const float c = cos_t[(pos + s) * half + i], sn = sin_t[(pos + s) * half + i];
     const float x0 = ks[i], x1 = ks[i + half];
-    kd[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-    kd[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-    vd[i] = vs[i];
-    vd[i + half] = vs[i + half];
+    kv_put(kd + i, __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    kv_put(kd + i + half, __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+    kv_put(vd + i, vs[i]);
+    kv_put(vd + i + half, vs[i + half]);
   }
 }
 
-__global__ void qkv_rope_append_kernel(float* q, float* kc, float* vc, const float* __restrict__ qkv,
+template <typename KT>
+__global__ void qkv_rope_append_kernel(float* q, KT* kc, KT* vc, const float* __restrict__ qkv,
                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                        const int64_t* pos_p, int64_t B, int64_t H, int64_t Hkv, int64_t D,
                                        int64_t max_seq) {
@@ -123,13 +124,21 @@ __global__ void qkv_rope_append_kernel(float* q, float* kc, float* vc, const flo
     const float x0 = src[i], x1 = src[i + half];
     if (hh < H + Hkv) {
       const float c = cos_t[pos * half + i], sn = sin_t[pos * half + i];
-      float* d = hh < H ? q + (b * H + hh) * D : kc + ((b * Hkv + (hh - H)) * max_seq + pos) * D;
-      d[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      d[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+      const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      const float r1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+      if (hh < H) {
+        float* d = q + (b * H + hh) * D;
+        d[i] = r0;
+        d[i + half] = r1;
+      } else {
+        KT* d = kc + ((b * Hkv + (hh - H)) * max_seq + pos) * D;
+        kv_put(d + i, r0);
+        kv_put(d + i + half, r1);
+      }
     } else {
-      float* d = vc + ((b * Hkv + (hh - H - Hkv)) * max_seq + pos) * D;
-      d[i] = x0;
-      d[i + half] = x1;
+      KT* d = vc + ((b * Hkv + (hh - H - Hkv)) * max_seq + pos) * D;
+      kv_put(d + i, x0);
+      kv_put(d + i + half, x1);
     }
   }
 }
@@ -267,13 +276,18 @@ tb_status_t rmsnorm(float* out, float* resid_out, const float* in, const float* 
   return check_launch("rmsnorm_kernel");
 }
 
-tb_status_t kv_append_rope(float* kc, float* vc, const float* k, const float* v, const float* cos_t,
+tb_status_t kv_append_rope(void* kc, void* vc, const float* k, const float* v, const float* cos_t,
                            const float* sin_t, int64_t B, int64_t Hkv, int64_t S, int64_t D, int64_t pos,
-                           int64_t max_seq, int64_t ld, cudaStream_t st) {
+                           int64_t max_seq, int64_t ld, cudaStream_t st, bool kv_bf16) {
   const int64_t total = B * S * Hkv * (D / 2);
   if (total == 0) return TB_SUCCESS;
-  kv_append_rope_kernel<<<grid_1d(total, 256), 256, 0, st>>>(kc, vc, k, v, cos_t, sin_t, B, Hkv, S, D, pos, max_seq,
-                                                             ld);
+  if (kv_bf16)
+    kv_append_rope_kernel<<<grid_1d(total, 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(kc),
+                                                               static_cast<__nv_bfloat16*>(vc), k, v, cos_t, sin_t, B,
+                                                               Hkv, S, D, pos, max_seq, ld);
+  else
+    kv_append_rope_kernel<<<grid_1d(total, 256), 256, 0, st>>>(static_cast<float*>(kc), static_cast<float*>(vc), k, v,
+                                                               cos_t, sin_t, B, Hkv, S, D, pos, max_seq, ld);
   return check_launch("kv_append_rope_kernel");
 }
 
@@ -298,13 +312,19 @@ tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, c
   return check_launch("argmax_kernel");
 }
 
-tb_status_t qkv_rope_append(float* q, float* kc, float* vc, const float* qkv, const float* cos_t, const float* sin_t,
+tb_status_t qkv_rope_append(float* q, void* kc, void* vc, const float* qkv, const float* cos_t, const float* sin_t,
                             const int64_t* pos, int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t max_seq,
-                            cudaStream_t st) {
+                            cudaStream_t st, bool kv_bf16) {
   const int64_t total = B * (H + 2 * Hkv) * (D / 2);
   if (total == 0) return TB_SUCCESS;
   const int64_t blocks = (total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096;
-  qkv_rope_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, kc, vc, qkv, cos_t, sin_t, pos, B, H, Hkv, D, max_seq);
+  if (kv_bf16)
+    qkv_rope_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, static_cast<__nv_bfloat16*>(kc),
+                                                             static_cast<__nv_bfloat16*>(vc), qkv, cos_t, sin_t, pos,
+                                                             B, H, Hkv, D, max_seq);
+  else
+    qkv_rope_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, static_cast<float*>(kc), static_cast<float*>(vc), qkv,
+                                                             cos_t, sin_t, pos, B, H, Hkv, D, max_seq);
   return check_launch("qkv_rope_append_kernel");
 }
 
