@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--workload", default="llama7b", choices=["llama7b", "llama70b-tp", "llama7b-serving"])
+    ap.add_argument("--kv-bf16", action="store_true",
+                    help="llama7b-serving only: the bf16 KV cache option (a numerics change; off by default)")
     return ap.parse_args()
 
 
@@ -543,14 +545,15 @@ SERVE_SEQS, SERVE_PROMPT, SERVE_NEW, SERVE_KV = 64, 1024, 32, 1280
 METRIC_SERVE = "int8 Llama-7B batched serving decode tok/s (64 sequences, greedy, replicas)"
 
 
-def step_bytes_serve(P, seqs):
+def step_bytes_serve(P, seqs, kv_bytes=4):
     """Algorithmic bytes of one decode step of `seqs` sequences on one replica
-    at cache position P: the weights once, every sequence's KV rows 0..P."""
+    at cache position P: the weights once, every sequence's KV rows 0..P
+    (kv_bytes per element: 4 fp32, 2 with the bf16 cache option)."""
     c = CFG
     d, H, Hkv, F, V, L = c["dim"], c["heads"], c["kv_heads"], c["hidden"], c["vocab"], c["layers"]
     D = d // H
     w = L * ((H + 2 * Hkv) * D * d + d * H * D + 3 * F * d) + V * d * 4
-    kv = L * 2 * Hkv * D * (P + 1) * 4 * seqs
+    kv = L * 2 * Hkv * D * (P + 1) * kv_bytes * seqs
     return w + kv
 
 
@@ -570,7 +573,8 @@ def run_serving(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     import tendo_b200 as tb
 
-    qm = tb.QuantizedModel(dict(CFG, max_seq=SERVE_KV), batch=B, device=local)
+    kv16 = bool(getattr(args, "kv_bf16", False))
+    qm = tb.QuantizedModel(dict(CFG, max_seq=SERVE_KV), batch=B, device=local, kv_bf16=kv16)
     qm.init_synthetic(0)
     stream = torch.cuda.ExternalStream(qm.stream_handle, device=dev)
     start = tb.synth_tokens(B, CFG["vocab"], 7 + rank)
@@ -613,16 +617,17 @@ def run_serving(args):
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     ms_tok = ms / (args.steps * SERVE_NEW)
-    per_gpu = statistics.mean(step_bytes_serve(SERVE_PROMPT + i, B) for i in range(SERVE_NEW))
+    per_gpu = statistics.mean(step_bytes_serve(SERVE_PROMPT + i, B, 2 if kv16 else 4) for i in range(SERVE_NEW))
     achieved = per_gpu / (ms_tok / 1000.0) / 1e9
     toks = qm.tokens(SERVE_NEW + 1)[:, 0]
     if rank == 0:
         line = {
             "metric": METRIC_SERVE, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8/fp32, bf16 KV" if kv16 else "int8/fp32", "data": "synthetic",
             "config": {"workload": f"llama7b-int8-serving: 64 sequences as {world} replicas of {B}; decode from "
-                                   "position 1024 (prompt KV zeros); 32 greedy tokens per step; KV 1280 positions",
+                                   "position 1024 (prompt KV zeros); 32 greedy tokens per step; KV 1280 positions"
+                                   + ("; bf16 KV cache option" if kv16 else ""),
                        "global_batch": SERVE_SEQS, "seq_len": SERVE_PROMPT + SERVE_NEW,
                        "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2: 7 GB weights + KV per step"},
