@@ -768,6 +768,8 @@ void fill_sizes(MkArgs& a, int grid) {
 
 }  // namespace
 
+size_t megakernel_partial_bytes(int H, int D, int nsplit) { return (size_t)H * nsplit * (D + 4) * sizeof(float); }
+
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch) {
   if (batch != 1) return false;
   if (d % 64 || (H * D) % 64 || F % 64 || (4 * d) % 64) return false;

@@ -646,7 +646,16 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->g, gw));
   A(dalloc(m, &m->u, R * m->F));
   A(dalloc(m, &m->qbuf, (size_t)m->B * m->H * m->D));
-  A(dalloc(m, &m->partial, tb::attn_decode_workspace((int)m->B, (int)m->H, (int)m->D, m->nsplit) / sizeof(float)));
+  {
+    // split partials of the decode attention: the per-step kernels' layout
+    // and, at batch 1, the persistent kernel's (its rows are D + 4 floats)
+    size_t pb = tb::attn_decode_workspace((int)m->B, (int)m->H, (int)m->D, m->nsplit);
+    if (m->mk) {
+      const size_t mb = tb::megakernel_partial_bytes((int)m->H, (int)m->D, m->mk_nsplit);
+      if (mb > pb) pb = mb;
+    }
+    A(dalloc(m, &m->partial, pb / sizeof(float)));
+  }
   A(dalloc(m, &m->logits, (size_t)m->B * m->V));
   A(dalloc(m, &m->last, (size_t)m->B * m->d));
   A(dalloc(m, &m->keys, (size_t)m->B));

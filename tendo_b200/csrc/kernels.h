@@ -104,6 +104,8 @@ struct MkArgs {
   size_t merge_bytes;
 };
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch);
+// Bytes of MkArgs::partial: H heads x nsplit splits x (D + 4) floats.
+size_t megakernel_partial_bytes(int H, int D, int nsplit);
 tb_status_t megakernel_launch(MkArgs a, cudaStream_t st);
 
 // gemv.cu
