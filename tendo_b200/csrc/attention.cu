@@ -5,7 +5,7 @@
 // (models/llama/forward.go:345-370) instead of materialising the repeat.
 //
 // Decode (Sq = 1) is HBM-bound on the cache (fp32 as the reference stores
-// it, or bf16 as a model option): split-K over positions,
+// it, or bf16 as a model option, read with its own 16-byte-load kernel): split-K over positions,
 // one CTA per (split, kv head, sequence) serving all H / Hkv query heads of
 // that kv head (each K/V row is read once), online softmax per warp, then a
 // combine kernel merges the splits.  Prefill is a tiled (flash-style) fp32
@@ -48,28 +48,13 @@ __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
     r[0] = t.x; r[1] = t.y;
   }
 }
-// bf16 cache rows: VEC consecutive elements widened to fp32 (exact)
-template <int VEC>
-__device__ __forceinline__ void load_vec(float (&r)[VEC], const __nv_bfloat16* p) {
-  if constexpr (VEC == 4) {
-    const uint2 t = *reinterpret_cast<const uint2*>(p);
-    r[0] = __uint_as_float(t.x << 16); r[1] = __uint_as_float(t.x & 0xffff0000u);
-    r[2] = __uint_as_float(t.y << 16); r[3] = __uint_as_float(t.y & 0xffff0000u);
-  } else if constexpr (VEC == 2) {
-    const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
-    r[0] = __uint_as_float(t << 16); r[1] = __uint_as_float(t & 0xffff0000u);
-  } else {
-    r[0] = __bfloat162float(*p);
-  }
-}
-
 // grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv
 // head; W warps (8 when G >= 4: the G running softmaxes take registers, so
 // fewer CTAs fit per SM and each needs more rows in flight).  Each warp takes
 // tiles of U consecutive positions: U K rows and U V rows are loaded at once
 // (2 U 16-byte loads in flight per lane for D = 128), the U scores reduced
 // together, and the running softmax updated once per tile.
-template <int VEC, int G, int W, typename KT>
+template <int VEC, int G, int W>
 __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int D = VEC * 32;
   constexpr int U = 8;
@@ -88,13 +73,13 @@ __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
   chunk = (chunk + U - 1) / U * U;
   const int64_t start = (int64_t)split * chunk;
   const int64_t end = min(start + chunk, sk);
-  const KT* kb = static_cast<const KT*>(a.kcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
-  const KT* vb = static_cast<const KT*>(a.vcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const float* kb = static_cast<const float*>(a.kcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const float* vb = static_cast<const float*>(a.vcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
   if (threadIdx.x == 0 && a.l2_prefetch) {
     const int64_t pend = min(end, sk - 1);  // row sk - 1 comes from the preceding kernel
     if (pend > start) {
-      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(KT)));
-      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * sizeof(KT)));
+      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
+      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * sizeof(float)));
     }
   }
   pdl_wait();
@@ -181,6 +166,160 @@ __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
     if (m != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kAttnWarps; w++) {
+        const float c = expf(sm_ml[w][gi][0] - m);
+        L = fmaf(sm_ml[w][gi][1], c, L);
+        O = fmaf(sm_o[w][gi][e], c, O);
+      }
+    }
+    float* part = a.partial + (((size_t)b * a.H + kvh * G + gi) * a.nsplit + split) * (D + 2);
+    part[e] = O;
+    if (e == 0) {
+      part[D] = m;
+      part[D + 1] = L;
+    }
+  }
+}
+
+// bf16 cache (D = 32, 64 or 128): each lane loads 16 bytes (8 elements) of a row,
+// so LR = D / 8 lanes cover a row and a warp load covers RW = 32 / LR rows.
+// A tile is UU such loads per lane (U = UU RW rows) of K and of V; a lane
+// keeps the scores and P V products of its own rows, the row groups agree on
+// the tile's max and sum through shuffles, and the partial outputs of the row
+// groups are added once at the end (they share every rescaling).  Same grid,
+// split and partial-output format as attn_decode_kernel.
+template <int D, int G, int W, int UU>
+__global__ void __launch_bounds__(W * 32) attn_decode_b16_kernel(AttnDecodeArgs a) {
+  constexpr int LR = D / 8, RW = 32 / LR, U = UU * RW;
+  __shared__ float sm_o[W][G][D];
+  __shared__ float sm_ml[W][G][2];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rl = lane / LR, el = (lane % LR) * 8;
+  const int64_t sk = a.pos ? (*a.pos + 1) : a.sk;
+  int64_t chunk = (sk + a.nsplit - 1) / a.nsplit;
+  chunk = (chunk + U - 1) / U * U;
+  const int64_t start = (int64_t)split * chunk;
+  const int64_t end = min(start + chunk, sk);
+  const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(a.kcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  const __nv_bfloat16* vb = static_cast<const __nv_bfloat16*>(a.vcache) + ((size_t)b * a.Hkv + kvh) * a.max_seq * D;
+  if (threadIdx.x == 0 && a.l2_prefetch) {
+    const int64_t pend = min(end, sk - 1);  // row sk - 1 comes from the preceding kernel
+    if (pend > start) {
+      prefetch_l2_bulk(kb + start * D, (uint32_t)((pend - start) * D * 2));
+      prefetch_l2_bulk(vb + start * D, (uint32_t)((pend - start) * D * 2));
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
+  float qr[G][8];
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+    const float* qp = a.q + ((size_t)b * a.H + kvh * G + gi) * D + el;
+    const float4 q0 = *reinterpret_cast<const float4*>(qp), q1 = *reinterpret_cast<const float4*>(qp + 4);
+    qr[gi][0] = q0.x; qr[gi][1] = q0.y; qr[gi][2] = q0.z; qr[gi][3] = q0.w;
+    qr[gi][4] = q1.x; qr[gi][5] = q1.y; qr[gi][6] = q1.z; qr[gi][7] = q1.w;
+  }
+  float mx[G], l[G], o[G][8];
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+    mx[gi] = -INFINITY;
+    l[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[gi][e] = 0.f;
+  }
+  for (int64_t j0 = start + (int64_t)warp * U; j0 < end; j0 += (int64_t)W * U) {
+    uint4 kr[UU], vr[UU];
+#pragma unroll
+    for (int u = 0; u < UU; u++) {
+      const int64_t j = j0 + u * RW + rl;
+      if (j < end) {
+        kr[u] = *reinterpret_cast<const uint4*>(kb + j * D + el);
+        vr[u] = *reinterpret_cast<const uint4*>(vb + j * D + el);
+      } else {
+        kr[u] = make_uint4(0u, 0u, 0u, 0u);
+        vr[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int gi = 0; gi < G; gi++) {
+      float s[UU];
+#pragma unroll
+      for (int u = 0; u < UU; u++) {
+        const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+        float d = 0.f;
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          d = fmaf(qr[gi][2 * h], __uint_as_float(w[h] << 16), d);
+          d = fmaf(qr[gi][2 * h + 1], __uint_as_float(w[h] & 0xffff0000u), d);
+        }
+        s[u] = d;
+      }
+      // the row's dot product over its LR lanes
+#pragma unroll
+      for (int o2 = LR / 2; o2 > 0; o2 >>= 1)
+#pragma unroll
+        for (int u = 0; u < UU; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < UU; u++) {
+        s[u] = (j0 + u * RW + rl < end) ? s[u] * a.scale : -INFINITY;
+        tmax = fmaxf(tmax, s[u]);
+      }
+      // the tile's max over the row groups
+#pragma unroll
+      for (int o2 = LR; o2 < 32; o2 <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o2));
+      const float mn = fmaxf(mx[gi], tmax);  // finite: row j0 < end is valid
+      const float corr = expf(mx[gi] - mn);
+      float psum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[gi][e] *= corr;
+#pragma unroll
+      for (int u = 0; u < UU; u++) {
+        const float p = expf(s[u] - mn);
+        psum += p;
+        const uint32_t w[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          o[gi][2 * h] = fmaf(p, __uint_as_float(w[h] << 16), o[gi][2 * h]);
+          o[gi][2 * h + 1] = fmaf(p, __uint_as_float(w[h] & 0xffff0000u), o[gi][2 * h + 1]);
+        }
+      }
+#pragma unroll
+      for (int o2 = LR; o2 < 32; o2 <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o2);
+      l[gi] = l[gi] * corr + psum;
+      mx[gi] = mn;
+    }
+  }
+  // add the row groups' partial outputs, then merge the warps of this CTA
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      float v = o[gi][e];
+#pragma unroll
+      for (int o2 = LR; o2 < 32; o2 <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
+      o[gi][e] = v;
+    }
+    if (rl == 0) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) sm_o[warp][gi][el + e] = o[gi][e];
+    }
+    if (lane == 0) {
+      sm_ml[warp][gi][0] = mx[gi];
+      sm_ml[warp][gi][1] = l[gi];
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < G * D; t += W * 32) {
+    const int gi = t / D, e = t - gi * D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; w++) m = fmaxf(m, sm_ml[w][gi][0]);
+    float L = 0.f, O = 0.f;
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < W; w++) {
         const float c = expf(sm_ml[w][gi][0] - m);
         L = fmaf(sm_ml[w][gi][1], c, L);
         O = fmaf(sm_o[w][gi][e], c, O);
@@ -343,8 +482,11 @@ tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = a.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W, __nv_bfloat16>, a)
-                            : cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W, float>, a);
+  // a bf16 cache: 16-byte loads of 8 elements (attn_decode_b16_kernel); UU
+  // loads per lane per tile, fewer where the G softmaxes take the registers
+  constexpr int UU = G <= 2 ? 8 : (G == 4 ? 4 : 2);
+  cudaError_t e = a.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_decode_b16_kernel<VEC * 32, G, W, UU>, a)
+                            : cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W>, a);
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
   const int warps = a.B * a.H;
   cfg.gridDim = dim3((warps + 3) / 4);
