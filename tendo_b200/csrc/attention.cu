@@ -467,6 +467,47 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(float* out, co
   }
 }
 
+// a bf16 cache: 16-byte loads of 8 elements (attn_decode_b16_kernel); loads
+// per lane per tile, fewer where the G softmaxes take the registers
+template <int G>
+constexpr int b16_loads() {
+  return G <= 2 ? 8 : (G == 4 ? 4 : 2);
+}
+
+// Resident CTAs per SM of the decode kernel for these shapes (0: none).
+template <int VEC, int G>
+int decode_occupancy_g(bool kv16) {
+  constexpr int W = G >= 4 ? 8 : 4;
+  int n = 0;
+  const cudaError_t e =
+      kv16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_b16_kernel<VEC * 32, G, W, b16_loads<G>()>,
+                                                           W * 32, 0)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_kernel<VEC, G, W>, W * 32, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <int VEC>
+int decode_occupancy_v(int G, bool kv16) {
+  switch (G) {
+    case 1: return decode_occupancy_g<VEC, 1>(kv16);
+    case 2: return decode_occupancy_g<VEC, 2>(kv16);
+    case 4: return decode_occupancy_g<VEC, 4>(kv16);
+    case 8: return VEC == 1 && !kv16 ? 0 : decode_occupancy_g<VEC, 8>(kv16);
+    default: return 0;
+  }
+}
+
+int decode_occupancy(int D, int G, bool kv16) {
+  if (D == 128) return decode_occupancy_v<4>(G, kv16);
+  if (D == 64) return decode_occupancy_v<2>(G, kv16);
+  if (D == 32) return decode_occupancy_v<1>(G, kv16);
+  return 0;
+}
+
 template <int VEC, int G>
 tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
   // the older rows are prefetched into L2 only while a layer's whole cache
@@ -482,9 +523,7 @@ tb_status_t launch_decode(AttnDecodeArgs a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  // a bf16 cache: 16-byte loads of 8 elements (attn_decode_b16_kernel); UU
-  // loads per lane per tile, fewer where the G softmaxes take the registers
-  constexpr int UU = G <= 2 ? 8 : (G == 4 ? 4 : 2);
+  constexpr int UU = b16_loads<G>();
   cudaError_t e = a.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_decode_b16_kernel<VEC * 32, G, W, UU>, a)
                             : cudaLaunchKernelEx(&cfg, attn_decode_kernel<VEC, G, W>, a);
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_kernel");
@@ -510,14 +549,32 @@ tb_status_t launch_decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) 
 
 }  // namespace
 
-int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq) {
-  (void)H;
-  // About four CTAs per SM, never a split shorter than 16 keys.
-  int64_t want = (4LL * sm_count() + (int64_t)B * Hkv - 1) / ((int64_t)B * Hkv);
+int attn_decode_splits(int B, int H, int Hkv, int D, int64_t max_seq, bool kv_bf16) {
+  // About four CTAs per SM, never a split shorter than 16 keys, at most 64.
+  const int sm = sm_count();
+  const int64_t units = (int64_t)B * Hkv;
   int64_t cap = (max_seq + 15) / 16;
-  if (want > cap) want = cap;
-  if (want > 64) want = 64;
-  return (int)(want < 1 ? 1 : want);
+  if (cap > 64) cap = 64;
+  auto clampv = [&](int64_t v) { return v > cap ? cap : (v < 1 ? 1 : v); };
+  const int64_t base = clampv((4LL * sm + units - 1) / units);
+  // never above the count for Hkv = 1, which sizes the C ABI's workspace
+  const int64_t bound = clampv((4LL * sm + B - 1) / B);
+  // A grid of more than one wave of resident CTAs: the count in
+  // [base, 2 base + 2] whose last wave is fullest (ties: fewer splits).
+  const int occ = Hkv > 0 && H % Hkv == 0 ? decode_occupancy(D, H / Hkv, kv_bf16) : 0;
+  const double slots = (double)sm * occ;
+  if (occ <= 0 || (double)(units * base) < slots) return (int)base;
+  int64_t best = base;
+  double best_eff = 0.0;
+  for (int64_t ns = base; ns <= 2 * base + 2 && ns <= bound; ns++) {
+    const double x = (double)(units * ns) / slots;
+    const double eff = x / ceil(x);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = ns;
+    }
+  }
+  return (int)best;
 }
 
 size_t attn_decode_workspace(int B, int H, int D, int nsplit) {
@@ -565,7 +622,7 @@ tb_status_t attn_prefill(float* out, const float* q, const void* kcache, const v
 // ---------------------------------------------------------------------------
 extern "C" size_t tb_attention_workspace_size(int64_t B, int64_t H, int64_t Sq, int64_t D, int64_t max_seq) {
   if (B <= 0 || H <= 0 || D <= 0 || Sq != 1) return 0;
-  const int ns = tb::attn_decode_splits((int)B, (int)H, 1, max_seq);
+  const int ns = tb::attn_decode_splits((int)B, (int)H, 1, (int)D, max_seq, false);
   // sized for the largest split count any Hkv can pick (Hkv = 1 maximises it)
   return tb::attn_decode_workspace((int)B, (int)H, (int)D, ns);
 }
@@ -596,7 +653,7 @@ extern "C" tb_status_t tb_attention_f32(float* out, const float* q, const float*
     a.D = (int)D;
     a.max_seq = (int)max_seq;
     a.scale = scale;
-    a.nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, max_seq);
+    a.nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, (int)D, max_seq, false);
     TB_REQUIRE(workspace && workspace_bytes >= tb::attn_decode_workspace(a.B, a.H, a.D, a.nsplit));
     a.partial = (float*)workspace;
     return tb::attn_decode(a, st, false);
@@ -655,7 +712,7 @@ extern "C" tb_status_t tb_attention_decode_noalloc_f32(float* out, const float* 
   // fits in the scratch array; a single split that does not fit is rejected.
   const size_t per_split = (size_t)B * H * (D + 2) * sizeof(float);
   TB_REQUIRE(per_split <= TB_ATTENTION_NOALLOC_SCRATCH_BYTES);
-  int nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, max_seq);
+  int nsplit = tb::attn_decode_splits((int)B, (int)H, (int)Hkv, (int)D, max_seq, false);
   const int fit = (int)(TB_ATTENTION_NOALLOC_SCRATCH_BYTES / per_split);
   if (nsplit > fit) nsplit = fit;
   void* scratch = nullptr;

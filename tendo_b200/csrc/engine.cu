@@ -61,7 +61,7 @@ struct tb_model {
   float* samp_u = nullptr;    // the sampler's uniform draws [B]
   int32_t* samp_bad = nullptr;  // rows the sampler could not serve
   bool gv = false;            // decode projections of 2..64 sequences on the tcgen05 GEMV (one weight pass)
-  int lm_rows = 8;            // rows of x the fused lm_head GEMV stages in shared memory (0: none fit)
+  int lm_rows = 8;            // rows of x the fused lm_head GEMV stages in shared memory (0: the GEMM path)
   void* gv_zero = nullptr;    // its split-tile counters and sums (kept zero between launches)
   void* gv_scratch = nullptr; // its digit rows
   int8_t* tcdig = nullptr;    // digit rows of the prefill projections' activations (tcgen05 GEMM)
@@ -344,8 +344,9 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
       if (kind == 3) {
         TB_TRY(tb::gemv_tc(m->g, m->h, wg, sg, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
                            m->mlp_norm + l * m->d, m->c.eps));
+        // the same normed x: the gate call's digit rows serve the up projection
         TB_TRY(tb::gemv_tc(m->u, m->h, wu, su, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
-                           m->mlp_norm + l * m->d, m->c.eps));
+                           m->mlp_norm + l * m->d, m->c.eps, 0, true));
         return tb::silu_mul(m->g, m->g, m->u, m->B * m->F, st);
       }
       if (kind == 4) return tb::gemv_tc(m->h, m->g, wd, sd, resid, B, d, F, m->gv_zero, false, m->gv_scratch, st);
@@ -422,7 +423,8 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
   la.v0 = (int)m->v0;
   la.l2_prefetch = tb::l2_prefetch_enabled();
   if (kind == 5 && !m->lm_rows) {
-    // d too wide for the fused kernel's staged rows: norm, fp32 GEMM, keys
+    // d too wide for the fused kernel's staged rows, or too many row groups:
+    // norm, fp32 GEMM, keys
     TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->final_norm, m->B, m->d, m->c.eps, st));
     TB_TRY(tb::gemm_f32_nt(m->logits, m->xn, m->lm_head, (int)m->B, (int)m->V, (int)m->d, st));
     return tb::argmax_keys(m->keys, m->logits, m->B, m->V, m->v0, st);
@@ -591,12 +593,16 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->lm_rows = 0;
   for (int r = 8; r >= 1 && !m->lm_rows; r /= 2)
     if (tb::gemv_smem_bytes(r, (int)m->d) <= 200 * 1024) m->lm_rows = r;
+  // each row group re-reads the whole fp32 lm_head: past four groups one
+  // fp32 GEMM over all rows is faster (7B shape, 64 sequences: 0.81 ms
+  // against 1.44 ms per step; 32 sequences: 0.81 against 0.72)
+  if (m->lm_rows && m->B > 4 * m->lm_rows) m->lm_rows = 0;
   m->fused = m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 && (m->D == 64 || m->D == 128) &&
              (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 || m->H / m->Hkv == 8) &&
              (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024 && !m->kv16));
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
-  m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, m->Ms);
+  m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, (int)m->D, m->Ms, m->kv16);
   {
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
     m->mk = !(e && e[0] == '0') && tp == 1 && !m->kv16 &&

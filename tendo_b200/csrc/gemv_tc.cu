@@ -629,7 +629,7 @@ tb_status_t launch_gv(const cudaLaunchConfig_t& cfg, bool inl, int G, const CUte
 
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st, const float* norm_w,
-                    float eps, int group) {
+                    float eps, int group, bool digits_ready) {
   const GvLayout L = gv_layout(M, N, K, group);
   unsigned char* z = static_cast<unsigned char*>(zeroed);
   unsigned char* w = static_cast<unsigned char*>(scratch);
@@ -682,7 +682,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return TB_ERROR_NOT_SUPPORTED;
-    TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, norm_w, eps, st));
+    if (!digits_ready) TB_TRY(gemm_tc_digits(dig, srow, x, M, K, 3, norm_w, eps, st));
   }
 
   GvArgs a{};

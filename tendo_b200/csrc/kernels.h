@@ -141,7 +141,9 @@ inline bool gemv_use_mma() { return gemv_kind() == GemvKind::kMma; }
 bool l2_prefetch_enabled();
 
 // attention.cu
-int attn_decode_splits(int B, int H, int Hkv, int64_t max_seq);
+// Split count of the decode attention: about four CTAs per SM; for grids of
+// several waves, the count whose last wave of resident CTAs is fullest.
+int attn_decode_splits(int B, int H, int Hkv, int D, int64_t max_seq, bool kv_bf16 = false);
 size_t attn_decode_workspace(int B, int H, int D, int nsplit);
 tb_status_t attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 tb_status_t attn_prefill(float* out, const float* q, const void* kcache, const void* vcache, int B, int H,
@@ -181,9 +183,11 @@ size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K, int64_t group = 0);
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group = 0);
 // norm_w != null: the product is of RMSNorm(x) * norm_w (the digit kernel applies it).
+// digits_ready: `scratch` already holds the digit rows of this x (and norm)
+// from the previous call with the same M and K (digit-kernel path only).
 tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M, int N,
                     int K, void* zeroed, bool zero_first, void* scratch, cudaStream_t st,
-                    const float* norm_w = nullptr, float eps = 0.f, int group = 0);
+                    const float* norm_w = nullptr, float eps = 0.f, int group = 0, bool digits_ready = false);
 
 // comm.cu: in-place NCCL allreduce on `st` (fp32 sum, or uint64 max for the
 // packed greedy keys); a no-op without a communicator or with one rank.
