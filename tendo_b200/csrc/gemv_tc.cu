@@ -418,15 +418,22 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 #pragma unroll
               for (int mm = 0; mm < 8; mm++)
                 if (m0 + mm < M) acc[(size_t)(p * M + m0 + mm) * kGvRows] = 0;
+            // row scales and residuals of the chunk before its first store
+            float sr[8], rs[8];
+#pragma unroll
+            for (int mm = 0; mm < 8; mm++) {
+              const int m = m0 + mm < M ? m0 + mm : M - 1;
+              sr[mm] = INL ? srow[m] : __ldcg(srow + m);
+              rs[mm] = (a.resid && live) ? __ldcg(a.resid + (size_t)m * a.N + n) : 0.f;
+            }
 #pragma unroll
             for (int mm = 0; mm < 8; mm++) {
               const int m = m0 + mm;
               if (m < M && live) {
-                const float y = (INL ? srow[m] : __ldcg(srow + m)) *
-                                ((float)d[0][mm] + (float)d[1][mm] * (1.0f / 128.0f) +
-                                 (float)d[2][mm] * (1.0f / 16384.0f));
+                const float y = sr[mm] * ((float)d[0][mm] + (float)d[1][mm] * (1.0f / 128.0f) +
+                                          (float)d[2][mm] * (1.0f / 16384.0f));
                 float o = y * sc;
-                if (a.resid) o += __ldcg(a.resid + (size_t)m * a.N + n);
+                if (a.resid) o += rs[mm];
                 a.out[(size_t)m * a.N + n] = o;
               }
             }
