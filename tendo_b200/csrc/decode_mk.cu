@@ -193,7 +193,9 @@ __device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& t
       }
       __nanosleep(32);
     }
-    __threadfence();
+    // no fence here: the acquire load above already orders this thread's
+    // later accesses after every CTA's release, and the CTA barrier below
+    // carries that order to the other threads
   }
   named_sync(kMkConsumers);
   tr.stamp();
