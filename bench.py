@@ -225,25 +225,23 @@ PHASE_NAMES = ["qkv", "attention", "o", "gateup", "down"]
 
 
 def summarize_phases(us):
-    """Per-token microseconds of the persistent decode kernel by phase: the
-    trace alternates work and barrier-wait intervals (CTA 0's view)."""
-    if us is None or len(us) < 4:
-        return None
+    """Per-token microseconds of the persistent decode kernel by phase step
+    (CTA 0's view).  A staging interval includes the wait for the previous
+    phase's tagged results; attention includes the combine of the splits."""
     L = CFG["layers"]
-    # intervals per layer: qkv [stage, tiles, epilogue, wait], attention [work, wait],
-    # o [combine, stage, tiles, epilogue, wait], gate/up and down [stage, tiles, epilogue, wait]
-    names = ["qkv.stage", "qkv.tiles", "qkv.epi", "wait", "attention", "wait", "o.start", "o.stage", "o.tiles",
-             "o.epi", "wait", "gateup.stage", "gateup.tiles", "gateup.epi", "wait", "down.stage", "down.tiles",
-             "down.epi", "wait"]
-    out = {"embed": float(us[0]), "wait": float(us[1])}
+    if us is None or len(us) < 13 * L + 3:
+        return None
+    names = ["qkv.stage", "qkv.tiles", "qkv.epi", "attention", "o.stage", "o.tiles", "o.epi", "gateup.stage",
+             "gateup.tiles", "gateup.epi", "down.stage", "down.tiles", "down.epi"]
+    out = {}
     for l in range(L):
         for k, name in enumerate(names):
-            out[name] = out.get(name, 0.0) + float(us[2 + 19 * l + k])
-    i = 2 + 19 * L
+            out[name] = out.get(name, 0.0) + float(us[13 * l + k])
+    i = 13 * L
     out["lm_head.norm"] = float(us[i])
     out["lm_head.tiles"] = float(us[i + 1])
-    out["wait"] += float(us[i + 2])
-    out["total"] = float(sum(us))
+    out["final.wait"] = float(us[i + 2])
+    out["total"] = float(sum(us[: i + 3]))
     return {k: round(v, 1) for k, v in out.items()}
 
 

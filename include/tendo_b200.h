@@ -362,11 +362,19 @@ TB_API tb_status_t tb_model_bench_kernel(tb_model* m, int kind, int layer);
  * timed with CUDA events on the engine stream; *us_per_launch = average. */
 TB_API tb_status_t tb_model_time_kernel(tb_model* m, int kind, int reps, float* us_per_launch);
 /* Phase timeline of the last persistent decode step (batch-1 engines): us[i]
- * = time between consecutive stamps taken by CTA 0 at the start and at every
- * grid barrier's arrival and departure (alternating work / barrier wait:
- * embed, then per layer qkv, attention, o, gate/up, down, then lm_head).
+ * = time between consecutive stamps taken by CTA 0: per layer 13 intervals
+ * (qkv staging, tiles, epilogue; attention; then staging, tiles and epilogue
+ * of o, gate/up and down; a staging interval includes the wait for the
+ * previous phase's results), then the lm_head's norm, its tiles up to the
+ * step's final barrier, and that barrier.
  * TB_ERROR_NOT_SUPPORTED when the engine decodes with separate kernels. */
 TB_API tb_status_t tb_model_phase_times(tb_model* m, double* us, int max_entries, int* n_out);
+/* Weight-stream trace of the last persistent decode step (batch-1 engines):
+ * for the first 4096 stream units of CTA 0 (a unit = 8 weight rows x one
+ * chunk of at most 4 KB), ns[2 u] = globaltimer when the producer issued its
+ * copies and ns[2 u + 1] = when the consumers found it landed.
+ * TB_ERROR_NOT_SUPPORTED when the engine decodes with separate kernels. */
+TB_API tb_status_t tb_model_unit_times(tb_model* m, uint64_t* ns, int max_entries, int* n_out);
 /* Kernel launches one decode step issues. */
 TB_API int64_t tb_model_launches_per_step(const tb_model* m);
 

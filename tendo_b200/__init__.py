@@ -98,6 +98,7 @@ SIGNATURES = [
     ("tb_model_stream", _vp, [_vp]),
     ("tb_model_launches_per_step", _i64, [_vp]),
     ("tb_model_phase_times", _st, [_vp, _vp, ctypes.c_int, _vp]),
+    ("tb_model_unit_times", _st, [_vp, _vp, ctypes.c_int, _vp]),
 ]
 
 
@@ -611,6 +612,19 @@ class QuantizedModel:
             return None
         check(st)
         return buf[: n.value].copy()
+
+    def unit_times(self):
+        """Weight-stream units of CTA 0 in the last persistent decode step:
+        array [units, 2] of (issued, landed) globaltimer nanoseconds."""
+        import numpy as np
+
+        buf = np.zeros(2 * 4096, np.uint64)
+        n = ctypes.c_int()
+        st = lib.tb_model_unit_times(self.h, buf.ctypes.data, buf.size, ctypes.byref(n))
+        if st == TB_ERROR_NOT_SUPPORTED:
+            return None
+        check(st)
+        return buf[: n.value].reshape(-1, 2).copy()
 
     @property
     def launches_per_step(self) -> int:

@@ -1,25 +1,31 @@
 // decode_mk.cu — the whole batch-1 decode step as one persistent kernel.
 //
 // One CTA per SM (cooperative launch: all co-resident), 8 consumer warps and
-// one producer warp.  The producer walks the step's weight tiles in order —
-// per layer the Q/K/V, O, gate/up and down projections, then the fp32
-// lm_head — and streams them through a ring of kMkStages shared-memory
-// stages with cp.async.bulk (mbarrier completion).  Weights never depend on
-// activations, so the stream never waits for a phase to finish: while the
-// consumers run attention or sit in a grid barrier, the next projection's
-// tiles are already landing.  The consumers run the phases in order,
-// separated by a grid barrier:
-//   embed | per layer: RMSNorm + QKV + RoPE + KV append | split-K attention |
-//   combine + O + residual | RMSNorm + gate/up + SwiGLU | down + residual |
-//   final RMSNorm + lm_head + argmax | token, position, history update.
-// Int8 projections use the integer tensor cores: the raw weight bytes are
-// the B operand, the activation row is three int8 digit rows
-// (x / s = d0 + d1 / 128 + d2 / 128^2), accumulation is exact in s32.  A
-// projection phase keeps every tile's per-warp partial sums in shared memory
-// and runs all of its epilogues after one barrier at the end, so the tile
-// loop itself never synchronises the warps.
-// Every wait (mbarrier or grid barrier) is bounded and counts a timeout in
-// an error word instead of hanging.
+// one producer warp.  The producer walks the step's input stream in the order
+// the consumers use it — per layer the Q/K/V weight tiles, this CTA's slice
+// of the KV cache, the O, gate/up and down weight tiles, then the fp32
+// lm_head — and moves it through a ring of kMkStages shared-memory stages
+// with cp.async.bulk (mbarrier completion).  None of it depends on this
+// step's activations (the cache rows it streams were written by earlier
+// steps), so the stream never waits for a phase to finish.
+//
+// Phases hand their results to the next phase through tagged exchange words:
+// a 64-bit store of (fp32 value, epoch tag of the writing phase).  A reader
+// polls the words it needs until every tag matches, so one L2 round trip both
+// synchronises and moves the data — there is no grid barrier between phases,
+// only one at the end of the step for the greedy token.  Per layer:
+//   RMSNorm + QKV + RoPE (q, new k/v tagged; k/v also appended to the cache) |
+//   split-K attention over the streamed cache rows, split 0 of each kv head
+//   combining the others' tagged partials | O + residual | RMSNorm + gate/up
+//   + SwiGLU | down + residual;
+// then final RMSNorm + lm_head + greedy argmax | token, position, history.
+// Each CTA keeps the residual rows its O and down tiles own in shared memory,
+// and fetches each phase's channel scales with cp.async during the tile loop.
+// Int8 projections use the integer tensor cores: the raw weight bytes are the
+// B operand, the activation row is three int8 digit rows
+// (x / s = d0 + d1 / 128 + d2 / 128^2), accumulation is exact in s32.
+// Every wait (mbarrier, tagged word, barrier) is bounded and counts a timeout
+// in an error word instead of hanging.
 #include <math.h>
 
 #include "common.cuh"
@@ -35,120 +41,216 @@ constexpr int kMkThreads = kMkConsumers + 32;  // + producer warp
 constexpr int kMkStages = 5;
 constexpr int kMkChunkMax = 4096;
 constexpr int kMkStageBytes = 8 * (kMkChunkMax + 64);
-constexpr int kMkXRegs = 12;  // float4 of x per consumer thread: K <= 12288
+constexpr int kMkKvBytes = 16384;  // K (or V) bytes of one cache unit: 32 rows of D 128, 64 of D 64
+constexpr int kMkXRegs = 12;       // float4 of x per consumer thread: K <= 12288
 constexpr int kMkPart = kMkWarps * 24;  // ints of partial sums per tile
 constexpr int kMkMaxSplit = 8;          // attention splits per kv head
+constexpr int kMkTagKinds = 8;          // tags per layer
+constexpr uint32_t kMkSpin = 1u << 18;  // polls of a tagged word before it counts as a timeout
+
+// tag kinds of a layer's exchange words
+constexpr int kTagQkv = 0, kTagPart = 1, kTagAttn = 2, kTagH1 = 3, kTagAct = 4, kTagH2 = 5;
+
+__device__ __forceinline__ uint32_t tag_of(uint32_t e, int L, int l, int k) {
+  return e * (uint32_t)(kMkTagKinds * (L + 1)) + (uint32_t)(kMkTagKinds * l + k);
+}
+
+// Offsets (in words) of the exchange buffers inside MkArgs::ll.
+struct LLOff {
+  size_t q, kv, part, attn, h, act, total;
+  __host__ __device__ void init(int d, int H, int Hkv, int D, int F, int nsplit) {
+    q = 0;
+    kv = q + (size_t)H * D;
+    part = kv + (size_t)2 * Hkv * D;
+    attn = part + (size_t)H * nsplit * (D + 2);
+    h = attn + (size_t)H * D;
+    act = h + (size_t)d;
+    total = act + (size_t)F;
+  }
+};
+
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Two consecutive words (16-byte aligned); each 8-byte word is read atomically.
+__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+// A poll loop gives up after kMkSpin polls, or at once when another wait of
+// the launch has already timed out: a broken exchange ends the step within a
+// fraction of a second instead of a wait per word.  The caller counts it.
+__device__ __forceinline__ bool spin_expired(uint32_t it, const int* err) {
+  if (it >= kMkSpin) return true;
+  return (it & 255u) == 255u && *reinterpret_cast<const volatile int*>(err) != 0;
+}
+__device__ __forceinline__ uint32_t ll_tag(unsigned long long w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 struct MkLayout {
-  size_t stage_off, dig_off, xbuf_off, red_off, bar_off, total;
+  size_t stage_off, dig_off, xbuf_off, ssc_off, res_off, rope_off, red_off, bar_off, total;
   int RSX;
-  // xbuf (fp32 activations, O input and lm_head input) and the per-tile
-  // partial sums share a region: the O phase is done with xbuf once its
-  // digits are staged, and the lm_head phase keeps no partials.
-  __host__ __device__ void init(int kmax_bytes, int xbuf_floats, size_t merge_bytes, int tiles_max) {
+  // xbuf (the lm_head's fp32 input) and the per-tile partial sums share a
+  // region: the lm_head phase keeps no partials.  The digit rows and the
+  // attention's warp merge share another.
+  __host__ __device__ void init(int kmax_bytes, int xbuf_floats, size_t merge_bytes, int tiles_max, int tiles_res,
+                                int D) {
     RSX = bank_stride(kmax_bytes);
     stage_off = 0;
     dig_off = (size_t)kMkStages * kMkStageBytes;
     size_t dig_bytes = (size_t)3 * RSX;
-    if (dig_bytes < merge_bytes) dig_bytes = merge_bytes;  // the attention merge reuses this region
+    if (dig_bytes < merge_bytes) dig_bytes = merge_bytes;
     xbuf_off = (dig_off + dig_bytes + 127) & ~(size_t)127;
     size_t xb = (size_t)xbuf_floats * sizeof(float);
     const size_t pb = (size_t)tiles_max * kMkPart * sizeof(int);
     if (xb < pb) xb = pb;
-    red_off = (xbuf_off + xb + 15) & ~(size_t)15;
+    ssc_off = (xbuf_off + xb + 15) & ~(size_t)15;
+    res_off = ssc_off + (size_t)tiles_max * 8 * sizeof(float);
+    rope_off = (res_off + (size_t)tiles_res * 8 * sizeof(float) + 15) & ~(size_t)15;
+    red_off = (rope_off + (size_t)D * sizeof(float) + 15) & ~(size_t)15;
     bar_off = (red_off + 64 * sizeof(float) + 15) & ~(size_t)15;
     total = bar_off + (size_t)2 * kMkStages * sizeof(uint64_t);
   }
 };
 
-// Weight stream of one phase: p = 4 l + {0 qkv, 1 o, 2 gate/up, 3 down}; p = 4 L: lm_head.
+// This CTA's attention split: kv head kvh, cache rows [j0, j1) of the rows
+// before the step's position, in nunits units of kMkKvBytes / (4 D) rows.
+struct AttnSplit {
+  int kvh, split, nunits;
+  int64_t j0, j1;
+};
+
+__device__ __forceinline__ AttnSplit attn_split_of(const MkArgs& a, int64_t pos) {
+  AttnSplit s{};
+  s.kvh = -1;
+  const int b = blockIdx.x;
+  if (b >= a.Hkv * a.nsplit) return s;
+  s.kvh = b / a.nsplit;
+  s.split = b % a.nsplit;
+  const int pu = kMkKvBytes / (a.D * 4);
+  int64_t chunk = (pos + a.nsplit - 1) / a.nsplit;
+  chunk = (chunk + pu - 1) / pu * pu;
+  s.j0 = (int64_t)s.split * chunk;
+  s.j1 = s.j0 + chunk < pos ? s.j0 + chunk : pos;
+  s.nunits = s.j1 > s.j0 ? (int)((s.j1 - s.j0 + pu - 1) / pu) : 0;
+  return s;
+}
+
+// Input stream of one phase: p = 5 l + {0 qkv, 1 cache slice, 2 o, 3 gate/up, 4 down}; p = 5 L: lm_head.
 struct Stream {
   const int8_t* base;
   const int8_t* base2;
-  int row_bytes, ntiles, kind, D, rows;
+  int row_bytes, ntiles, kind, D, rows, layer;
 };
+constexpr int kKindPlain = 0, kKindQkv = 1, kKindGateUp = 2, kKindLmHead = 3, kKindKv = 4;
 
-__device__ __forceinline__ Stream stream_of(const MkArgs& a, int p) {
+__device__ __forceinline__ Stream stream_of(const MkArgs& a, int p, const AttnSplit& at) {
   Stream s{};
   const int HD = a.H * a.D, NQKV = (a.H + 2 * a.Hkv) * a.D;
-  if (p == 4 * a.L) {
+  if (p == 5 * a.L) {
     s.base = reinterpret_cast<const int8_t*>(a.lm_head);
     s.row_bytes = a.d * 4;
     s.ntiles = (a.V + 7) / 8;
-    s.kind = 3;
+    s.kind = kKindLmHead;
     s.rows = a.V;
     return s;
   }
-  const int l = p >> 2, k = p & 3;
+  const int l = p / 5, k = p - 5 * l;
+  s.layer = l;
   if (k == 0) {
     s.base = a.wqkv + (size_t)l * NQKV * a.d;
     s.row_bytes = a.d;
     s.ntiles = (a.H + 2 * a.Hkv) * (a.D / 8);
-    s.kind = 1;
+    s.kind = kKindQkv;
     s.D = a.D;
   } else if (k == 1) {
+    s.ntiles = at.nunits;
+    s.kind = kKindKv;
+    s.D = a.D;
+  } else if (k == 2) {
     s.base = a.wo + (size_t)l * a.d * HD;
     s.row_bytes = HD;
     s.ntiles = a.d / 8;
-    s.kind = 0;
-  } else if (k == 2) {
+    s.kind = kKindPlain;
+  } else if (k == 3) {
     s.base = a.wg + (size_t)l * a.F * a.d;
     s.base2 = a.wu + (size_t)l * a.F * a.d;
     s.row_bytes = a.d;
     s.ntiles = a.F / 4;
-    s.kind = 2;
+    s.kind = kKindGateUp;
   } else {
     s.base = a.wd + (size_t)l * a.d * a.F;
     s.row_bytes = a.F;
     s.ntiles = a.d / 8;
-    s.kind = 0;
+    s.kind = kKindPlain;
   }
   return s;
 }
 
-// Row of column n (0..7) of a tile: plain rows 8 t + n; QKV rotate-half pairs
-// (columns n and n + 4 are rows i and i + D/2 of one head); gate rows 4 t +
-// n and the same up rows; lm_head rows 8 t + n (clamped).
+// Row of column n (0..7) of a weight tile: plain rows 8 t + n; QKV rotate-half
+// pairs (columns n and n + 4 are rows i and i + D/2 of one head); gate rows
+// 4 t + n and the same up rows; lm_head rows 8 t + n (clamped).
 __device__ __forceinline__ const int8_t* row_of(const Stream& s, int tile, int n) {
-  if (s.kind == 1) {
+  if (s.kind == kKindQkv) {
     const int per = s.D / 8, head = tile / per, i0 = (tile % per) * 4;
     const int r = head * s.D + i0 + (n & 3) + (n >> 2) * (s.D / 2);
     return s.base + (size_t)r * s.row_bytes;
   }
-  if (s.kind == 2) return ((n >> 2) ? s.base2 : s.base) + (size_t)(tile * 4 + (n & 3)) * s.row_bytes;
+  if (s.kind == kKindGateUp) return ((n >> 2) ? s.base2 : s.base) + (size_t)(tile * 4 + (n & 3)) * s.row_bytes;
   int r = tile * 8 + n;
-  if (s.kind == 3 && r >= s.rows) r = s.rows - 1;
+  if (s.kind == kKindLmHead && r >= s.rows) r = s.rows - 1;
   return s.base + (size_t)r * s.row_bytes;
 }
 
-// Walks this CTA's weight-stream units (phase p, tile, chunk) in consumption order.
+// Walks this CTA's stream units (phase p, tile, chunk) in consumption order.
+// Weight phases visit tiles blockIdx.x, + gridDim.x, ...; the cache slice
+// visits its units 0, 1, ...
 struct UnitCursor {
   Stream s;
   int p, tile, ch, Kc, nch;
   bool done;
-  __device__ __forceinline__ void load(const MkArgs& a) {
-    for (; p <= 4 * a.L; p++) {
-      s = stream_of(a, p);
-      Kc = chunk_bytes(s.row_bytes);
-      nch = s.row_bytes / Kc;
-      tile = blockIdx.x;
+  __device__ __forceinline__ void load(const MkArgs& a, const AttnSplit& at) {
+    for (; p <= 5 * a.L; p++) {
+      s = stream_of(a, p, at);
+      if (s.kind == kKindKv) {
+        Kc = 0;
+        nch = 1;
+        tile = 0;
+      } else {
+        Kc = chunk_bytes(s.row_bytes);
+        nch = s.row_bytes / Kc;
+        tile = blockIdx.x;
+      }
       ch = 0;
       if (tile < s.ntiles) return;
     }
     done = true;
   }
-  __device__ __forceinline__ void start(const MkArgs& a) {
+  __device__ __forceinline__ void start(const MkArgs& a, const AttnSplit& at) {
     p = 0;
     done = false;
-    load(a);
+    load(a, at);
   }
-  __device__ __forceinline__ void advance(const MkArgs& a) {
+  __device__ __forceinline__ void advance(const MkArgs& a, const AttnSplit& at) {
     if (++ch < nch) return;
     ch = 0;
-    tile += gridDim.x;
+    tile += s.kind == kKindKv ? 1 : (int)gridDim.x;
     if (tile < s.ntiles) return;
     p++;
-    load(a);
+    load(a, at);
   }
 };
 
@@ -158,6 +260,7 @@ struct Pipe {
   uint64_t* empty;
   int* err;
   int u;  // next unit
+  uint64_t* utrace;
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -166,7 +269,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Optional phase trace (CTA 0): arrival and departure time of every barrier.
+// Unit trace (CTA 0): when the consumers find unit u landed.
+__device__ __forceinline__ void unit_landed(const Pipe& pp) {
+  if (pp.utrace && blockIdx.x == 0 && threadIdx.x == 0 && pp.u < kMkUnitTrace) pp.utrace[2 * pp.u + 1] = global_ns();
+}
+
+// Optional phase trace (CTA 0): a stamp at the end of every phase step.
 struct Trace {
   uint64_t* buf;
   int n;
@@ -176,56 +284,106 @@ struct Trace {
   }
 };
 
-__device__ __forceinline__ void grid_sync(unsigned int* counter, unsigned int& target, int* err, Trace& tr) {
+// The step's one grid barrier (before the greedy token is read).
+__device__ __forceinline__ void grid_sync(unsigned int* counter, int* err, Trace& tr) {
   named_sync(kMkConsumers);
   tr.stamp();
-  target += gridDim.x;
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(counter, 1u);
     for (uint32_t it = 0;; it++) {
       unsigned int v;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
-      if (v >= target) break;
+      if (v >= gridDim.x) break;
       if (it > (1u << 22)) {
         atomicAdd(err, 1);
         break;
       }
       __nanosleep(32);
     }
-    // no fence here: the acquire load above already orders this thread's
-    // later accesses after every CTA's release, and the CTA barrier below
-    // carries that order to the other threads
   }
   named_sync(kMkConsumers);
   tr.stamp();
 }
 
-// x (global, optionally RMSNorm(x) * w, or shared) -> three int8 digit rows,
+// x -> registers: element 4 v + j of thread v = threadIdx.x + i * 256.
+// From tagged words (polled until every tag is `tag`) or from plain memory.
+template <int NV>
+__device__ __forceinline__ void gather_x(float4 (&xv)[NV], const float* plain, const unsigned long long* ll,
+                                         uint32_t tag, int K, int* err) {
+  const int nv = K >> 2;
+  if (ll) {
+    ulonglong2 ra[NV], rb[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int v = threadIdx.x + i * kMkConsumers;
+      ra[i] = rb[i] = make_ulonglong2(0ull, 0ull);
+      if (v < nv) {
+        ra[i] = ll_load2(ll + 4 * v);
+        rb[i] = ll_load2(ll + 4 * v + 2);
+      }
+    }
+    for (uint32_t it = 0;; it++) {
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        const int v = threadIdx.x + i * kMkConsumers;
+        if (v >= nv) continue;
+        if (ll_tag(ra[i].x) != tag || ll_tag(ra[i].y) != tag) {
+          ok = false;
+          ra[i] = ll_load2(ll + 4 * v);
+        }
+        if (ll_tag(rb[i].x) != tag || ll_tag(rb[i].y) != tag) {
+          ok = false;
+          rb[i] = ll_load2(ll + 4 * v + 2);
+        }
+      }
+      if (ok) break;
+      if (spin_expired(it, err)) {
+        atomicAdd(err, 1);
+        break;
+      }
+      __nanosleep(100);
+    }
+#pragma unroll
+    for (int i = 0; i < NV; i++)
+      xv[i] = make_float4(ll_val(ra[i].x), ll_val(ra[i].y), ll_val(rb[i].x), ll_val(rb[i].y));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int v = threadIdx.x + i * kMkConsumers;
+      xv[i] = v < nv ? __ldg(reinterpret_cast<const float4*>(plain) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+// x (optionally RMSNorm(x) * w) -> three int8 digit rows in shared memory,
 // one pass: each thread keeps its NV float4s in registers between the
-// reduction and the digit step (NV * 4 * 256 >= K).  Returns the row scale s
+// reduction and the digit step.  Returns the row scale s
 // (x = s * (d0 + d1 / 128 + d2 / 128^2)).
 template <int NV>
-__device__ float stage_digits_n(int8_t* dig, int RSX, const float* src, bool src_smem, int K, const float* norm_w,
-                                float eps, float* red) {
+__device__ float stage_digits_n(int8_t* dig, int RSX, const float* plain, const unsigned long long* ll, uint32_t tag,
+                                int K, const float* norm_w, float eps, float* red, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = K >> 2;
-  float4 xv[NV];
+  // the norm weights do not depend on the step: their loads go out before
+  // the poll of x, so both round trips overlap
+  float4 w4[NV];
 #pragma unroll
   for (int i = 0; i < NV; i++) {
     const int v = threadIdx.x + i * kMkConsumers;
-    xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (v < nv) xv[i] = src_smem ? reinterpret_cast<const float4*>(src)[v] : ldcg4(src + 4 * v);
+    w4[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w && v < nv) w4[i] = __ldg(reinterpret_cast<const float4*>(norm_w) + v);
   }
+  float4 xv[NV];
+  gather_x<NV>(xv, plain, ll, tag, K, err);
   float ss = 0.f, mx = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; i++) {
-    const int v = threadIdx.x + i * kMkConsumers;
     const float4 t = xv[i];
     ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
-    float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (norm_w && v < nv) w4 = reinterpret_cast<const float4*>(norm_w)[v];
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w4.x), fabsf(t.y * w4.y)), fmaxf(fabsf(t.z * w4.z), fabsf(t.w * w4.w))));
+    const float4 w = w4[i];
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w))));
   }
   ss = warp_sum(ss);
   mx = warp_max(mx);
@@ -250,11 +408,11 @@ __device__ float stage_digits_n(int8_t* dig, int RSX, const float* src, bool src
     if (v >= nv) continue;
     float4 t = xv[i];
     if (norm_w) {
-      const float4 w4 = reinterpret_cast<const float4*>(norm_w)[v];
-      t.x = __fmul_rn(__fdiv_rn(t.x, rms), w4.x);
-      t.y = __fmul_rn(__fdiv_rn(t.y, rms), w4.y);
-      t.z = __fmul_rn(__fdiv_rn(t.z, rms), w4.z);
-      t.w = __fmul_rn(__fdiv_rn(t.w, rms), w4.w);
+      const float4 w = w4[i];
+      t.x = __fmul_rn(__fdiv_rn(t.x, rms), w.x);
+      t.y = __fmul_rn(__fdiv_rn(t.y, rms), w.y);
+      t.z = __fmul_rn(__fdiv_rn(t.z, rms), w.z);
+      t.w = __fmul_rn(__fdiv_rn(t.w, rms), w.w);
     }
     const float vals[4] = {t.x, t.y, t.z, t.w};
     uint32_t p0 = 0, p1 = 0, p2 = 0;
@@ -277,10 +435,32 @@ __device__ float stage_digits_n(int8_t* dig, int RSX, const float* src, bool src
   return sc;
 }
 
-__device__ __forceinline__ float stage_digits(int8_t* dig, int RSX, const float* src, bool src_smem, int K,
-                                              const float* norm_w, float eps, float* red) {
-  if (K <= 4 * 4 * kMkConsumers) return stage_digits_n<4>(dig, RSX, src, src_smem, K, norm_w, eps, red);
-  return stage_digits_n<kMkXRegs>(dig, RSX, src, src_smem, K, norm_w, eps, red);
+__device__ __forceinline__ float stage_digits(int8_t* dig, int RSX, const float* plain, const unsigned long long* ll,
+                                              uint32_t tag, int K, const float* norm_w, float eps, float* red,
+                                              int* err) {
+  if (K <= 4 * 4 * kMkConsumers) return stage_digits_n<4>(dig, RSX, plain, ll, tag, K, norm_w, eps, red, err);
+  return stage_digits_n<kMkXRegs>(dig, RSX, plain, ll, tag, K, norm_w, eps, red, err);
+}
+
+// Channel scales of this CTA's nt tiles of a phase -> ssc[it * 8 + column]
+// (two 16-byte cp.async per tile; waited for before the epilogue).
+__device__ __forceinline__ void prefetch_scales(float* ssc, const MkArgs& a, int l, int kind, int nt) {
+  const int t = threadIdx.x;
+  if (t < 2 * nt) {
+    const int it = t >> 1, hf = t & 1;
+    const int tile = blockIdx.x + it * gridDim.x;
+    const float* src;
+    if (kind == 0) {  // qkv: rows i0..i0+3 and i0+D/2..i0+D/2+3 of a head
+      const int per = a.D / 8, head = tile / per, i0 = (tile % per) * 4;
+      src = a.sqkv + (size_t)l * (a.H + 2 * a.Hkv) * a.D + head * a.D + i0 + hf * (a.D / 2);
+    } else if (kind == 2) {  // gate rows 4 t.., up rows 4 t..
+      src = (hf ? a.su : a.sg) + (size_t)l * a.F + tile * 4;
+    } else {  // o (1) / down (3): rows 8 t .. 8 t + 7
+      src = (kind == 1 ? a.so : a.sd) + (size_t)l * a.d + tile * 8 + hf * 4;
+    }
+    cp_async16(ssc + it * 8 + hf * 4, src);
+  }
+  cp_async_commit();
 }
 
 // One int8 tile through the pipe; this warp's partial sums of digit rows 0..2
@@ -288,29 +468,45 @@ __device__ __forceinline__ float stage_digits(int8_t* dig, int RSX, const float*
 __device__ __forceinline__ void int8_tile(int* part, Pipe& pp, const int8_t* dig, int RSX, int Kc, int nch) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int RS = bank_stride(Kc), kbc = Kc / 64;
-  int d[4] = {0, 0, 0, 0};
+  // four independent accumulators: a stage's MMAs form four short dependency
+  // chains instead of one long one (integer sums, so the split is exact)
+  int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0}, d3[4] = {0, 0, 0, 0};
   for (int ch = 0; ch < nch; ch++, pp.u++) {
     const int st = pp.u % kMkStages, use = pp.u / kMkStages;
     mbarrier_wait(&pp.full[st], (uint32_t)(use & 1), pp.err);
+    unit_landed(pp);
     const unsigned char* sp = pp.stages + (size_t)st * kMkStageBytes + (size_t)g * RS + 16 * t;
     const int8_t* xr = dig + (size_t)(g < 3 ? g : 0) * RSX + ch * Kc + 16 * t;
-#pragma unroll 4
-    for (int kb = warp; kb < kbc; kb += kMkWarps) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(sp + kb * 64);
+    int kb = warp;
+    for (; kb + kMkWarps < kbc; kb += 2 * kMkWarps) {
+      const uint4 wa = *reinterpret_cast<const uint4*>(sp + kb * 64);
+      const uint4 wb = *reinterpret_cast<const uint4*>(sp + (kb + kMkWarps) * 64);
+      uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = make_uint4(0u, 0u, 0u, 0u);
+      if (g < 3) {
+        xa = *reinterpret_cast<const uint4*>(xr + kb * 64);
+        xb = *reinterpret_cast<const uint4*>(xr + (kb + kMkWarps) * 64);
+      }
+      mma_s8_16832(d0, xa.x, 0u, xa.y, 0u, wa.x, wa.y);
+      mma_s8_16832(d1, xa.z, 0u, xa.w, 0u, wa.z, wa.w);
+      mma_s8_16832(d2, xb.x, 0u, xb.y, 0u, wb.x, wb.y);
+      mma_s8_16832(d3, xb.z, 0u, xb.w, 0u, wb.z, wb.w);
+    }
+    if (kb < kbc) {
+      const uint4 wa = *reinterpret_cast<const uint4*>(sp + kb * 64);
       uint4 xa = make_uint4(0u, 0u, 0u, 0u);
       if (g < 3) xa = *reinterpret_cast<const uint4*>(xr + kb * 64);
-      mma_s8_16832(d, xa.x, 0u, xa.y, 0u, wv.x, wv.y);
-      mma_s8_16832(d, xa.z, 0u, xa.w, 0u, wv.z, wv.w);
+      mma_s8_16832(d0, xa.x, 0u, xa.y, 0u, wa.x, wa.y);
+      mma_s8_16832(d1, xa.z, 0u, xa.w, 0u, wa.z, wa.w);
     }
     mbarrier_arrive(&pp.empty[st]);
   }
   if (g < 3) {
-    part[warp * 24 + g * 8 + 2 * t] = d[0];
-    part[warp * 24 + g * 8 + 2 * t + 1] = d[1];
+    part[warp * 24 + g * 8 + 2 * t] = d0[0] + d1[0] + d2[0] + d3[0];
+    part[warp * 24 + g * 8 + 2 * t + 1] = d0[1] + d1[1] + d2[1] + d3[1];
   }
 }
 
-// After the phase barrier: y of column `lane` (< 8) of tile `it`.
+// After the phase's tile loop: y of column `lane` (< 8) of tile `it`.
 __device__ __forceinline__ float tile_value(const int* part_all, int it, float sc) {
   const int lane = threadIdx.x & 31;
   if (lane >= 8) return 0.f;
@@ -325,174 +521,254 @@ __device__ __forceinline__ float tile_value(const int* part_all, int it, float s
   return sc * ((float)s0 + (float)s1 * (1.0f / 128.0f) + (float)s2 * (1.0f / 16384.0f));
 }
 
-// L2-only load whose line is marked evict-first: the KV rows of a layer are
-// read once per token.
-__device__ __forceinline__ float4 ld_evict_first4(const float* p, uint64_t pol) {
-  float4 v;
-  asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p), "l"(pol));
-  return v;
+// Online-softmax update of one query head with R key/value rows (the
+// reference's scale after Q.K^T; masked rows carry -inf).
+template <int VEC, int R>
+__device__ __forceinline__ void softmax_rows(const float (&qv)[VEC], const float (&kr)[R][VEC], const float (&vr)[R][VEC],
+                                             const bool (&valid)[R], float scale, float& mx, float& ls,
+                                             float (&o)[VEC]) {
+  float s[R];
+#pragma unroll
+  for (int u = 0; u < R; u++) {
+    float dd = 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; e++) dd = fmaf(qv[e], kr[u][e], dd);
+    s[u] = dd;
+  }
+#pragma unroll
+  for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+    for (int u = 0; u < R; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
+  float tmax = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < R; u++) {
+    s[u] = valid[u] ? s[u] * scale : -INFINITY;
+    tmax = fmaxf(tmax, s[u]);
+  }
+  const float mn = fmaxf(mx, tmax);
+  const float corr = expf(mx - mn);
+  float psum = 0.f;
+#pragma unroll
+  for (int e = 0; e < VEC; e++) o[e] *= corr;
+#pragma unroll
+  for (int u = 0; u < R; u++) {
+    const float p = expf(s[u] - mn);
+    psum += p;
+#pragma unroll
+    for (int e = 0; e < VEC; e++) o[e] = fmaf(p, vr[u][e], o[e]);
+  }
+  ls = ls * corr + psum;
+  mx = mn;
 }
 
-template <int VEC, int G>
-__device__ void attention_unit(const MkArgs& a, int l, int unit, int64_t sk, float* merge) {
-  constexpr int D = VEC * 32, U = 8;
+// This CTA's attention split of kv head at.kvh: the cache rows [j0, j1)
+// arrive through the ring; split 0 adds the step's own row (tagged new k/v)
+// and combines the other splits' tagged partials into the heads' outputs.
+// The G query heads of the kv head each get 8 / G warps, and each of those
+// warps a fixed range of every unit's rows, so the registers one warp holds
+// do not grow with G.
+template <int VEC>
+__device__ void attention_split(const MkArgs& a, const LLOff& lo, const AttnSplit& at, Pipe& pp, float* merge,
+                                uint32_t tag_qkv, uint32_t tag_part, uint32_t tag_attn) {
+  constexpr int D = VEC * 32;
+  constexpr int PU = kMkKvBytes / (D * 4);  // cache rows per unit
+  constexpr int R = 4;                       // rows per softmax update
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = unit / a.nsplit, split = unit % a.nsplit;
-  int64_t chunk = (sk + a.nsplit - 1) / a.nsplit;
-  chunk = (chunk + U - 1) / U * U;
-  const int64_t start = (int64_t)split * chunk, end = min(start + chunk, sk);
-  const float* kb = a.kc + (((size_t)l * a.Hkv + kvh) * a.max_seq) * D;
-  const float* vb = a.vc + (((size_t)l * a.Hkv + kvh) * a.max_seq) * D;
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  float qr[G][VEC];
+  const int kvh = at.kvh, G = a.H / a.Hkv, WPH = kMkWarps / G;
+  const int gi = warp / WPH, wr = warp - gi * WPH;  // query head of the group, row range
+  const int RW = PU / WPH;                          // rows per warp per unit (a multiple of R)
+  const int hq = kvh * G + gi;
+  unsigned long long* ll = a.ll;
+  // q of this warp's query head
+  float qr[VEC];
+  {
+    unsigned long long w[VEC];
 #pragma unroll
-  for (int gi = 0; gi < G; gi++)
+    for (int e = 0; e < VEC; e++) w[e] = ll_load(ll + lo.q + (size_t)hq * D + lane * VEC + e);
+    for (uint32_t it = 0;; it++) {
+      bool ok = true;
 #pragma unroll
-    for (int e = 0; e < VEC; e++) qr[gi][e] = ldcg(a.q + (size_t)(kvh * G + gi) * D + lane * VEC + e);
-  float mx[G], lsum[G], o[G][VEC];
+      for (int e = 0; e < VEC; e++)
+        if (ll_tag(w[e]) != tag_qkv) {
+          ok = false;
+          w[e] = ll_load(ll + lo.q + (size_t)hq * D + lane * VEC + e);
+        }
+      if (ok) break;
+      if (spin_expired(it, pp.err)) {
+        atomicAdd(pp.err, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
 #pragma unroll
-  for (int gi = 0; gi < G; gi++) {
-    mx[gi] = -INFINITY;
-    lsum[gi] = 0.f;
-#pragma unroll
-    for (int e = 0; e < VEC; e++) o[gi][e] = 0.f;
+    for (int e = 0; e < VEC; e++) qr[e] = ll_val(w[e]);
   }
-  for (int64_t j0 = start + (int64_t)warp * U; j0 < end; j0 += (int64_t)kMkWarps * U) {
-    float kr[U][VEC], vr[U][VEC];
+  float mx = -INFINITY, lsum = 0.f, o[VEC];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const int64_t j = j0 + u;
+  for (int e = 0; e < VEC; e++) o[e] = 0.f;
+  for (int u = 0; u < at.nunits; u++, pp.u++) {
+    const int st = pp.u % kMkStages, use = pp.u / kMkStages;
+    mbarrier_wait(&pp.full[st], (uint32_t)(use & 1), pp.err);
+    unit_landed(pp);
+    const int64_t js = at.j0 + (int64_t)u * PU;
+    const int rows = (int)((at.j1 - js) < PU ? (at.j1 - js) : PU);
+    const float* ks = reinterpret_cast<const float*>(pp.stages + (size_t)st * kMkStageBytes);
+    const float* vs = ks + kMkKvBytes / 4;
+    for (int r0 = wr * RW; r0 < wr * RW + RW && r0 < rows; r0 += R) {
+      float kr[R][VEC], vr[R][VEC];
+      bool valid[R];
 #pragma unroll
-      for (int e = 0; e < VEC; e++) kr[u][e] = vr[u][e] = 0.f;
-      if (j < end) {
+      for (int i = 0; i < R; i++) {
+        valid[i] = r0 + i < rows;
+        const int rr = valid[i] ? r0 + i : r0;
         if constexpr (VEC == 4) {
-          const float4 k4 = ld_evict_first4(kb + j * D + lane * 4, pol), v4 = ld_evict_first4(vb + j * D + lane * 4, pol);
-          kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
-          vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
+          const float4 k4 = *reinterpret_cast<const float4*>(ks + rr * D + lane * 4);
+          const float4 v4 = *reinterpret_cast<const float4*>(vs + rr * D + lane * 4);
+          kr[i][0] = k4.x; kr[i][1] = k4.y; kr[i][2] = k4.z; kr[i][3] = k4.w;
+          vr[i][0] = v4.x; vr[i][1] = v4.y; vr[i][2] = v4.z; vr[i][3] = v4.w;
         } else {
-#pragma unroll
-          for (int e = 0; e < VEC; e++) {
-            kr[u][e] = ldcg(kb + j * D + lane * VEC + e);
-            vr[u][e] = ldcg(vb + j * D + lane * VEC + e);
-          }
+          const float2 k2 = *reinterpret_cast<const float2*>(ks + rr * D + lane * 2);
+          const float2 v2 = *reinterpret_cast<const float2*>(vs + rr * D + lane * 2);
+          kr[i][0] = k2.x; kr[i][1] = k2.y;
+          vr[i][0] = v2.x; vr[i][1] = v2.y;
         }
       }
+      softmax_rows<VEC, R>(qr, kr, vr, valid, a.attn_scale, mx, lsum, o);
     }
-#pragma unroll
-    for (int gi = 0; gi < G; gi++) {
-      float s[U];
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        float dd = 0.f;
-#pragma unroll
-        for (int e = 0; e < VEC; e++) dd = fmaf(qr[gi][e], kr[u][e], dd);
-        s[u] = dd;
-      }
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        s[u] = (j0 + u < end) ? s[u] * a.attn_scale : -INFINITY;
-        tmax = fmaxf(tmax, s[u]);
-      }
-      const float mn = fmaxf(mx[gi], tmax);
-      const float corr = expf(mx[gi] - mn);
-      float psum = 0.f;
-#pragma unroll
-      for (int e = 0; e < VEC; e++) o[gi][e] *= corr;
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const float p = expf(s[u] - mn);
-        psum += p;
-#pragma unroll
-        for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e]);
-      }
-      lsum[gi] = lsum[gi] * corr + psum;
-      mx[gi] = mn;
-    }
+    mbarrier_arrive(&pp.empty[st]);
   }
-  // merge the warps: merge[warp][gi][D + 2]
+  if (at.split == 0 && wr == 0) {
+    // the step's own key/value row, written tagged by the QKV epilogues
+    float kr[1][VEC], vr[1][VEC];
+    const bool valid[1] = {true};
+    unsigned long long wk[VEC], wv[VEC];
 #pragma unroll
-  for (int gi = 0; gi < G; gi++) {
-    float* mw = merge + ((size_t)warp * G + gi) * (D + 2);
+    for (int e = 0; e < VEC; e++) {
+      wk[e] = ll_load(ll + lo.kv + (size_t)kvh * D + lane * VEC + e);
+      wv[e] = ll_load(ll + lo.kv + (size_t)(a.Hkv + kvh) * D + lane * VEC + e);
+    }
+    for (uint32_t it = 0;; it++) {
+      bool ok = true;
 #pragma unroll
-    for (int e = 0; e < VEC; e++) mw[lane * VEC + e] = o[gi][e];
+      for (int e = 0; e < VEC; e++) {
+        if (ll_tag(wk[e]) != tag_qkv) {
+          ok = false;
+          wk[e] = ll_load(ll + lo.kv + (size_t)kvh * D + lane * VEC + e);
+        }
+        if (ll_tag(wv[e]) != tag_qkv) {
+          ok = false;
+          wv[e] = ll_load(ll + lo.kv + (size_t)(a.Hkv + kvh) * D + lane * VEC + e);
+        }
+      }
+      if (ok) break;
+      if (spin_expired(it, pp.err)) {
+        atomicAdd(pp.err, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; e++) {
+      kr[0][e] = ll_val(wk[e]);
+      vr[0][e] = ll_val(wv[e]);
+    }
+    softmax_rows<VEC, 1>(qr, kr, vr, valid, a.attn_scale, mx, lsum, o);
+  }
+  // merge the warps of each query head: merge[warp][D + 2]
+  {
+    float* mw = merge + (size_t)warp * (D + 2);
+#pragma unroll
+    for (int e = 0; e < VEC; e++) mw[lane * VEC + e] = o[e];
     if (lane == 0) {
-      mw[D] = mx[gi];
-      mw[D + 1] = lsum[gi];
+      mw[D] = mx;
+      mw[D + 1] = lsum;
     }
   }
   named_sync(kMkConsumers);
+  const int ns = a.nsplit;
   for (int idx = threadIdx.x; idx < G * D; idx += kMkConsumers) {
-    const int gi = idx / D, e = idx - gi * D;
+    const int g = idx / D, e = idx - g * D;
+    const float* mg = merge + (size_t)g * WPH * (D + 2);
     float m = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kMkWarps; w++) m = fmaxf(m, merge[((size_t)w * G + gi) * (D + 2) + D]);
+    for (int w = 0; w < WPH; w++) m = fmaxf(m, mg[(size_t)w * (D + 2) + D]);
     float L = 0.f, O = 0.f;
     if (m != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kMkWarps; w++) {
-        const float* mw = merge + ((size_t)w * G + gi) * (D + 2);
+      for (int w = 0; w < WPH; w++) {
+        const float* mw = mg + (size_t)w * (D + 2);
         const float c = expf(mw[D] - m);
         L = fmaf(mw[D + 1], c, L);
         O = fmaf(mw[e], c, O);
       }
     }
-    float* part = a.partial + ((size_t)(kvh * G + gi) * a.nsplit + split) * (D + 4);
-    part[e] = O;
-    if (e == 0) {
-      part[D] = m;
-      part[D + 1] = L;
+    const int hqo = kvh * G + g;
+    if (at.split != 0) {
+      unsigned long long* p = ll + lo.part + ((size_t)hqo * ns + at.split) * (D + 2);
+      ll_store(p + e, O, tag_part);
+      if (e == 0) {
+        ll_store(p + D, m, tag_part);
+        ll_store(p + D + 1, L, tag_part);
+      }
+      continue;
     }
-  }
-  // the last split of this kv head to finish combines all its splits
-  __threadfence();
-  named_sync(kMkConsumers);
-  int* flag = reinterpret_cast<int*>(merge);
-  if (threadIdx.x == 0) {
-    const unsigned int ticket = atomicAdd(a.head_done + kvh, 1u);
-    flag[0] = ticket == (unsigned int)(a.nsplit - 1);
-  }
-  named_sync(kMkConsumers);
-  const bool last = flag[0] != 0;
-  named_sync(kMkConsumers);
-  if (last) {
-    __threadfence();
-    for (int idx = threadIdx.x; idx < G * D; idx += kMkConsumers) {
-      const int gi = idx / D, e = idx - gi * D;
-      const float* p = a.partial + (size_t)(kvh * G + gi) * a.nsplit * (D + 4);
-      float ms[kMkMaxSplit], ls[kMkMaxSplit], os[kMkMaxSplit];
+    // split 0 combines: its own (m, L, O) and the other splits' tagged partials
+    unsigned long long pm[kMkMaxSplit], pl[kMkMaxSplit], po[kMkMaxSplit];
+    const unsigned long long* pb = ll + lo.part + (size_t)hqo * ns * (D + 2);
 #pragma unroll
-      for (int s = 0; s < kMkMaxSplit; s++) {
-        ms[s] = -INFINITY;
-        ls[s] = os[s] = 0.f;
-        if (s < a.nsplit) {
-          ms[s] = ldcg(p + (size_t)s * (D + 4) + D);
-          ls[s] = ldcg(p + (size_t)s * (D + 4) + D + 1);
-          os[s] = ldcg(p + (size_t)s * (D + 4) + e);
+    for (int s = 1; s < kMkMaxSplit; s++) {
+      pm[s] = pl[s] = po[s] = 0ull;
+      if (s < ns) {
+        pm[s] = ll_load(pb + (size_t)s * (D + 2) + D);
+        pl[s] = ll_load(pb + (size_t)s * (D + 2) + D + 1);
+        po[s] = ll_load(pb + (size_t)s * (D + 2) + e);
+      }
+    }
+    for (uint32_t it = 0;; it++) {
+      bool ok = true;
+#pragma unroll
+      for (int s = 1; s < kMkMaxSplit; s++) {
+        if (s >= ns) continue;
+        if (ll_tag(pm[s]) != tag_part) {
+          ok = false;
+          pm[s] = ll_load(pb + (size_t)s * (D + 2) + D);
+        }
+        if (ll_tag(pl[s]) != tag_part) {
+          ok = false;
+          pl[s] = ll_load(pb + (size_t)s * (D + 2) + D + 1);
+        }
+        if (ll_tag(po[s]) != tag_part) {
+          ok = false;
+          po[s] = ll_load(pb + (size_t)s * (D + 2) + e);
         }
       }
-      float m = -INFINITY;
-#pragma unroll
-      for (int s = 0; s < kMkMaxSplit; s++) m = fmaxf(m, ms[s]);
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int s = 0; s < kMkMaxSplit; s++) {
-        const float c = ms[s] == -INFINITY ? 0.f : expf(ms[s] - m);
-        L = fmaf(ls[s], c, L);
-        O = fmaf(os[s], c, O);
+      if (ok) break;
+      if (spin_expired(it, pp.err)) {
+        atomicAdd(pp.err, 1);
+        break;
       }
-      a.attn[(size_t)(kvh * G + gi) * D + e] = O / L;
+      __nanosleep(64);
     }
-    if (threadIdx.x == 0) a.head_done[kvh] = 0u;  // ready for the next step
+    float M = m;
+#pragma unroll
+    for (int s = 1; s < kMkMaxSplit; s++)
+      if (s < ns) M = fmaxf(M, ll_val(pm[s]));
+    float Lc = 0.f, Oc = 0.f;
+    if (m != -INFINITY) {
+      const float c = expf(m - M);
+      Lc = L * c;
+      Oc = O * c;
+    }
+#pragma unroll
+    for (int s = 1; s < kMkMaxSplit; s++) {
+      if (s >= ns) continue;
+      const float ms = ll_val(pm[s]);
+      if (ms == -INFINITY) continue;
+      const float c = expf(ms - M);
+      Lc = fmaf(ll_val(pl[s]), c, Lc);
+      Oc = fmaf(ll_val(po[s]), c, Oc);
+    }
+    ll_store(ll + lo.attn + (size_t)hqo * D + e, Oc / Lc, tag_attn);
   }
-  named_sync(kMkConsumers);  // merge is reused by the next unit
+  named_sync(kMkConsumers);  // merge is reused by the next phase's digits
 }
 
 __device__ __forceinline__ unsigned long long greedy_key(float v, int idx) {
@@ -503,17 +779,21 @@ __device__ __forceinline__ unsigned long long greedy_key(float v, int idx) {
 
 __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  MkLayout Ly;
-  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
-  unsigned char* stages = smem + Ly.stage_off;
-  int8_t* dig = reinterpret_cast<int8_t*>(smem + Ly.dig_off);
-  float* merge = reinterpret_cast<float*>(smem + Ly.dig_off);
-  float* xbuf = reinterpret_cast<float*>(smem + Ly.xbuf_off);
-  int* part = reinterpret_cast<int*>(smem + Ly.xbuf_off);  // shares the region with xbuf
-  float* redf = reinterpret_cast<float*>(smem + Ly.red_off);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Ly.bar_off);
+  const LLOff lo{a.ll_q, a.ll_kv, a.ll_part, a.ll_attn, a.ll_h, a.ll_act, 0};
+  unsigned char* stages = smem;
+  int8_t* dig = reinterpret_cast<int8_t*>(smem + a.sm_dig);
+  float* merge = reinterpret_cast<float*>(smem + a.sm_dig);
+  float* xbuf = reinterpret_cast<float*>(smem + a.sm_xbuf);
+  int* part = reinterpret_cast<int*>(smem + a.sm_xbuf);  // shares the region with xbuf
+  float* ssc = reinterpret_cast<float*>(smem + a.sm_ssc);
+  float* hres = reinterpret_cast<float*>(smem + a.sm_res);
+  float* srope = reinterpret_cast<float*>(smem + a.sm_rope);
+  float* redf = reinterpret_cast<float*>(smem + a.sm_red);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.sm_bar);
   uint64_t* empty = full + kMkStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pos = *a.pos;
+  const AttnSplit at = attn_split_of(a, pos);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMkStages; s++) {
       mbarrier_init(&full[s], 1);
@@ -524,177 +804,232 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
   __syncthreads();
 
   if (warp == kMkWarps) {
-    // producer: the step's weight tiles in consumption order
-    if (lane == 0) {
-      // weights are read once per token: evict them first, so the activations,
-      // norm weights, channel scales and KV rows the consumers touch stay in L2
-      uint64_t policy;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-      UnitCursor c;
-      c.start(a);
-      for (int u = 0; !c.done; u++) {
-        const int st = u % kMkStages, use = u / kMkStages;
-        if (use > 0) mbarrier_wait(&empty[st], (uint32_t)((use - 1) & 1), a.err);
-        unsigned char* dst = stages + (size_t)st * kMkStageBytes;
-        const int RS = bank_stride(c.Kc);
-        mbarrier_expect_tx(&full[st], (uint32_t)(8 * c.Kc));
-#pragma unroll
-        for (int n = 0; n < 8; n++)
-          bulk_copy_g2s_hint(dst + (size_t)n * RS, row_of(c.s, c.tile, n) + (size_t)c.ch * c.Kc, (uint32_t)c.Kc,
-                             &full[st], policy);
-        c.advance(a);
+    // producer warp: the step's stream in consumption order.  All lanes walk
+    // the units; lane 0 posts a unit's byte count and lanes 0..7 each issue
+    // one row's copy (one thread issuing all of them cannot keep up with HBM)
+    // weights and cache rows are read once per step: evict them first, so
+    // the exchange words, norm weights and scales stay in L2
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    const int pu = kMkKvBytes / (a.D * 4);
+    UnitCursor c;
+    c.start(a, at);
+    for (int u = 0; !c.done; u++) {
+      const int st = u % kMkStages, use = u / kMkStages;
+      if (use > 0) mbarrier_wait(&empty[st], (uint32_t)((use - 1) & 1), a.err);
+      unsigned char* dst = stages + (size_t)st * kMkStageBytes;
+      if (c.s.kind == kKindKv) {
+        const int64_t js = at.j0 + (int64_t)c.tile * pu;
+        const int rows = (int)((at.j1 - js) < pu ? (at.j1 - js) : pu);
+        const uint32_t bytes = (uint32_t)rows * (uint32_t)a.D * 4u;
+        if (lane == 0) mbarrier_expect_tx(&full[st], 2u * bytes);
+        __syncwarp();
+        if (lane < 2) {
+          const size_t off = (((size_t)c.s.layer * a.Hkv + at.kvh) * a.max_seq + (size_t)js) * a.D;
+          bulk_copy_g2s_hint(dst + lane * kMkKvBytes, (lane ? a.vc : a.kc) + off, bytes, &full[st], policy);
+        }
+      } else {
+        if (lane == 0) mbarrier_expect_tx(&full[st], (uint32_t)(8 * c.Kc));
+        __syncwarp();
+        if (lane < 8)
+          bulk_copy_g2s_hint(dst + (size_t)lane * bank_stride(c.Kc), row_of(c.s, c.tile, lane) + (size_t)c.ch * c.Kc,
+                             (uint32_t)c.Kc, &full[st], policy);
       }
-      // every copy lands before the consumers release its stage, so the CTA
-      // never exits with a copy in flight
+      if (lane == 0 && a.utrace && blockIdx.x == 0 && u < kMkUnitTrace) a.utrace[2 * u] = global_ns();
+      c.advance(a, at);
     }
+    // every copy lands before the consumers release its stage, so the CTA
+    // never exits with a copy in flight
     return;
   }
   // consumers
-  unsigned int target = 0;
   Trace tr{a.trace, 0};
   tr.stamp();
-  Pipe pp{stages, full, empty, a.err, 0};
-  const int64_t pos = *a.pos;
-  const int64_t sk = pos + 1;
+  Pipe pp{stages, full, empty, a.err, 0, a.utrace};
   const int64_t token = __ldcg(a.tokens);
+  const uint32_t e = *a.epoch + 1u;
   const int half = a.D / 2;
   const int HD = a.H * a.D;
-  // embedding (cpu/backend.go:1289-1339): h = embed[token]
-  for (int i = blockIdx.x * kMkConsumers + threadIdx.x; i < a.d; i += gridDim.x * kMkConsumers)
-    a.h[i] = a.embed[(size_t)token * a.d + i];
-  grid_sync(a.bar_counter, target, a.err, tr);
+  const int L = a.L;
+  unsigned long long* ll = a.ll;
+  const float* emb = a.embed + (size_t)token * a.d;
+  // residual rows this CTA's O / down tiles own, from the embedding
+  // (cpu/backend.go:1289-1339); the rotary table row of the position
+  for (int j = threadIdx.x; j < a.tiles_res * 8; j += kMkConsumers) {
+    const int tile = blockIdx.x + (j >> 3) * gridDim.x;
+    hres[j] = tile < a.d / 8 ? __ldg(emb + tile * 8 + (j & 7)) : 0.f;
+  }
+  for (int i = threadIdx.x; i < half; i += kMkConsumers) {
+    srope[i] = __ldg(a.cos_t + (size_t)pos * half + i);
+    srope[half + i] = __ldg(a.sin_t + (size_t)pos * half + i);
+  }
+  // (the first staging's CTA barriers order these before their readers)
 
-  for (int l = 0; l < a.L; l++) {
+  for (int l = 0; l < L; l++) {
     // ---- RMSNorm + Q/K/V + RoPE + KV append ----
     {
-      const Stream s = stream_of(a, 4 * l + 0);
+      const Stream s = stream_of(a, 5 * l, at);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
-      const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.attn_norm + (size_t)l * a.d, a.eps, redf);
+      const float sc = l == 0 ? stage_digits(dig, a.RSX, emb, nullptr, 0u, a.d, a.attn_norm, a.eps, redf, a.err)
+                              : stage_digits(dig, a.RSX, nullptr, ll + lo.h, tag_of(e, L, l - 1, kTagH2), a.d,
+                                             a.attn_norm + (size_t)l * a.d, a.eps, redf, a.err);
       tr.stamp();
-      int nt = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
-        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      const int nt = s.ntiles > (int)blockIdx.x ? (s.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+      prefetch_scales(ssc, a, l, 0, nt);
+      for (int it = 0; it < nt; it++) int8_tile(part + it * kMkPart, pp, dig, a.RSX, Kc, nch);
+      cp_async_wait_all();
       named_sync(kMkConsumers);
       tr.stamp();
-      const float* sqkv = a.sqkv + (size_t)l * (a.H + 2 * a.Hkv) * a.D;
+      const uint32_t tg = tag_of(e, L, l, kTagQkv);
       float* kcl = a.kc + (size_t)l * a.Hkv * a.max_seq * a.D;
       float* vcl = a.vc + (size_t)l * a.Hkv * a.max_seq * a.D;
       for (int it = warp; it < nt; it += kMkWarps) {
         const int tile = blockIdx.x + it * gridDim.x;
         const int per = a.D / 8, head = tile / per, i = (tile % per) * 4 + (lane & 3);
-        const int r = head * a.D + i + ((lane >> 2) & 1) * half;
         const float y = tile_value(part, it, sc);
-        const float v = lane < 8 ? y * sqkv[r] : 0.f;
+        const float v = lane < 8 ? y * ssc[it * 8 + lane] : 0.f;
         const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
         if (lane < 4) {
           if (head < a.H + a.Hkv) {
-            const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
+            const float c = srope[i], sn = srope[half + i];
             const float o0 = __fsub_rn(__fmul_rn(v, c), __fmul_rn(partner, sn));
             const float o1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(partner, c));
-            float* o = head < a.H ? a.q + (size_t)head * a.D : kcl + ((size_t)(head - a.H) * a.max_seq + pos) * a.D;
-            o[i] = o0;
-            o[i + half] = o1;
+            if (head < a.H) {
+              ll_store(ll + lo.q + (size_t)head * a.D + i, o0, tg);
+              ll_store(ll + lo.q + (size_t)head * a.D + i + half, o1, tg);
+            } else {
+              const int kh = head - a.H;
+              float* o = kcl + ((size_t)kh * a.max_seq + pos) * a.D;
+              o[i] = o0;
+              o[i + half] = o1;
+              ll_store(ll + lo.kv + (size_t)kh * a.D + i, o0, tg);
+              ll_store(ll + lo.kv + (size_t)kh * a.D + i + half, o1, tg);
+            }
           } else {
-            float* o = vcl + ((size_t)(head - a.H - a.Hkv) * a.max_seq + pos) * a.D;
+            const int vh = head - a.H - a.Hkv;
+            float* o = vcl + ((size_t)vh * a.max_seq + pos) * a.D;
             o[i] = v;
             o[i + half] = partner;
+            ll_store(ll + lo.kv + (size_t)(a.Hkv + vh) * a.D + i, v, tg);
+            ll_store(ll + lo.kv + (size_t)(a.Hkv + vh) * a.D + i + half, partner, tg);
           }
         }
       }
-    }
-    grid_sync(a.bar_counter, target, a.err, tr);
-    // ---- split-K attention over the cache ----
-    {
-      const int units = a.Hkv * a.nsplit;
-      const int G = a.H / a.Hkv;
-      for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
-        if (a.D == 128) {
-          if (G == 1) attention_unit<4, 1>(a, l, unit, sk, merge);
-          else if (G == 2) attention_unit<4, 2>(a, l, unit, sk, merge);
-          else if (G == 4) attention_unit<4, 4>(a, l, unit, sk, merge);
-          else attention_unit<4, 8>(a, l, unit, sk, merge);
-        } else {
-          if (G == 1) attention_unit<2, 1>(a, l, unit, sk, merge);
-          else if (G == 2) attention_unit<2, 2>(a, l, unit, sk, merge);
-          else if (G == 4) attention_unit<2, 4>(a, l, unit, sk, merge);
-          else attention_unit<2, 8>(a, l, unit, sk, merge);
-        }
-      }
-    }
-    grid_sync(a.bar_counter, target, a.err, tr);
-    // ---- O projection + residual (the attention phase left the combined heads in a.attn) ----
-    {
       tr.stamp();
-      const Stream s = stream_of(a, 4 * l + 1);
+    }
+    // ---- split-K attention over the cache (quantized.go:319-372) ----
+    if (at.kvh >= 0) {
+      const uint32_t tq = tag_of(e, L, l, kTagQkv), tp = tag_of(e, L, l, kTagPart), ta = tag_of(e, L, l, kTagAttn);
+      if (a.D == 128) attention_split<4>(a, lo, at, pp, merge, tq, tp, ta);
+      else attention_split<2>(a, lo, at, pp, merge, tq, tp, ta);
+    }
+    tr.stamp();
+    // ---- O projection + residual ----
+    {
+      const Stream s = stream_of(a, 5 * l + 2, at);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
-      const float sc = stage_digits(dig, Ly.RSX, a.attn, false, HD, nullptr, 0.f, redf);
+      const float sc = stage_digits(dig, a.RSX, nullptr, ll + lo.attn, tag_of(e, L, l, kTagAttn), HD, nullptr, 0.f,
+                                    redf, a.err);
       tr.stamp();
-      int nt = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
-        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      const int nt = s.ntiles > (int)blockIdx.x ? (s.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+      prefetch_scales(ssc, a, l, 1, nt);
+      for (int it = 0; it < nt; it++) int8_tile(part + it * kMkPart, pp, dig, a.RSX, Kc, nch);
+      cp_async_wait_all();
       named_sync(kMkConsumers);
       tr.stamp();
-      const float* so = a.so + (size_t)l * a.d;
+      const uint32_t tg = tag_of(e, L, l, kTagH1);
       for (int it = warp; it < nt; it += kMkWarps) {
         const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
         const float y = tile_value(part, it, sc);
-        if (lane < 8) a.h[r] = ldcg(a.h + r) + y * so[r];
+        if (lane < 8) {
+          const float hv = hres[it * 8 + lane] + y * ssc[it * 8 + lane];
+          hres[it * 8 + lane] = hv;
+          ll_store(ll + lo.h + r, hv, tg);
+        }
       }
+      tr.stamp();
     }
-    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- RMSNorm + gate/up + SwiGLU ----
     {
-      const Stream s = stream_of(a, 4 * l + 2);
+      const Stream s = stream_of(a, 5 * l + 3, at);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
-      const float sc = stage_digits(dig, Ly.RSX, a.h, false, a.d, a.mlp_norm + (size_t)l * a.d, a.eps, redf);
+      const float sc = stage_digits(dig, a.RSX, nullptr, ll + lo.h, tag_of(e, L, l, kTagH1), a.d,
+                                    a.mlp_norm + (size_t)l * a.d, a.eps, redf, a.err);
       tr.stamp();
-      int nt = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
-        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      const int nt = s.ntiles > (int)blockIdx.x ? (s.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+      prefetch_scales(ssc, a, l, 2, nt);
+      for (int it = 0; it < nt; it++) int8_tile(part + it * kMkPart, pp, dig, a.RSX, Kc, nch);
+      cp_async_wait_all();
       named_sync(kMkConsumers);
       tr.stamp();
-      const float* sg = a.sg + (size_t)l * a.F;
-      const float* su = a.su + (size_t)l * a.F;
+      const uint32_t tg = tag_of(e, L, l, kTagAct);
       for (int it = warp; it < nt; it += kMkWarps) {
         const int j = (blockIdx.x + it * gridDim.x) * 4 + (lane & 3);
         const float y = tile_value(part, it, sc);
-        const float v = lane < 8 ? y * ((lane >> 2) ? su[j] : sg[j]) : 0.f;
+        const float v = lane < 8 ? y * ssc[it * 8 + lane] : 0.f;
         const float partner = __shfl_xor_sync(0xffffffffu, v, 4);
         if (lane < 4) {
           const float sig = 1.0f / (1.0f + expf(-v));
-          a.act[j] = (v * sig) * partner;
+          ll_store(ll + lo.act + j, (v * sig) * partner, tg);
         }
       }
+      tr.stamp();
     }
-    grid_sync(a.bar_counter, target, a.err, tr);
     // ---- down projection + residual ----
     {
-      const Stream s = stream_of(a, 4 * l + 3);
+      const Stream s = stream_of(a, 5 * l + 4, at);
       const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc;
-      const float sc = stage_digits(dig, Ly.RSX, a.act, false, a.F, nullptr, 0.f, redf);
+      const float sc = stage_digits(dig, a.RSX, nullptr, ll + lo.act, tag_of(e, L, l, kTagAct), a.F, nullptr, 0.f,
+                                    redf, a.err);
       tr.stamp();
-      int nt = 0;
-      for (int tile = blockIdx.x; tile < s.ntiles; tile += gridDim.x, nt++)
-        int8_tile(part + nt * kMkPart, pp, dig, Ly.RSX, Kc, nch);
+      const int nt = s.ntiles > (int)blockIdx.x ? (s.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+      prefetch_scales(ssc, a, l, 3, nt);
+      for (int it = 0; it < nt; it++) int8_tile(part + it * kMkPart, pp, dig, a.RSX, Kc, nch);
+      cp_async_wait_all();
       named_sync(kMkConsumers);
       tr.stamp();
-      const float* sd = a.sd + (size_t)l * a.d;
+      const uint32_t tg = tag_of(e, L, l, kTagH2);
       for (int it = warp; it < nt; it += kMkWarps) {
         const int r = (blockIdx.x + it * gridDim.x) * 8 + lane;
         const float y = tile_value(part, it, sc);
-        if (lane < 8) a.h[r] = ldcg(a.h + r) + y * sd[r];
+        if (lane < 8) {
+          const float hv = hres[it * 8 + lane] + y * ssc[it * 8 + lane];
+          hres[it * 8 + lane] = hv;
+          ll_store(ll + lo.h + r, hv, tg);
+          if (l == L - 1) a.h[r] = hv;
+        }
       }
+      tr.stamp();
     }
-    grid_sync(a.bar_counter, target, a.err, tr);
   }
 
   // ---- final RMSNorm + fp32 lm_head + greedy argmax ----
   {
     // xbuf = RMSNorm(h) * final_norm in fp32 (quantized.go:154-172)
     float ss = 0.f;
-    for (int v = threadIdx.x; v < a.d / 4; v += kMkConsumers) {
-      const float4 t = ldcg4(a.h + 4 * v);
-      ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    const uint32_t th = tag_of(e, L, L - 1, kTagH2);
+    if (a.d <= 4 * 4 * kMkConsumers) {
+      float4 xv[4];
+      gather_x<4>(xv, nullptr, ll + lo.h, th, a.d, a.err);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int v = threadIdx.x + i * kMkConsumers;
+        if (v < a.d / 4) {
+          reinterpret_cast<float4*>(xbuf)[v] = xv[i];
+          ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+        }
+      }
+    } else {
+      float4 xv[kMkXRegs];
+      gather_x<kMkXRegs>(xv, nullptr, ll + lo.h, th, a.d, a.err);
+#pragma unroll
+      for (int i = 0; i < kMkXRegs; i++) {
+        const int v = threadIdx.x + i * kMkConsumers;
+        if (v < a.d / 4) {
+          reinterpret_cast<float4*>(xbuf)[v] = xv[i];
+          ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+        }
+      }
     }
     ss = warp_sum(ss);
     if (lane == 0) redf[warp] = ss;
@@ -703,11 +1038,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
 #pragma unroll
     for (int w = 0; w < kMkWarps; w++) tot += redf[w];
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.d), a.eps));
-    for (int i = threadIdx.x; i < a.d; i += kMkConsumers)
-      xbuf[i] = __fmul_rn(__fdiv_rn(ldcg(a.h + i), rms), a.final_norm[i]);
+    for (int i = threadIdx.x; i < a.d; i += kMkConsumers) xbuf[i] = __fmul_rn(__fdiv_rn(xbuf[i], rms), a.final_norm[i]);
     named_sync(kMkConsumers);
     tr.stamp();
-    const Stream s = stream_of(a, 4 * a.L);
+    const Stream s = stream_of(a, 5 * L, at);
     const int Kc = chunk_bytes(s.row_bytes), nch = s.row_bytes / Kc, RS = bank_stride(Kc);
     const int fpc = Kc / 4;  // floats per chunk
     unsigned long long best = 0ull;
@@ -716,6 +1050,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
       for (int ch = 0; ch < nch; ch++, pp.u++) {
         const int st = pp.u % kMkStages, use = pp.u / kMkStages;
         mbarrier_wait(&full[st], (uint32_t)(use & 1), a.err);
+        unit_landed(pp);
         const float* wr = reinterpret_cast<const float*>(stages + (size_t)st * kMkStageBytes + (size_t)warp * RS);
         const float* xr = xbuf + ch * fpc;
         for (int v = lane; v < fpc / 4; v += 32) {
@@ -738,7 +1073,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     }
     if (lane == 0 && best) atomicMax(a.keys, best);
   }
-  grid_sync(a.bar_counter, target, a.err, tr);
+  grid_sync(a.bar_counter, a.err, tr);
   // ---- token, history and position (models/sampling.go:73-83) ----
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     const unsigned long long k = atomicAdd(a.keys, 0ull);
@@ -749,6 +1084,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(MkArgs a) {
     *a.step = st + 1;
     *a.pos = pos + 1;
     *a.keys = 0ull;
+    *a.epoch = e;
   }
 }
 
@@ -763,14 +1099,44 @@ void fill_sizes(MkArgs& a, int grid) {
   int kmax = a.d > a.H * a.D ? a.d : a.H * a.D;
   if (a.F > kmax) kmax = a.F;
   a.kmax_bytes = kmax;
-  a.xbuf_floats = a.H * a.D > a.d ? a.H * a.D : a.d;
-  a.merge_bytes = (size_t)kMkWarps * (a.H / a.Hkv) * (a.D + 2) * sizeof(float);
+  a.xbuf_floats = a.d;
+  a.merge_bytes = (size_t)kMkWarps * (a.D + 2) * sizeof(float);
   a.tiles_max = max_tiles_per_cta(a, grid);
+  a.tiles_res = (a.d / 8 + grid - 1) / grid;
+  MkLayout Ly;
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max, a.tiles_res, a.D);
+  a.RSX = Ly.RSX;
+  a.sm_dig = (uint32_t)Ly.dig_off;
+  a.sm_xbuf = (uint32_t)Ly.xbuf_off;
+  a.sm_ssc = (uint32_t)Ly.ssc_off;
+  a.sm_res = (uint32_t)Ly.res_off;
+  a.sm_rope = (uint32_t)Ly.rope_off;
+  a.sm_red = (uint32_t)Ly.red_off;
+  a.sm_bar = (uint32_t)Ly.bar_off;
+  LLOff lo;
+  lo.init(a.d, a.H, a.Hkv, a.D, a.F, a.nsplit);
+  a.ll_q = (uint32_t)lo.q;
+  a.ll_kv = (uint32_t)lo.kv;
+  a.ll_part = (uint32_t)lo.part;
+  a.ll_attn = (uint32_t)lo.attn;
+  a.ll_h = (uint32_t)lo.h;
+  a.ll_act = (uint32_t)lo.act;
 }
 
 }  // namespace
 
-size_t megakernel_partial_bytes(int H, int D, int nsplit) { return (size_t)H * nsplit * (D + 4) * sizeof(float); }
+int megakernel_splits(int Hkv) {
+  int ns = Hkv > 0 ? sm_count() / Hkv : 1;  // one split per CTA
+  if (ns < 1) ns = 1;
+  if (ns > kMkMaxSplit) ns = kMkMaxSplit;
+  return ns;
+}
+
+size_t megakernel_ll_words(int d, int H, int Hkv, int D, int F, int nsplit) {
+  LLOff lo;
+  lo.init(d, H, Hkv, D, F, nsplit);
+  return lo.total;
+}
 
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch) {
   if (batch != 1) return false;
@@ -778,6 +1144,7 @@ bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch)
   if (d % 8 || F % 4 || D % 8 || (D != 64 && D != 128)) return false;
   const int G = H / Hkv;
   if (H % Hkv || (G != 1 && G != 2 && G != 4 && G != 8)) return false;
+  if (Hkv > sm_count()) return false;  // one attention split per CTA
   int kmax = d > H * D ? d : H * D;
   if (F > kmax) kmax = F;
   if (kmax > 4 * kMkConsumers * kMkXRegs) return false;  // digits staged from registers
@@ -789,8 +1156,9 @@ bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch)
   a.F = F;
   a.V = V;
   fill_sizes(a, sm_count());
+  if (a.tiles_max * 2 > kMkConsumers) return false;  // scale prefetch: one cp.async per thread
   MkLayout Ly;
-  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max, a.tiles_res, a.D);
   return Ly.total <= 227 * 1024;
 }
 
@@ -798,7 +1166,7 @@ tb_status_t megakernel_launch(MkArgs a, cudaStream_t st) {
   const int grid = sm_count();
   fill_sizes(a, grid);
   MkLayout Ly;
-  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max);
+  Ly.init(a.kmax_bytes, a.xbuf_floats, a.merge_bytes, a.tiles_max, a.tiles_res, a.D);
   const size_t smem = Ly.total;
   cudaError_t e = cudaFuncSetAttribute(decode_megakernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_megakernel)");

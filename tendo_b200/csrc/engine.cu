@@ -51,7 +51,8 @@ struct tb_model {
   bool mk = false;      // whole decode step as one persistent kernel (batch 1)
   int mk_nsplit = 1;
   unsigned int* bar_counter = nullptr;
-  unsigned int* head_done = nullptr;
+  unsigned long long* mk_ll = nullptr;  // the persistent kernel's tagged exchange words (zeroed at creation)
+  unsigned int* mk_epoch = nullptr;      // its decode-step counter (never reset: tags stay unique)
   int* err_word = nullptr;
   uint64_t* trace = nullptr;  // [2 + 2 * (1 + 5 L + 1)] phase stamps of the last decode step
   tb_comm* comm = nullptr;    // tensor-parallel group (null: the whole model on one GPU)
@@ -523,11 +524,8 @@ tb::MkArgs mk_args(tb_model* m) {
   a.kc = static_cast<float*>(m->kc);  // the persistent kernel runs fp32 caches only
   a.vc = static_cast<float*>(m->vc);
   a.h = m->h;
-  a.q = m->qbuf;
-  a.partial = m->partial;
-  a.attn = m->attn;
-  a.head_done = m->head_done;
-  a.act = m->g;
+  a.ll = m->mk_ll;
+  a.epoch = m->mk_epoch;
   a.logits = m->logits;
   a.keys = m->keys;
   a.tokens = m->tokens;
@@ -538,6 +536,7 @@ tb::MkArgs mk_args(tb_model* m) {
   a.bar_counter = m->bar_counter;
   a.err = m->err_word;
   a.trace = m->trace;
+  a.utrace = m->trace ? m->trace + m->trace_n : nullptr;
   return a;
 }
 
@@ -635,11 +634,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
     m->mk = !(e && e[0] == '0') && tp == 1 && !m->kv16 &&
             tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
-    int ns = tb::sm_count() / (int)m->Hkv;  // about one attention unit per SM
-    if (ns < 1) ns = 1;
-    if (ns > 8) ns = 8;  // kMkMaxSplit
-    if (ns > m->nsplit) ns = m->nsplit;
-    m->mk_nsplit = ns;
+    m->mk_nsplit = tb::megakernel_splits((int)m->Hkv);
   }
   tb_status_t s = TB_SUCCESS;
   auto A = [&](tb_status_t r) {
@@ -684,11 +679,12 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     // split partials of the decode attention: the per-step kernels' layout
     // and, at batch 1, the persistent kernel's (its rows are D + 4 floats)
     size_t pb = tb::attn_decode_workspace((int)m->B, (int)m->H, (int)m->D, m->nsplit);
-    if (m->mk) {
-      const size_t mb = tb::megakernel_partial_bytes((int)m->H, (int)m->D, m->mk_nsplit);
-      if (mb > pb) pb = mb;
-    }
     A(dalloc(m, &m->partial, pb / sizeof(float)));
+  }
+  if (m->mk) {
+    const size_t w = tb::megakernel_ll_words((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, m->mk_nsplit);
+    A(dalloc(m, &m->mk_ll, w));
+    A(dalloc(m, &m->mk_epoch, 1));
   }
   A(dalloc(m, &m->logits, (size_t)m->B * m->V));
   A(dalloc(m, &m->last, (size_t)m->B * m->d));
@@ -700,10 +696,8 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->step, 1));
   A(dalloc(m, &m->bad, 1));
   A(dalloc(m, &m->bar_counter, 1));
-  A(dalloc(m, &m->head_done, (size_t)m->Hkv));
-  // start, embed barrier (2), per layer 19 stamps, lm_head (1 + barrier 2)
-  m->trace_n = 1 + 2 + 19 * (int)m->L + 3;
-  A(dalloc(m, &m->trace, (size_t)m->trace_n));
+  m->trace_n = tb::megakernel_trace_stamps((int)m->L);
+  A(dalloc(m, &m->trace, (size_t)m->trace_n + 2 * (size_t)tb::kMkUnitTrace));
   A(dalloc(m, &m->err_word, 1));
   A(dalloc(m, &m->samp_u, (size_t)m->B));
   A(dalloc(m, &m->samp_bad, 1));
@@ -745,7 +739,11 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     if (e == cudaSuccess) e = cudaMemset(m->step, 0, sizeof(int64_t));
     if (e == cudaSuccess) e = cudaMemset(m->bad, 0, sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMemset(m->bar_counter, 0, sizeof(unsigned int));
-    if (e == cudaSuccess) e = cudaMemset(m->head_done, 0, sizeof(unsigned int) * m->Hkv);
+    if (e == cudaSuccess && m->mk) {
+      const size_t w = tb::megakernel_ll_words((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, m->mk_nsplit);
+      e = cudaMemset(m->mk_ll, 0, w * sizeof(unsigned long long));
+      if (e == cudaSuccess) e = cudaMemset(m->mk_epoch, 0, sizeof(unsigned int));
+    }
     if (e == cudaSuccess) e = cudaMemset(m->err_word, 0, sizeof(int));
     if (e != cudaSuccess) s = tb::cuda_fail(e, "engine init");
   }
@@ -943,6 +941,19 @@ extern "C" tb_status_t tb_model_phase_times(tb_model* m, double* us, int max_ent
   TB_CUDA(cudaMemcpy(t.data(), m->trace, sizeof(uint64_t) * t.size(), cudaMemcpyDeviceToHost));
   int n = 0;
   for (int i = 1; i < m->trace_n && n < max_entries; i++, n++) us[n] = (double)(t[i] - t[i - 1]) * 1e-3;
+  *n_out = n;
+  return TB_SUCCESS;
+}
+
+extern "C" tb_status_t tb_model_unit_times(tb_model* m, uint64_t* ns, int max_entries, int* n_out) {
+  TB_REQUIRE(m && ns && n_out && max_entries >= 0);
+  DeviceGuard guard(m->device);
+  *n_out = 0;
+  if (!m->mk) return TB_ERROR_NOT_SUPPORTED;
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  int n = 2 * tb::kMkUnitTrace;
+  if (n > max_entries) n = max_entries;
+  TB_CUDA(cudaMemcpy(ns, m->trace + m->trace_n, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
   *n_out = n;
   return TB_SUCCESS;
 }

@@ -84,28 +84,40 @@ struct MkArgs {
   const float* sin_t;
   float* kc;  // [L][Hkv][max_seq][D]
   float* vc;
-  float* h;        // [d]
-  float* q;        // [H D]
-  float* partial;  // [H][nsplit][D + 4]
-  float* attn;     // [H D] combined attention output
-  unsigned int* head_done;  // [Hkv] splits finished this step (zero between steps)
-  float* act;      // [F]
-  float* logits;   // [V]
+  float* h;  // [d] residual stream after the last layer
+  // Tagged exchange words (megakernel_ll_words of them, zeroed at creation):
+  // each holds an fp32 value in its low half and the epoch tag of the phase
+  // that wrote it in its high half, so a reader polls the data itself.
+  unsigned long long* ll;
+  unsigned int* epoch;  // decode steps run so far (tags of step e are unique to it)
+  float* logits;  // [V]
   unsigned long long* keys;
   int64_t* tokens;
   int64_t* history;
   int64_t* step;
   int64_t* pos;
   int64_t hist_cap;
-  unsigned int* bar_counter;  // grid-barrier arrivals (zeroed by the launch)
+  unsigned int* bar_counter;  // arrivals at the step's final barrier (zeroed by the launch)
   int* err;                   // bounded waits that expired
-  uint64_t* trace;            // optional: CTA 0 barrier arrival/departure times (ns)
-  int kmax_bytes, xbuf_floats, tiles_max;  // filled by megakernel_launch
+  uint64_t* trace;            // optional: CTA 0 phase stamps (ns)
+  uint64_t* utrace;           // optional: CTA 0 weight-stream units: [2 u] issued, [2 u + 1] landed (ns)
+  // filled by megakernel_launch: sizes, and the shared-memory layout and
+  // exchange-buffer offsets (kept in the parameter bank, not in registers)
+  int kmax_bytes, xbuf_floats, tiles_max, tiles_res, RSX;
   size_t merge_bytes;
+  uint32_t sm_dig, sm_xbuf, sm_ssc, sm_res, sm_rope, sm_red, sm_bar;
+  uint32_t ll_q, ll_kv, ll_part, ll_attn, ll_h, ll_act;
 };
+// weight-stream units of CTA 0 whose issue and landing times the unit trace keeps
+constexpr int kMkUnitTrace = 4096;
+// phase stamps of one persistent decode step: start, 13 per layer, 3 for the
+// lm_head (norm, tiles up to the final barrier, barrier)
+inline int megakernel_trace_stamps(int L) { return 1 + 13 * L + 3; }
 bool megakernel_supported(int d, int H, int Hkv, int D, int F, int V, int batch);
-// Bytes of MkArgs::partial: H heads x nsplit splits x (D + 4) floats.
-size_t megakernel_partial_bytes(int H, int D, int nsplit);
+// attention splits per kv head of the persistent kernel (one split per CTA)
+int megakernel_splits(int Hkv);
+// tagged exchange words MkArgs::ll holds
+size_t megakernel_ll_words(int d, int H, int Hkv, int D, int F, int nsplit);
 tb_status_t megakernel_launch(MkArgs a, cudaStream_t st);
 
 // gemv.cu
