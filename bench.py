@@ -408,6 +408,18 @@ def run_ours(args):
                "sample": f"{n} greedy decode tokens at positions 512.. of the same 7B workload, oracle restatement "
                          f"of tendo's CPU path on {threads} host threads (weights copied from the device)"}
 
+    # the timed tokens against the oracle's golden stream of this workload
+    # (tests/golden/llama7b_decode.json: same weights, prompt seed 0)
+    parity = None
+    if rank == 0:
+        with open(os.path.join(ROOT, "tests", "golden", "llama7b_decode.json")) as f:
+            gold = [st["token"] for st in json.load(f)["steps"]]
+        n_chk = min(len(gold), NEW + 1)
+        got = [int(t) for t in toks[:n_chk]]
+        if got != gold[:n_chk]:
+            raise SystemExit(f"decode tokens differ from the oracle's golden stream: {got} != {gold[:n_chk]}")
+        parity = {"fixture": "tests/golden/llama7b_decode.json", "greedy_tokens_checked": n_chk, "match": True}
+
     phases = summarize_phases(qm.phase_times())
     launches = qm.launches_per_step * NEW * args.steps
     if rank == 0:
@@ -420,6 +432,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2: 6.5 GB int8 weights + 0.52 GB fp32 lm_head stream per token"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clk, "standalone_kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
+            "parity": parity,
         }
         print(json.dumps(line), flush=True)
     qm.close()

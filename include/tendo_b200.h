@@ -87,7 +87,10 @@ TB_API tb_status_t tb_dequantize_i8_f32(float* w, const int8_t* q, const float* 
  * 2^-21 s sum|w| of the fp32 product.  M <= 32: the weights are the MMA's
  * 128-row operand and the (tile, K block) work is split evenly over the SMs
  * (K % 128 == 0; other K run the CUDA-core GEMV).  M > 32: 128 x 128 output
- * tiles.  Per-group scales (group_size > 0) run the CUDA-core kernels.
+ * tiles.  Per-group scales (group_size > 0) take the same tcgen05 paths when
+ * the group is a multiple of 128 (M > 32: at most 128 groups per row): the
+ * exact s32 sum of each group is scaled by scale[n, group] and added in fp32
+ * in a fixed order; other group sizes run the CUDA-core kernels.
  * Scratch: this entry point keeps library-owned buffers per device,
  * allocated on first use and grown on demand (calls that overlap in time on
  * one device must use tb_dequant_matmul_i8f32_ws). */
@@ -194,9 +197,10 @@ TB_API tb_status_t tb_attention_f32(float* out, const float* q, const float* kca
  * layout as tb_attention_f32 with Sq == 1.  Its split-K partials live in one
  * library-owned device array of TB_ATTENTION_NOALLOC_SCRATCH_BYTES per GPU
  * (kept until the process exits); sizes whose partials do not fit are
- * rejected with TB_ERROR_INVALID_ARGUMENT.  The first call on a device looks
- * up that array's address (cudaGetSymbolAddress) and caches it; make that
- * first call before any stream capture.  Every call on a device shares the
+ * rejected with TB_ERROR_INVALID_ARGUMENT.  Each call looks up that array's
+ * address on the current device (cudaGetSymbolAddress); the first call on a
+ * device also loads the library's device code there, so make that first call
+ * before any stream capture.  Every call on a device shares the
  * array, so calls that overlap on the GPU (different streams, or host
  * threads without ordering) race and corrupt each other's partials. */
 #define TB_ATTENTION_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
@@ -312,6 +316,10 @@ TB_API tb_status_t tb_model_set_tensor(tb_model* m, int which, int layer, const 
 TB_API tb_status_t tb_model_get_tensor(tb_model* m, int which, int layer, float* host);
 /* Copies one quantized Linear back to host arrays. */
 TB_API tb_status_t tb_model_get_linear(tb_model* m, int layer, int mat, int8_t* q_host, float* scale_host);
+/* ExtractLastLogits (models/sampling.go:214-243): the logits [B, V] of the
+ * last forward or decode step (this rank's vocabulary rows under tensor
+ * parallelism) copied to a host array, after the engine stream drains. */
+TB_API tb_status_t tb_model_last_logits(tb_model* m, float* logits_host);
 /* Empties the KV cache (position 0). */
 TB_API tb_status_t tb_model_reset(tb_model* m);
 TB_API int64_t tb_model_position(const tb_model* m);

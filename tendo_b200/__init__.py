@@ -99,6 +99,7 @@ SIGNATURES = [
     ("tb_model_launches_per_step", _i64, [_vp]),
     ("tb_model_phase_times", _st, [_vp, _vp, ctypes.c_int, _vp]),
     ("tb_model_unit_times", _st, [_vp, _vp, ctypes.c_int, _vp]),
+    ("tb_model_last_logits", _st, [_vp, _vp]),
 ]
 
 
@@ -487,6 +488,8 @@ class QuantizedModel:
         else:
             check(lib.tb_model_create_tp(ctypes.byref(h), ctypes.byref(c), device, comm.h))
         self.h = h
+        # vocabulary rows of this rank's lm_head (all of them without tensor parallelism)
+        self.V_local = cfg["vocab"] // (comm.nranks if comm else 1)
 
     def close(self):
         if getattr(self, "h", None):
@@ -538,6 +541,14 @@ class QuantizedModel:
         us = ctypes.c_float()
         check(lib.tb_model_time_kernel(self.h, kind, reps, ctypes.byref(us)))
         return float(us.value)
+
+    def last_logits(self):
+        """Logits [B, V] of the last forward or decode step (ExtractLastLogits)."""
+        import numpy as np
+
+        out = np.empty((self.B, self.V_local), np.float32)
+        check(lib.tb_model_last_logits(self.h, out.ctypes.data))
+        return out
 
     def reset(self):
         check(lib.tb_model_reset(self.h))

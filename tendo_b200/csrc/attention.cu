@@ -12,7 +12,6 @@
 // kernel with the online softmax, so no [S, S] score matrix is stored.
 #include <math.h>
 
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -674,24 +673,15 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_attn_scratch[TB_ATTENTION_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {nullptr};
-
-// Device address of the scratch array on the current device, looked up once
-// per device (the host-side symbol is only a stand-in for it).
+// Device address of the scratch array on the current device.  The host-side
+// symbol is only a stand-in for it; the address is looked up on every call
+// (a cheap host query), so it stays right after a device reset reloads the
+// library's device code at a new address.
 tb_status_t noalloc_scratch(void** out) {
-  int dev = 0;
-  TB_CUDA(cudaGetDevice(&dev));
-  TB_REQUIRE(dev >= 0 && dev < kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
-    if (e != cudaSuccess) return tb::cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_attn_scratch)");
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
+  if (e != cudaSuccess) return tb::cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_attn_scratch)");
+  *out = p;
   return TB_SUCCESS;
 }
 

@@ -958,6 +958,15 @@ extern "C" tb_status_t tb_model_unit_times(tb_model* m, uint64_t* ns, int max_en
   return TB_SUCCESS;
 }
 
+extern "C" tb_status_t tb_model_last_logits(tb_model* m, float* logits_host) {
+  TB_INJECT("tb_model_last_logits");
+  TB_REQUIRE(m && logits_host);
+  DeviceGuard guard(m->device);
+  TB_CUDA(cudaStreamSynchronize(m->stream));
+  TB_CUDA(cudaMemcpy(logits_host, m->logits, sizeof(float) * m->B * m->V, cudaMemcpyDeviceToHost));
+  return TB_SUCCESS;
+}
+
 extern "C" tb_status_t tb_model_reset(tb_model* m) {
   TB_REQUIRE(m);
   DeviceGuard guard(m->device);

@@ -29,8 +29,13 @@ def _case(B, H, Hkv, D, sk, max_seq, seed):
     return q, kc, vc
 
 
-@pytest.mark.parametrize("B,H,Hkv,D,sk,max_seq", [(1, 32, 32, 128, 641, 2048), (2, 64, 8, 128, 300, 512),
-                                                  (3, 8, 8, 64, 1, 16)])
+@pytest.mark.parametrize("B,H,Hkv,D,sk,max_seq", [
+    (1, 32, 32, 128, 641, 2048),  # the 7B decode shape
+    (2, 64, 8, 128, 300, 512),    # 70B grouping: 8 query heads per kv head
+    (2, 32, 4, 64, 97, 256),      # 8 query heads per kv head at head_dim 64
+    (3, 8, 8, 64, 1, 16),         # a one-key cache
+    (16, 64, 8, 128, 2000, 2048),  # one split of partials is 532 KB: fewer splits than the workspace path
+])
 def test_noalloc_matches_workspace_entry_point(tb, cuda, B, H, Hkv, D, sk, max_seq):
     import torch
 
@@ -51,6 +56,29 @@ def test_noalloc_matches_workspace_entry_point(tb, cuda, B, H, Hkv, D, sk, max_s
         r, g = ref.cpu().numpy(), got.cpu().numpy()
         assert np.isfinite(g).all()
         assert float(np.abs(g - r).max()) <= TOL * float(np.abs(r).max())
+
+
+def test_noalloc_split_count_is_capped_by_the_scratch(tb):
+    """The 16-sequence case above runs with fewer splits than the workspace
+    path picks: B * H * (D + 2) * 4 bytes per split fit three times."""
+    B, H, D = 16, 64, 128
+    per_split = B * H * (D + 2) * 4
+    assert 2 * 1024 * 1024 // per_split == 3
+    # the workspace entry point sizes for more splits than that
+    assert tb.lib.tb_attention_workspace_size(B, H, 1, D, 2048) > 3 * per_split
+
+
+def test_noalloc_rejects_unsupported_head_grouping(tb, cuda):
+    import torch
+
+    # head_dim 32 with 8 query heads per kv head has no decode kernel (as for tb_attention_f32)
+    B, H, Hkv, D = 1, 16, 2, 32
+    q = torch.zeros((B, 1, H, D), device=cuda)
+    kc = torch.zeros((B, Hkv, 8, D), device=cuda)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = tb.lib.tb_attention_decode_noalloc_f32(q.data_ptr(), q.data_ptr(), kc.data_ptr(), kc.data_ptr(), B, H, Hkv,
+                                                4, D, 8, 0.1, st)
+    assert rc == tb.TB_ERROR_NOT_SUPPORTED
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(tb, cuda):
