@@ -153,6 +153,61 @@ TB_API tb_status_t tb_silu_mul_f32(float* out, const float* gate, const float* u
 TB_API tb_status_t tb_add_f32(float* out, const float* a, const float* b, int64_t n, tb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Generic fp32 tensor ops of llama.Backend (models/llama/forward.go:13-27)
+ *
+ * The ops unchanged models/llama attention issues between its projections
+ * (quantized.go:282-372): Q.K^T and P.V on strided views, the scale Mul, the
+ * causal mask (Ones, Tril, Full, Where), Softmax and the KV-cache Cat.  Each
+ * takes views as (rank, shape, element strides per dimension; a stride of 0
+ * broadcasts or expands) and writes a new contiguous tensor of the output
+ * shape, as the reference backends return new tensors.  NULL strides mean
+ * contiguous.  Shape and stride arrays are HOST memory; data pointers are
+ * device memory.  Arithmetic in the reference CPU backend's order
+ * (cpu/backend.go).
+ * ------------------------------------------------------------------------- */
+
+#define TB_MAX_RANK 6
+
+typedef enum { TB_BINARY_ADD = 0, TB_BINARY_SUB = 1, TB_BINARY_MUL = 2, TB_BINARY_DIV = 3 } tb_binary_op_t;
+
+/* Full / Ones / Zeros (cpu/backend.go:60-86; cuda/backend.go:88-96): n
+ * elements set to value. */
+TB_API tb_status_t tb_fill_f32(float* out, float value, int64_t n, tb_stream_t stream);
+/* Add / Sub / Mul / Div with broadcasting (cpu/backend.go:257-271,
+ * binaryElementwise :1511-1560; cuda/backend.go:244-266): out[i] =
+ * a[i] op b[i] in float32 over `shape`; a broadcast operand has stride 0. */
+TB_API tb_status_t tb_binary_f32(float* out, const float* a, const float* b, int op, int rank, const int64_t* shape,
+                          const int64_t* a_strides, const int64_t* b_strides, tb_stream_t stream);
+/* Where (cpu/backend.go:1191-1255; cuda/backend.go:644): out = cond > 0 ? x : y. */
+TB_API tb_status_t tb_where_f32(float* out, const float* cond, const float* x, const float* y, int rank,
+                         const int64_t* shape, const int64_t* cond_strides, const int64_t* x_strides,
+                         const int64_t* y_strides, tb_stream_t stream);
+/* Tril (cpu/backend.go:1257-1285; cuda/backend.go:650) of a contiguous 2-D
+ * tensor: keeps [r, c] where c <= r + k, else 0. */
+TB_API tb_status_t tb_tril_f32(float* out, const float* in, int64_t rows, int64_t cols, int64_t k, tb_stream_t stream);
+/* Softmax along dim (cpu/backend.go:1690-1744; cuDNN in cuda/ops.go:88-180):
+ * per slice the max seeded at -MaxFloat32, exp(x - max) in double precision
+ * rounded to float, a sequential float32 sum, then x / sum. */
+TB_API tb_status_t tb_softmax_f32(float* out, const float* in, int rank, const int64_t* shape,
+                           const int64_t* in_strides, int dim, tb_stream_t stream);
+/* MatMul (cpu/backend.go:281-308 via gonum Gemm; cuBLAS in cuda/backend.go:268)
+ * over batch dimensions: out[batch..., M, N] = sum_k a[batch..., m, k] *
+ * b[batch..., k, n], with a's element (m, k) at a_rs m + a_cs k plus its batch
+ * offset and b's (k, n) at b_rs k + b_cs n (a transposed view is a stride
+ * swap; a broadcast batch dimension has stride 0).  Products rounded, then
+ * summed in k order. */
+TB_API tb_status_t tb_matmul_f32(float* out, const float* a, const float* b, int batch_rank,
+                          const int64_t* batch_shape, const int64_t* a_batch_strides,
+                          const int64_t* b_batch_strides, int64_t M, int64_t N, int64_t K, int64_t a_rs,
+                          int64_t a_cs, int64_t b_rs, int64_t b_cs, tb_stream_t stream);
+/* Cat of two tensors along dim (cpu/backend.go:1343-1407; popcornCat_f32,
+ * cuda/popcorn.go:1077-1085): out has a's shape with a_shape[dim] +
+ * b_shape[dim] along dim. */
+TB_API tb_status_t tb_cat_f32(float* out, const float* a, const float* b, int rank, const int64_t* a_shape,
+                       const int64_t* a_strides, const int64_t* b_shape, const int64_t* b_strides, int dim,
+                       tb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * RoPE and attention (nn/rope.go; models/llama/quantized.go:229-382)
  * ------------------------------------------------------------------------- */
 

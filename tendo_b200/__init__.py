@@ -31,6 +31,8 @@ TB_GEMM_SIMT = 2
 
 TB_MODEL_KV_BF16 = 1
 
+TB_BINARY_ADD, TB_BINARY_SUB, TB_BINARY_MUL, TB_BINARY_DIV = 0, 1, 2, 3
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -58,6 +60,14 @@ SIGNATURES = [
     ("tb_rope_tables_host", _st, [_vp, _vp, ctypes.c_int, ctypes.c_int, _f32]),
     ("tb_rope_apply_f32", _st, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     ("tb_kv_append_rope_f32", _st, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    ("tb_fill_f32", _st, [_vp, _f32, _i64, _vp]),
+    ("tb_binary_f32", _st, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp]),
+    ("tb_where_f32", _st, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, _vp]),
+    ("tb_tril_f32", _st, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    ("tb_softmax_f32", _st, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp]),
+    ("tb_matmul_f32", _st, [_vp, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                            _vp]),
+    ("tb_cat_f32", _st, [_vp, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
     ("tb_attention_workspace_size", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     ("tb_attention_f32", _st,
      [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, ctypes.c_size_t, _vp]),
@@ -160,6 +170,15 @@ def _stream(stream=None):
     return ctypes.c_void_p(s.cuda_stream)
 
 
+def _need_cuda_view(*ts):
+    """CUDA fp32 tensors of any strides (the strided tensor ops)."""
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ShapeError("tendo_b200 ops take CUDA tensors (DeviceError in tendo terms)")
+        if t is not None and t.dtype != _torch().float32:
+            raise ShapeError("tendo_b200 tensor ops take float32 tensors")
+
+
 def _need_cuda(*ts):
     for t in ts:
         if t is not None and not t.is_cuda:
@@ -176,6 +195,42 @@ class QuantizedTensor:
     scale: object  # torch.float32 [N] or [N, K / group]
     shape: tuple
     group_size: int = 0
+
+
+def _broadcast_shape(a, b, op):
+    """tendo.BroadcastShapes: right-aligned, each pair equal or one of them 1."""
+    a, b = tuple(a), tuple(b)
+    n = max(len(a), len(b))
+    a = (1,) * (n - len(a)) + a
+    b = (1,) * (n - len(b)) + b
+    out = []
+    for x, y in zip(a, b):
+        if x != y and x != 1 and y != 1:
+            raise ShapeError(f"{op}: shapes {a} and {b} do not broadcast")
+        out.append(max(x, y))
+    return tuple(out)
+
+
+def _bcast_strides(out_shape, shape, strides):
+    """Element strides of a view of `shape` broadcast to `out_shape` (0 where broadcast)."""
+    n = len(out_shape)
+    shape, strides = tuple(shape), tuple(strides)
+    pad = n - len(shape)
+    res = []
+    for d in range(n):
+        if d < pad or shape[d - pad] == 1 and out_shape[d] != 1:
+            res.append(0)
+        else:
+            res.append(strides[d - pad])
+    return res
+
+
+def _view_arrays(out_shape, t):
+    """(shape, strides) ctypes arrays of tensor t viewed at out_shape."""
+    n = len(out_shape)
+    sh = (ctypes.c_int64 * n)(*out_shape)
+    st = (ctypes.c_int64 * n)(*_bcast_strides(out_shape, t.shape, t.stride()))
+    return sh, st
 
 
 class Backend:
@@ -300,13 +355,116 @@ class Backend:
         check(lib.tb_silu_mul_f32(_ptr(out), _ptr(gate), _ptr(up), gate.numel(), _stream()))
         return out
 
+    # ElementwiseOps with broadcasting (cpu/backend.go:257-271, :1511-1560)
     def Add(self, a, b):
         torch = _torch()
-        _need_cuda(a, b)
-        if a.shape != b.shape:
-            raise ShapeError(f"add: shapes {tuple(a.shape)} and {tuple(b.shape)}")
-        out = torch.empty_like(a)
-        check(lib.tb_add_f32(_ptr(out), _ptr(a), _ptr(b), a.numel(), _stream()))
+        _need_cuda_view(a, b)
+        if a.shape == b.shape and a.is_contiguous() and b.is_contiguous():
+            out = torch.empty_like(a)
+            check(lib.tb_add_f32(_ptr(out), _ptr(a), _ptr(b), a.numel(), _stream()))
+            return out
+        return self._binary(TB_BINARY_ADD, a, b)
+
+    def Sub(self, a, b):
+        return self._binary(TB_BINARY_SUB, a, b)
+
+    def Mul(self, a, b):
+        return self._binary(TB_BINARY_MUL, a, b)
+
+    def Div(self, a, b):
+        return self._binary(TB_BINARY_DIV, a, b)
+
+    def _binary(self, op, a, b):
+        torch = _torch()
+        _need_cuda_view(a, b)
+        shape = _broadcast_shape(a.shape, b.shape, "binary op")
+        out = torch.empty(shape, dtype=torch.float32, device=a.device)
+        sh, sa = _view_arrays(shape, a)
+        _, sb = _view_arrays(shape, b)
+        check(lib.tb_binary_f32(_ptr(out), _ptr(a), _ptr(b), op, len(shape), sh, sa, sb, _stream()))
+        return out
+
+    # StorageBackend Full / Ones / Zeros (cpu/backend.go:60-86)
+    def Full(self, value: float, *shape):
+        torch = _torch()
+        out = torch.empty(shape, dtype=torch.float32, device=f"cuda:{self.device}")
+        check(lib.tb_fill_f32(_ptr(out), float(value), out.numel(), _stream()))
+        return out
+
+    def Ones(self, *shape):
+        return self.Full(1.0, *shape)
+
+    def Zeros(self, *shape):
+        return self.Full(0.0, *shape)
+
+    # Where (cpu/backend.go:1191-1255): cond > 0 ? x : y, broadcast over all three
+    def Where(self, condition, x, y):
+        torch = _torch()
+        _need_cuda_view(condition, x, y)
+        shape = _broadcast_shape(_broadcast_shape(condition.shape, x.shape, "where"), y.shape, "where")
+        out = torch.empty(shape, dtype=torch.float32, device=x.device)
+        sh, sc = _view_arrays(shape, condition)
+        _, sx = _view_arrays(shape, x)
+        _, sy = _view_arrays(shape, y)
+        check(lib.tb_where_f32(_ptr(out), _ptr(condition), _ptr(x), _ptr(y), len(shape), sh, sc, sx, sy, _stream()))
+        return out
+
+    # Tril (cpu/backend.go:1257-1285): 2-D input
+    def Tril(self, t, k: int = 0):
+        torch = _torch()
+        _need_cuda_view(t)
+        if t.dim() != 2:
+            raise ShapeError("tril: input must be 2D")
+        src = t.contiguous()
+        out = torch.empty_like(src)
+        check(lib.tb_tril_f32(_ptr(out), _ptr(src), t.shape[0], t.shape[1], int(k), _stream()))
+        return out
+
+    # Softmax along dim (cpu/backend.go:1690-1744)
+    def Softmax(self, t, dim: int = -1):
+        torch = _torch()
+        _need_cuda_view(t)
+        out = torch.empty(t.shape, dtype=torch.float32, device=t.device)
+        sh, st = _view_arrays(tuple(t.shape), t)
+        check(lib.tb_softmax_f32(_ptr(out), _ptr(t), t.dim(), sh, st, int(dim), _stream()))
+        return out
+
+    # MatrixOps.MatMul (cpu/backend.go:281-308): a [..., M, K] @ b [..., K, N], batch dims broadcast
+    def MatMul(self, a, b):
+        torch = _torch()
+        _need_cuda_view(a, b)
+        if a.dim() < 2 or b.dim() < 2:
+            raise ShapeError("matmul: operands must be at least 2D")
+        M, K = a.shape[-2], a.shape[-1]
+        K2, N = b.shape[-2], b.shape[-1]
+        if K != K2:
+            raise ShapeError(f"matmul: inner dimensions {K} and {K2}")
+        batch = _broadcast_shape(a.shape[:-2], b.shape[:-2], "matmul")
+        out = torch.empty((*batch, M, N), dtype=torch.float32, device=a.device)
+        nb = len(batch)
+        bs = (ctypes.c_int64 * max(nb, 1))(*batch)
+        sa = (ctypes.c_int64 * max(nb, 1))(*_bcast_strides(batch, a.shape[:-2], a.stride()[:-2]))
+        sb = (ctypes.c_int64 * max(nb, 1))(*_bcast_strides(batch, b.shape[:-2], b.stride()[:-2]))
+        check(lib.tb_matmul_f32(_ptr(out), _ptr(a), _ptr(b), nb, bs, sa, sb, M, N, K, a.stride(-2), a.stride(-1),
+                                b.stride(-2), b.stride(-1), _stream()))
+        return out
+
+    # Cat along dim (cpu/backend.go:1343-1407)
+    def Cat(self, tensors, dim: int):
+        torch = _torch()
+        out = tensors[0]
+        for t in tensors[1:]:
+            _need_cuda_view(out, t)
+            if out.dim() != t.dim():
+                raise ShapeError("cat: ranks differ")
+            d = dim % out.dim()
+            shape = list(out.shape)
+            shape[d] += t.shape[d]
+            res = torch.empty(shape, dtype=torch.float32, device=out.device)
+            sa_shape, sa = _view_arrays(tuple(out.shape), out)
+            sb_shape, sb = _view_arrays(tuple(t.shape), t)
+            check(lib.tb_cat_f32(_ptr(res), _ptr(out), _ptr(t), out.dim(), sa_shape, sa, sb_shape, sb, d, _stream()))
+            out = res
         return out
 
     # EmbeddingOps.Embedding (cpu/backend.go:1289-1339)
