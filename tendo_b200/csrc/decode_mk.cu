@@ -401,32 +401,34 @@ __device__ float stage_digits_n(int8_t* dig, int RSX, const float* plain, const 
   const float rms = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)) : 1.0f;
   if (norm_w) a = a / rms * 1.0001f;
   const float sc = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
-  const float inv = 1.0f / sc;
+  // one multiplier per element: u = x * w / (rms * sc), |u| < 127; then u is
+  // rounded to a multiple of 2^-14 (U = round(u 2^14)) and U is split exactly
+  // into balanced digits U = d0 2^14 + d1 2^7 + d2 (d0 in [-127, 127], d1
+  // and d2 in [-64, 63]) with integer shifts
+  const float c = __fdiv_rn(1.0f, rms) * (1.0f / sc);
 #pragma unroll
   for (int i = 0; i < NV; i++) {
     const int v = threadIdx.x + i * kMkConsumers;
     if (v >= nv) continue;
-    float4 t = xv[i];
-    if (norm_w) {
-      const float4 w = w4[i];
-      t.x = __fmul_rn(__fdiv_rn(t.x, rms), w.x);
-      t.y = __fmul_rn(__fdiv_rn(t.y, rms), w.y);
-      t.z = __fmul_rn(__fdiv_rn(t.z, rms), w.z);
-      t.w = __fmul_rn(__fdiv_rn(t.w, rms), w.w);
-    }
-    const float vals[4] = {t.x, t.y, t.z, t.w};
-    uint32_t p0 = 0, p1 = 0, p2 = 0;
+    const float4 t = xv[i];
+    const float4 w = w4[i];  // ones without a norm
+    const float vals[4] = {t.x * (w.x * c), t.y * (w.y * c), t.z * (w.z * c), t.w * (w.w * c)};
+    int b0[4], b1[4], b2[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const float uu = fminf(fmaxf(vals[j] * inv, -127.0f), 127.0f);
-      const float d0 = rintf(uu);
-      const float r1 = (uu - d0) * 128.0f;
-      const float d1 = rintf(r1);
-      const float d2 = rintf((r1 - d1) * 128.0f);
-      p0 |= ((uint32_t)__float2int_rn(d0) & 0xffu) << (8 * j);
-      p1 |= ((uint32_t)__float2int_rn(d1) & 0xffu) << (8 * j);
-      p2 |= ((uint32_t)__float2int_rn(d2) & 0xffu) << (8 * j);
+      int U = __float2int_rn(vals[j] * 16384.0f);
+      U = min(max(U, -127 * 16384), 127 * 16384);
+      const int d0 = (U + 8192) >> 14;
+      const int r = U - (d0 << 14);
+      const int d1 = (r + 64) >> 7;
+      b0[j] = d0;
+      b1[j] = d1;
+      b2[j] = r - (d1 << 7);
     }
+    // low bytes of four ints -> one word
+    const uint32_t p0 = __byte_perm(__byte_perm(b0[0], b0[1], 0x0040), __byte_perm(b0[2], b0[3], 0x0040), 0x5410);
+    const uint32_t p1 = __byte_perm(__byte_perm(b1[0], b1[1], 0x0040), __byte_perm(b1[2], b1[3], 0x0040), 0x5410);
+    const uint32_t p2 = __byte_perm(__byte_perm(b2[0], b2[1], 0x0040), __byte_perm(b2[2], b2[3], 0x0040), 0x5410);
     reinterpret_cast<uint32_t*>(dig)[v] = p0;
     reinterpret_cast<uint32_t*>(dig + RSX)[v] = p1;
     reinterpret_cast<uint32_t*>(dig + 2 * RSX)[v] = p2;
