@@ -312,12 +312,11 @@ TB_API tb_status_t tb_model_create(tb_model** out, const tb_model_config* cfg, i
  * [V] logits: temperature (x / T when T != 1 and T > 0), top-k by value (0 or
  * >= V: off), top-p (0 or >= 1: off), then the first index whose fp32
  * cumulative probability exceeds uniforms[b] (the caller's draw in [0, 1),
- * the reference's rng.Float32()), in the reference's arithmetic and order.
- * V <= 40000; top-p needs at most 4096 tokens left after top-k, else the row
- * returns V - 1 and *unsupported is incremented.  Greedy is tb_argmax_f32. */
+ * the reference's rng.Float32()), in the reference's arithmetic and order;
+ * top-p orders every remaining candidate, as applyTopP (:99-124) does.
+ * V <= 40000.  Greedy is tb_argmax_f32. */
 TB_API tb_status_t tb_sample_f32(int64_t* tokens, const float* logits, const float* uniforms, int64_t B, int64_t V,
-                                 float temperature, int64_t top_k, float top_p, int32_t* unsupported,
-                                 tb_stream_t stream);
+                                 float temperature, int64_t top_k, float top_p, tb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Tensor parallelism (the 70B shape over 2/4/8 GPUs)

@@ -60,7 +60,6 @@ struct tb_model {
   int64_t Hg = 0, Hkvg = 0, Fg = 0, Vg = 0;  // unsharded heads, kv heads, hidden, vocabulary
   int64_t v0 = 0;                            // vocabulary index of this rank's first lm_head row
   float* samp_u = nullptr;    // the sampler's uniform draws [B]
-  int32_t* samp_bad = nullptr;  // rows the sampler could not serve
   bool gv = false;            // decode projections of 2..64 sequences on the tcgen05 GEMV (one weight pass)
   int lm_rows = 8;            // rows of x the fused lm_head GEMV stages in shared memory (0: the GEMM path)
   void* gv_zero = nullptr;    // its split-tile counters and sums (kept zero between launches)
@@ -700,7 +699,6 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->trace, (size_t)m->trace_n + 2 * (size_t)tb::kMkUnitTrace));
   A(dalloc(m, &m->err_word, 1));
   A(dalloc(m, &m->samp_u, (size_t)m->B));
-  A(dalloc(m, &m->samp_bad, 1));
   if (m->gv) {
     int64_t nmax = m->NQKV > m->d ? m->NQKV : m->d;
     if (m->F > nmax) nmax = m->F;
@@ -1074,11 +1072,10 @@ namespace {
 
 // After a step (greedy tail included): sample the step's logits instead and
 // make the sampled tokens the step's output (tokens feed the next step).
-tb_status_t sample_tail(tb_model* m, float temperature, int64_t top_k, float top_p, uint64_t seed, float* u,
-                        int32_t* bad) {
+tb_status_t sample_tail(tb_model* m, float temperature, int64_t top_k, float top_p, uint64_t seed, float* u) {
   cudaStream_t st = m->stream;
   TB_TRY(tb::sample_uniforms(u, m->step, m->B, seed, st));
-  TB_TRY(tb_sample_f32(m->tokens, m->logits, u, m->B, m->V, temperature, top_k, top_p, bad, (tb_stream_t)st));
+  TB_TRY(tb_sample_f32(m->tokens, m->logits, u, m->B, m->V, temperature, top_k, top_p, (tb_stream_t)st));
   return tb::history_set(m->history, m->tokens, m->step, m->B, m->hist_cap, st);
 }
 
@@ -1093,20 +1090,14 @@ extern "C" tb_status_t tb_model_generate_sample(tb_model* m, const int64_t* prom
   if (m->tp > 1) return TB_ERROR_NOT_SUPPORTED;  // the logits are sharded over the ranks
   DeviceGuard guard(m->device);
   float* u = m->samp_u;
-  int32_t* bad = m->samp_bad;
-  tb_status_t s = cudaMemset(bad, 0, sizeof(int32_t)) == cudaSuccess ? TB_SUCCESS : TB_ERROR_CUDA;
-  if (s == TB_SUCCESS) s = tb_model_reset(m);
+  tb_status_t s = tb_model_reset(m);
   if (s == TB_SUCCESS) s = tb_model_forward(m, prompt_host, B, S, nullptr, nullptr);
-  if (s == TB_SUCCESS) s = sample_tail(m, temperature, top_k, top_p, seed, u, bad);
+  if (s == TB_SUCCESS) s = sample_tail(m, temperature, top_k, top_p, seed, u);
   for (int64_t i = 1; i < n_new && s == TB_SUCCESS; i++) {
     s = tb_model_decode(m, nullptr, 1);  // the step's logits (and its greedy choice, replaced below)
-    if (s == TB_SUCCESS) s = sample_tail(m, temperature, top_k, top_p, seed, u, bad);
+    if (s == TB_SUCCESS) s = sample_tail(m, temperature, top_k, top_p, seed, u);
   }
-  int32_t bad_h = 0;
-  if (s == TB_SUCCESS && cudaMemcpy(&bad_h, bad, sizeof(int32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
-    s = TB_ERROR_CUDA;
   TB_TRY(s);
-  if (bad_h) return TB_ERROR_NOT_SUPPORTED;  // top-p over more than 4096 tokens
   std::vector<int64_t> hist((size_t)(n_new * B));
   TB_TRY(tb_model_tokens(m, hist.data(), n_new));
   for (int64_t t = 0; t < n_new; t++)

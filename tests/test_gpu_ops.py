@@ -240,7 +240,9 @@ def test_attention(oracle, be, cuda, B, H, Hkv, D, Sq, sk):
 
 # --- Sampler.Sample on the device (models/sampling.go:47-70) ----------------
 @pytest.mark.parametrize("V,T,K,P", [(32000, 1.0, 0, 0.0), (32000, 0.7, 50, 0.0), (32000, 1.3, 40, 0.9),
-                                     (4000, 1.0, 0, 0.9), (32000, 1.0, 1, 0.0), (1000, 0.5, 999, 0.95)])
+                                     (4000, 1.0, 0, 0.9), (32000, 1.0, 1, 0.0), (1000, 0.5, 999, 0.95),
+                                     (32000, 1.0, 0, 0.9), (32000, 0.8, 0, 0.5), (32000, 1.0, 0, 0.999),
+                                     (32000, 1.0, 20000, 0.97), (40000, 2.0, 0, 0.9)])
 def test_sample_matches_oracle(oracle, be, cuda, V, T, K, P):
     rng = np.random.default_rng(V + K)
     B = 6
@@ -252,9 +254,15 @@ def test_sample_matches_oracle(oracle, be, cuda, V, T, K, P):
     np.testing.assert_array_equal(got, np.array(want))
 
 
-def test_sample_top_p_without_top_k_over_a_large_vocab_is_reported(be, cuda):
-    import tendo_b200 as tb
-
-    logits = np.zeros((1, 32000), np.float32)
-    with pytest.raises(tb.ShapeError):
-        be.Sample(_t(logits, cuda), _t(np.array([0.5], np.float32), cuda), 1.0, 0, 0.9)
+@pytest.mark.parametrize("P", [0.9, 0.3])
+def test_sample_top_p_over_a_flat_vocab(oracle, be, cuda, P):
+    """Every probability equal: the cutoff lies thousands of candidates deep,
+    across several sorted batches, and the ties keep index order."""
+    V = 32000
+    logits = np.zeros((3, V), np.float32)
+    logits[1, 5:9] = 1e-3  # a few slightly larger values ahead of the ties
+    logits[2, ::2] = -50.0  # half the vocabulary with probabilities near zero
+    r = np.array([0.5, 0.999, 0.01], np.float32)
+    got = _np(be.Sample(_t(logits, cuda), _t(r, cuda), 1.0, 0, P))
+    want = [oracle.sample(logits[b], 1.0, 0, P, float(r[b])) for b in range(3)]
+    np.testing.assert_array_equal(got, np.array(want))
