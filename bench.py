@@ -17,6 +17,11 @@ collective): weak scaling.  `--impl reference` times the CPU restatement of
 tendo's path (the oracle) on the host cores for the same metric; under
 torchrun only rank 0 runs it.
 
+After the headline measurement the default run also measures, at the same
+rank count and in the same process group, the two multi-GPU workloads below
+(3 warm-up and min(K, 3) timed steps each) and attaches their lines to the
+one JSON line under "multi_gpu_workloads" (`--no-extra` skips them).
+
     python -m torch.distributed.run --nproc-per-node N bench.py --workload llama70b-tp --gpus N
 
 runs the Llama-70B shape tensor-parallel over the N ranks (N = 1 keeps the
@@ -65,6 +70,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default workload only: skip the serving and 70B tensor-parallel lines attached to it")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--workload", default="llama7b", choices=["llama7b", "llama70b-tp", "llama7b-serving"])
     ap.add_argument("--kv-bf16", action="store_true",
@@ -284,7 +291,7 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
         pg = dist
     import tendo_b200 as tb
 
@@ -434,8 +441,21 @@ def run_ours(args):
             "clocks": clk, "standalone_kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
             "parity": parity,
         }
-        print(json.dumps(line), flush=True)
     qm.close()
+    if not args.no_extra:
+        # the multi-GPU workloads at this rank count, in the same process
+        # group, after the headline model is freed: serving (64 sequences
+        # split over the ranks) and the 70B shape tensor parallel over them
+        xs, xw = min(args.steps, 3), 3
+        extra = {}
+        if SERVE_SEQS % world == 0:
+            extra["llama7b-serving"] = measure_serving(args, xs, xw)
+        if CFG70["kv_heads"] % world == 0:
+            extra["llama70b-tp"] = measure_70b_tp(args, xs, xw)
+        if rank == 0:
+            line["multi_gpu_workloads"] = extra
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
@@ -463,17 +483,14 @@ def step_bytes70(P):
     return L * (per_layer + 4 * scales + kv) + V * d * 4
 
 
-def run_70b_tp(args):
-    import datetime
-
+def measure_70b_tp(args, steps, warmup):
+    """The 70B tensor-parallel decode over every rank of the (already
+    initialised) process group; returns rank 0's JSON line (others: None)."""
     import torch
     import torch.distributed as dist
 
     rank, world, local = dist_env()
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     import tendo_b200 as tb
 
     comm = tb.Comm.from_process_group(local) if world > 1 else None
@@ -486,7 +503,7 @@ def run_70b_tp(args):
         qm.set_position(PROMPT70)
         qm.decode(NEW70, start_tokens=start)
 
-    for _ in range(max(args.warmup, 0)):
+    for _ in range(max(warmup, 0)):
         step()
     qm.sync()
 
@@ -501,7 +518,7 @@ def run_70b_tp(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
     qm.sync()
@@ -512,7 +529,7 @@ def run_70b_tp(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     toks = qm.tokens(NEW70 + 1)[:, 0]
-    tokens = args.steps * NEW70 * B70
+    tokens = steps * NEW70 * B70
     value = tokens / (ms / 1000.0)
     peaks = {}
     try:
@@ -521,13 +538,14 @@ def run_70b_tp(args):
     except OSError:
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    ms_tok = ms / (args.steps * NEW70)
+    ms_tok = ms / (steps * NEW70)
     byts = statistics.mean(step_bytes70(PROMPT70 + i) for i in range(NEW70))
     achieved = byts / (ms_tok / 1000.0) / 1e9
+    line = None
     if rank == 0:
         line = {
-            "metric": METRIC70, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "metric": METRIC70, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
             "config": {"workload": "llama70b-int8-tp-decode: 80 layers, d_model 8192, 64/8 heads x 128 (GQA), SwiGLU "
                                    "28672, vocab 32000; batch 16; decode from position 2048 (prompt KV zeros); "
@@ -540,12 +558,29 @@ def run_70b_tp(args):
             "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clk, "first_tokens": toks[:8].tolist(),
             "note": "no e2e or CPU leg for this workload: see the module docstring",
         }
-        print(json.dumps(line), flush=True)
     qm.close()
     if comm is not None:
         comm.close()
     if world > 1:
         dist.barrier()
+    return line
+
+
+def run_70b_tp(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    line = measure_70b_tp(args, args.steps, args.warmup)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 
@@ -568,20 +603,15 @@ def step_bytes_serve(P, seqs, kv_bytes=4):
     return w + kv
 
 
-def run_serving(args):
-    import datetime
-
+def measure_serving(args, steps, warmup):
+    """The 7B serving decode, 64 sequences split over the ranks of the
+    (already initialised) process group; returns rank 0's JSON line."""
     import torch
     import torch.distributed as dist
 
     rank, world, local = dist_env()
-    if SERVE_SEQS % world:
-        raise SystemExit(f"{SERVE_SEQS} sequences do not split over {world} replicas")
     B = SERVE_SEQS // world
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     import tendo_b200 as tb
 
     kv16 = bool(getattr(args, "kv_bf16", False))
@@ -594,7 +624,7 @@ def run_serving(args):
         qm.set_position(SERVE_PROMPT)
         qm.decode(SERVE_NEW, start_tokens=start)
 
-    for _ in range(max(args.warmup, 0)):
+    for _ in range(max(warmup, 0)):
         step()
     qm.sync()
 
@@ -609,7 +639,7 @@ def run_serving(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
     qm.sync()
@@ -619,7 +649,7 @@ def run_serving(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    value = SERVE_SEQS * SERVE_NEW * args.steps / (ms / 1000.0)
+    value = SERVE_SEQS * SERVE_NEW * steps / (ms / 1000.0)
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -627,14 +657,15 @@ def run_serving(args):
     except OSError:
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    ms_tok = ms / (args.steps * SERVE_NEW)
+    ms_tok = ms / (steps * SERVE_NEW)
     per_gpu = statistics.mean(step_bytes_serve(SERVE_PROMPT + i, B, 2 if kv16 else 4) for i in range(SERVE_NEW))
     achieved = per_gpu / (ms_tok / 1000.0) / 1e9
     toks = qm.tokens(SERVE_NEW + 1)[:, 0]
+    line = None
     if rank == 0:
         line = {
-            "metric": METRIC_SERVE, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "metric": METRIC_SERVE, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8/fp32, bf16 KV" if kv16 else "int8/fp32", "data": "synthetic",
             "config": {"workload": f"llama7b-int8-serving: 64 sequences as {world} replicas of {B}; decode from "
                                    "position 1024 (prompt KV zeros); 32 greedy tokens per step; KV 1280 positions"
@@ -649,10 +680,29 @@ def run_serving(args):
             "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clk, "first_tokens": toks[:8].tolist(),
             "note": "no e2e or CPU leg for this workload: see the module docstring",
         }
-        print(json.dumps(line), flush=True)
     qm.close()
     if world > 1:
         dist.barrier()
+    return line
+
+
+def run_serving(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if SERVE_SEQS % world:
+        raise SystemExit(f"{SERVE_SEQS} sequences do not split over {world} replicas")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    line = measure_serving(args, args.steps, args.warmup)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 
