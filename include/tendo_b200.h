@@ -80,17 +80,20 @@ TB_API tb_status_t tb_dequantize_i8_f32(float* w, const int8_t* q, const float* 
  * Replaces popcornDequantizeMatmul_i8f32 (cuda/popcorn.go:1306-1315, per
  * channel) and popcornDequantizeMatmulGrouped_i8f32 (cuda/popcorn.go:1353-1363,
  * group_size > 0), reached from cuda.Backend.DequantizeMatmul
- * (cuda/backend.go:676-721).  Both regimes run on the tcgen05 tensor cores:
- * each row of x is split into three int8 digit rows (x = s (d0 + d1/128 +
- * d2/128^2), s = max|x|/127) and every digit row times the raw int8 weights
- * is summed exactly in s32 (tcgen05.mma kind::i8), so the result is within
- * 2^-21 s sum|w| of the fp32 product.  M <= 32: the weights are the MMA's
- * 128-row operand and the (tile, K block) work is split evenly over the SMs
- * (K % 128 == 0; other K run the CUDA-core GEMV).  M > 32: 128 x 128 output
- * tiles.  Per-group scales (group_size > 0) take the same tcgen05 paths when
- * the group is a multiple of 128 (M > 32: at most 128 groups per row): the
- * exact s32 sum of each group is scaled by scale[n, group] and added in fp32
- * in a fixed order; other group sizes run the CUDA-core kernels.
+ * (cuda/backend.go:676-721).  Every tensor-core path splits each row of x
+ * into three int8 digit rows (x = s (d0 + d1/128 + d2/128^2), s = max|x|/127)
+ * and sums every digit row times the raw int8 weights exactly in s32, so the
+ * result is within 2^-21 s sum|w| of the fp32 product.  Routing:
+ *   M <= 5, per-channel scales, K % 64 == 0: one weight stream through a
+ *     shared-memory ring per SM, integer mma.sync (no workspace);
+ *   M <= 32 otherwise: tcgen05.mma kind::i8 with the weights as the 128-row
+ *     operand and the (tile, K block) work split evenly over the SMs
+ *     (K % 128 == 0; other K run the CUDA-core GEMV);
+ *   M > 32: tcgen05 128 x 128 output tiles.
+ * Per-group scales (group_size > 0) take the tcgen05 paths when the group is
+ * a multiple of 128 (M > 32: at most 128 groups per row): the exact s32 sum
+ * of each group is scaled by scale[n, group] and added in fp32 in a fixed
+ * order; other group sizes run the CUDA-core kernels.
  * Scratch: this entry point keeps library-owned buffers per device,
  * allocated on first use and grown on demand (calls that overlap in time on
  * one device must use tb_dequant_matmul_i8f32_ws). */

@@ -129,6 +129,10 @@ tb_status_t arena_get(int kind, size_t bytes, void** out) {
 tb_status_t dqmm(float* out, const float* x, const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
                  int64_t group_size, tb_gemm_mode_t mode, void* ws, size_t ws_bytes, bool arena, cudaStream_t st) {
   if (M <= 32) {
+    // up to 5 rows with per-channel scales: one weight stream through a
+    // shared-memory ring, no workspace
+    if (mode != TB_GEMM_SIMT && group_size == 0 && tb::gemv_ring_ok(x, q, M, N, K))
+      return tb::gemv_ring(out, x, q, scale, nullptr, (int)M, (int)N, (int)K, st);
     const size_t gneed = dqmm_workspace(M, N, K, group_size, mode);
     if (gneed > 0 && tb::gemv_tc_ok(q, M, N, K, group_size) && (uintptr_t)x % 16 == 0) {
       const size_t zb = tb::gemv_tc_zeroed_bytes(M, N, K), sb = tb::gemv_tc_scratch_bytes(M, N, K, group_size);

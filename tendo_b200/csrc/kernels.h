@@ -194,6 +194,12 @@ constexpr int kGemvTcMaxM = 64;
 size_t gemv_tc_zeroed_bytes(int64_t M, int64_t N, int64_t K);
 size_t gemv_tc_scratch_bytes(int64_t M, int64_t N, int64_t K, int64_t group = 0);
 bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group = 0);
+
+// gemv_ring.cu: the quantized Linear for 1 <= M <= 5 rows, per-channel scales,
+// K a multiple of 64, x and q 16-byte aligned; no workspace.
+bool gemv_ring_ok(const float* x, const int8_t* q, int64_t M, int64_t N, int64_t K);
+tb_status_t gemv_ring(float* out, const float* x, const int8_t* q, const float* scale, const float* resid, int M,
+                      int N, int K, cudaStream_t st);
 // norm_w != null: the product is of RMSNorm(x) * norm_w (the digit kernel applies it).
 // digits_ready: `scratch` already holds the digit rows of this x (and norm)
 // from the previous call with the same M and K (digit-kernel path only).
