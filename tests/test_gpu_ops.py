@@ -137,11 +137,31 @@ def test_dequant_matmul_float_coded_weights(oracle, be, cuda):
     assert rel_err(got, oracle.dequant_matmul(x, q, s, 0)) <= GEMV_TOL
 
 
-def test_matmul_nt_fp32(oracle, be, cuda):
+@pytest.mark.parametrize("K", [512, 500])
+def test_matmul_nt_fp32(oracle, be, cuda, K):
+    """K % 32 == 0 with aligned rows takes the staged fp32 kernel, K = 500 the
+    generic CUDA-core tiles."""
     rng = np.random.default_rng(4)
-    a = rng.standard_normal((3, 512)).astype(np.float32)
-    b = (rng.standard_normal((1000, 512)) * 0.02).astype(np.float32)
+    a = rng.standard_normal((3, K)).astype(np.float32)
+    b = (rng.standard_normal((1000, K)) * 0.02).astype(np.float32)
     assert rel_err(_np(be.MatMulNT(_t(a, cuda), _t(b, cuda))), oracle.matmul_nt(a, b)) <= 1e-5
+
+
+def test_matmul_nt_fp32_paths_agree_bitwise(be, cuda):
+    """The staged kernel and the generic tiles sum in the same order: an operand
+    4 bytes off a 16-byte boundary takes the generic path, with the same bits."""
+    import torch
+
+    rng = np.random.default_rng(14)
+    a = rng.standard_normal((5, 512)).astype(np.float32)
+    b = (rng.standard_normal((777, 512)) * 0.02).astype(np.float32)
+    fast = _np(be.MatMulNT(_t(a, cuda), _t(b, cuda)))
+    flat = torch.empty(a.size + 1, dtype=torch.float32, device=cuda)
+    a_off = flat[1:].view(5, 512)  # contiguous, base 4 bytes past a 16-byte boundary
+    a_off.copy_(_t(a, cuda))
+    assert a_off.data_ptr() % 16 != 0
+    slow = _np(be.MatMulNT(a_off, _t(b, cuda)))
+    np.testing.assert_array_equal(fast, slow)
 
 
 # --- glue ops -------------------------------------------------------------------
