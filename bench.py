@@ -199,6 +199,56 @@ def cpu_decode_sample(model_fill, budget_s, max_tokens=None):
     return n / dt, n, pyoracle.get_threads()
 
 
+def cpu_planned_workloads(rows_cap=256):
+    """The other CPU baseline workloads timed beside the headline, on all host
+    threads, with the oracle restatement of tendo's CPU path: the tiny config
+    end to end (prefill of its 128-token prompt, then 128 greedy decode steps),
+    and the quantized Linear (dequantize then the fp32 product) at K 4096 over
+    the decode/prefill grid.  Linear rows are independent, so M 2048 is timed
+    on its first rows_cap rows and reported per full call."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import pyoracle
+
+    pyoracle.build()
+    pyoracle.set_threads(os.cpu_count() or 1)
+    out = {"cores": pyoracle.get_threads(), "kind": "port"}
+    cfg = dict(pyoracle.TINY)
+    m = pyoracle.Model(cfg, 1, seed=0)
+    prompt = pyoracle.synth_tokens(1, 128, cfg["vocab"])
+    t0 = time.perf_counter()
+    _, last, _ = m.forward(prompt[None, :], want_logits=False)
+    t1 = time.perf_counter()
+    tok = np.array([int(np.argmax(last[0]))], np.int64)
+    for _ in range(128):
+        tok = m.decode_step(tok)
+    t2 = time.perf_counter()
+    m.close()
+    out["tiny_end_to_end"] = {"prefill_ms": (t1 - t0) * 1e3, "decode_ms_per_token": (t2 - t1) * 1e3 / 128,
+                              "workload": "8 layers, d_model 512, 8x64 MHA, SwiGLU 1408, vocab 32000; batch 1; "
+                                          "128-token prompt, 128 greedy tokens"}
+    rng = np.random.default_rng(42)
+    K = 4096
+    grid = []
+    for N in (4096, 11008):
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        _, q, sc = pyoracle.quantize(w, 0)
+        del w
+        for M in (1, 8, 32, 128, 2048):
+            rows = min(M, rows_cap)
+            x = rng.standard_normal((rows, K)).astype(np.float32)
+            reps = max(1, 8 // rows)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                pyoracle.dequant_matmul(x, q, sc, 0)
+            us = (time.perf_counter() - t0) / reps * 1e6 * (M / rows)
+            byts = linear_bytes(M, N, K)
+            grid.append({"M": M, "N": N, "K": K, "us": us, "GB_s": byts / (us * 1e-6) / 1e9,
+                         "GFLOP_s": 2.0 * M * N * K / (us * 1e-6) / 1e9, "rows_timed": rows})
+    out["linear_grid"] = grid
+    return out
+
+
 def fill_from_device(qm):
     def fill(m, po):
         for layer in range(CFG["layers"]):
@@ -415,6 +465,10 @@ def run_ours(args):
                "sample": f"{n} greedy decode tokens at positions 512.. of the same 7B workload, oracle restatement "
                          f"of tendo's CPU path on {threads} host threads (weights copied from the device)"}
 
+    cpu_more = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_more = cpu_planned_workloads()
+
     # the timed tokens against the oracle's golden stream of this workload
     # (tests/golden/llama7b_decode.json: same weights, prompt seed 0)
     parity = None
@@ -441,6 +495,8 @@ def run_ours(args):
             "clocks": clk, "standalone_kernels": kern, "phases_us": phases, "first_tokens": toks[:8].tolist(),
             "parity": parity,
         }
+        if cpu_more is not None:
+            line["cpu_workloads"] = cpu_more
     qm.close()
     if not args.no_extra:
         # the multi-GPU workloads at this rank count, in the same process
