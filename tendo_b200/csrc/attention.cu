@@ -12,13 +12,11 @@
 // kernel with the online softmax, so no [S, S] score matrix is stored.
 #include <math.h>
 
-
 #include "common.cuh"
 #include "kernels.h"
 
 namespace tb {
 namespace {
-
 
 template <int VEC>
 struct VecT;
@@ -47,6 +45,87 @@ __device__ __forceinline__ void load_vec(float (&r)[VEC], const float* p) {
     r[0] = t.x; r[1] = t.y;
   }
 }
+// One tile of U cached rows for G >= 32 / U query heads sharing them (the
+// online softmax of each head, the reference's scale after Q.K^T, rows at or
+// past `end` masked).  The G U partial dot products of a lane are summed over
+// the warp in one butterfly: each round a lane keeps half of its values and
+// adds the partner's copy of them, so after five rounds (NV = G U values,
+// 62 shuffles for 64) lane l holds the finished scores v = (l << log2(NV/32)) + i,
+// i.e. 32 / G consecutive lanes hold one head's U scores.  Those lanes find
+// the head's tile max and its exponentials once (not in every lane), and
+// the probabilities are then broadcast to every lane for P.V.
+template <int VEC, int G, int U>
+__device__ __forceinline__ void tile_grouped(const float (&qr)[G][VEC], const float (&kr)[U][VEC],
+                                             const float (&vr)[U][VEC], int64_t j0, int64_t end, float scale,
+                                             float (&mx)[G], float (&l)[G], float (&o)[G][VEC]) {
+  constexpr int NV = G * U;      // scores of the tile
+  constexpr int PL = NV / 32;    // finished scores per lane
+  constexpr int LG = 32 / G;     // lanes holding one head's scores
+  const int lane = threadIdx.x & 31;
+  float s[NV];
+#pragma unroll
+  for (int gi = 0; gi < G; gi++)
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < VEC; e++) d = fmaf(qr[gi][e], kr[u][e], d);
+      s[gi * U + u] = d;
+    }
+  // butterfly: offsets 16, 8, 4, 2, 1, halving the values a lane keeps
+#pragma unroll
+  for (int r = 0; r < 5; r++) {
+    const int off = 16 >> r;
+    const int half = NV >> (r + 1);
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; i++) {
+      const float keep = up ? s[i + half] : s[i];
+      const float send = up ? s[i] : s[i + half];
+      s[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  // this lane's scores: head gi = lane / LG, rows u0 .. u0 + PL - 1
+  const int gi_own = lane / LG, u0 = (lane % LG) * PL;
+  float tmax = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PL; i++) {
+    s[i] = (j0 + u0 + i < end) ? s[i] * scale : -INFINITY;
+    tmax = fmaxf(tmax, s[i]);
+  }
+#pragma unroll
+  for (int o2 = LG / 2; o2 > 0; o2 >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o2));
+  float mown = mx[0];
+#pragma unroll
+  for (int gi = 1; gi < G; gi++)
+    if (gi == gi_own) mown = mx[gi];
+  const float mn_own = fmaxf(mown, tmax);  // finite: position j0 < end is valid
+  float p[PL], psum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PL; i++) {
+    p[i] = expf(s[i] - mn_own);
+    psum += p[i];
+  }
+#pragma unroll
+  for (int o2 = LG / 2; o2 > 0; o2 >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o2);
+#pragma unroll
+  for (int gi = 0; gi < G; gi++) {
+    const float mn = __shfl_sync(0xffffffffu, mn_own, gi * LG);
+    const float ps = __shfl_sync(0xffffffffu, psum, gi * LG);
+    const float corr = expf(mx[gi] - mn);
+#pragma unroll
+    for (int e = 0; e < VEC; e++) o[gi][e] *= corr;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const float pu = __shfl_sync(0xffffffffu, p[u % PL], gi * LG + u / PL);
+#pragma unroll
+      for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(pu, vr[u][e], o[gi][e]);
+    }
+    l[gi] = l[gi] * corr + ps;
+    mx[gi] = mn;
+  }
+}
+
 // grid (nsplit, Hkv, B); VEC = D / 32 values per lane; G query heads per kv
 // head; W warps (8 when G >= 4: the G running softmaxes take registers, so
 // fewer CTAs fit per SM and each needs more rows in flight).  Each warp takes
@@ -109,40 +188,44 @@ __global__ void __launch_bounds__(W * 32) attn_decode_kernel(AttnDecodeArgs a) {
         for (int e = 0; e < VEC; e++) kr[u][e] = vr[u][e] = 0.f;
       }
     }
+    if constexpr (G * U >= 32) {
+      tile_grouped<VEC, G, U>(qr, kr, vr, j0, end, a.scale, mx, l, o);
+    } else {
 #pragma unroll
-    for (int gi = 0; gi < G; gi++) {
-      float s[U];
+      for (int gi = 0; gi < G; gi++) {
+        float s[U];
 #pragma unroll
-      for (int u = 0; u < U; u++) {
-        float d = 0.f;
+        for (int u = 0; u < U; u++) {
+          float d = 0.f;
 #pragma unroll
-        for (int e = 0; e < VEC; e++) d = fmaf(qr[gi][e], kr[u][e], d);
-        s[u] = d;
+          for (int e = 0; e < VEC; e++) d = fmaf(qr[gi][e], kr[u][e], d);
+          s[u] = d;
+        }
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+          for (int u = 0; u < U; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+          s[u] = (j0 + u < end) ? s[u] * a.scale : -INFINITY;
+          tmax = fmaxf(tmax, s[u]);
+        }
+        const float mn = fmaxf(mx[gi], tmax);  // finite: position j0 < end is valid
+        const float corr = expf(mx[gi] - mn);
+        float psum = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; e++) o[gi][e] *= corr;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+          const float p = expf(s[u] - mn);
+          psum += p;
+#pragma unroll
+          for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e]);
+        }
+        l[gi] = l[gi] * corr + psum;
+        mx[gi] = mn;
       }
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o2);
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        s[u] = (j0 + u < end) ? s[u] * a.scale : -INFINITY;
-        tmax = fmaxf(tmax, s[u]);
-      }
-      const float mn = fmaxf(mx[gi], tmax);  // finite: position j0 < end is valid
-      const float corr = expf(mx[gi] - mn);
-      float psum = 0.f;
-#pragma unroll
-      for (int e = 0; e < VEC; e++) o[gi][e] *= corr;
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const float p = expf(s[u] - mn);
-        psum += p;
-#pragma unroll
-        for (int e = 0; e < VEC; e++) o[gi][e] = fmaf(p, vr[u][e], o[gi][e]);
-      }
-      l[gi] = l[gi] * corr + psum;
-      mx[gi] = mn;
     }
   }
   // merge the warps of this CTA
