@@ -328,14 +328,22 @@ TB_API tb_status_t tb_sample_f32(int64_t* tokens, const float* logits, const flo
 /* A communicator over the ranks of one tensor-parallel group, one process (or
  * thread) per GPU: NCCL, loaded at run time (libnccl.so.2).  Rank 0 makes the
  * unique id, the caller distributes its bytes to every rank (any channel),
- * and each rank creates its communicator with it.  The tb_comm_init /
- * tb_allreduce_sum_f32 pair planned for the reference's cgo layer. */
+ * and each rank creates its communicator with it (collective: every rank
+ * calls it).  Creation also maps every rank's 4 MB peer-exchange region into
+ * every other rank (CUDA IPC; up to 8 ranks on one node); allreduces of up to
+ * 4 MB then run as one kernel over peer memory, larger ones through NCCL.  If
+ * any rank cannot map a peer, or TENDO_B200_ALLREDUCE=nccl is set, every
+ * rank uses NCCL throughout.  The tb_comm_init / tb_allreduce_sum_f32 pair
+ * planned for the reference's cgo layer. */
 typedef struct tb_comm tb_comm;
 TB_API size_t tb_comm_unique_id_bytes(void);
 TB_API tb_status_t tb_comm_unique_id(void* id_out, size_t bytes);
 TB_API tb_status_t tb_comm_create(tb_comm** out, const void* id, size_t bytes, int rank, int nranks, int device);
 TB_API tb_status_t tb_comm_destroy(tb_comm* comm);
-/* In-place sum over the ranks on `stream` (ncclAllReduce, fp32). */
+/* 1 when the communicator's allreduces run over peer memory, 0 when NCCL. */
+TB_API int tb_comm_peer_active(const tb_comm* comm);
+/* In-place fp32 sum over the ranks on `stream`.  Every rank gets the same
+ * bits: the peer kernel adds the ranks' values in rank order. */
 TB_API tb_status_t tb_allreduce_sum_f32(tb_comm* comm, float* buf, int64_t n, tb_stream_t stream);
 
 /* The model's share on rank r of a tensor-parallel group of `nranks` GPUs

@@ -89,6 +89,7 @@ SIGNATURES = [
     ("tb_comm_create", _st, [_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ("tb_comm_destroy", _st, [_vp]),
     ("tb_allreduce_sum_f32", _st, [_vp, _vp, _i64, _vp]),
+    ("tb_comm_peer_active", ctypes.c_int, [_vp]),
     ("tb_model_destroy", _st, [_vp]),
     ("tb_model_init_synthetic", _st, [_vp, ctypes.c_uint64]),
     ("tb_model_set_linear", _st, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
@@ -580,7 +581,7 @@ class ModelConfig(ctypes.Structure):
 
 
 class Comm:
-    """A tensor-parallel communicator (tb_comm_*: NCCL), one per rank.
+    """A tensor-parallel communicator (tb_comm_*: peer memory, NCCL), one per rank.
 
     ``Comm.from_process_group(device)`` builds it over an initialised
     torch.distributed group: rank 0 makes the unique id and the group
@@ -608,6 +609,11 @@ class Comm:
         obj = [cls.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         return cls(obj[0], rank, world, device)
+
+    @property
+    def peer(self) -> bool:
+        """True when allreduces run over peer memory (tb_comm_peer_active)."""
+        return bool(lib.tb_comm_peer_active(self.h))
 
     def allreduce_sum(self, t, stream=None):
         """In-place fp32 sum over the ranks (tb_allreduce_sum_f32)."""

@@ -206,16 +206,16 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     const float* resid = m->tp_rank == 0 ? m->h : nullptr;
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, 0, (tb_stream_t)st));
-      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st, m->err_word));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
       const int HD = (int)(m->H * m->D);
       TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->attn, (int)rows, HD, kTcPlanes, nullptr, 0.f, st));
       TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wo, so, resid, (int)rows, (int)m->d, HD, kTcPlanes, st));
-      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st, m->err_word));
     } else {
       TB_TRY(tb::gemm_simt_i8(m->h, m->attn, wo, so, resid, (int)rows, (int)m->d, (int)(m->H * m->D), 0, st));
-      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st, m->err_word));
     }
     // MLP block (models/llama/quantized.go:206-219, :385-417)
     if (tc) {
@@ -231,15 +231,15 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     TB_TRY(tb::silu_mul(m->g, m->g, m->u, rows * m->F, st));
     if (rows <= 32) {
       TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, 0, (tb_stream_t)st));
-      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st, m->err_word));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
       TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->g, (int)rows, (int)m->F, kTcPlanes, nullptr, 0.f, st));
       TB_TRY(tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wd, sd, resid, (int)rows, (int)m->d, (int)m->F, kTcPlanes, st));
-      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st, m->err_word));
     } else {
       TB_TRY(tb::gemm_simt_i8(m->h, m->g, wd, sd, resid, (int)rows, (int)m->d, (int)m->F, 0, st));
-      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st));
+      TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(rows * m->d), false, st, m->err_word));
     }
   }
   return TB_SUCCESS;
@@ -274,7 +274,7 @@ tb_status_t finish_logits(tb_model* m, int64_t S) {
     TB_TRY(tb::gemm_f32_nt(m->logits, m->xn, m->lm_head, (int)m->B, (int)m->V, (int)m->d, st));
     TB_TRY(tb::argmax_keys(m->keys, m->logits, m->B, m->V, m->v0, st));
   }
-  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, st));
+  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, st, m->err_word));
   int64_t p = m->host_pos - 1;
   TB_CUDA(cudaMemcpyAsync(m->pos, &p, sizeof(int64_t), cudaMemcpyHostToDevice, st));
   TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, st, false));
@@ -481,10 +481,11 @@ tb_status_t decode_step_fused(tb_model* m) {
     for (int kind = 0; kind < 5; kind++) {
       TB_TRY(decode_kernel(m, kind, l, pdl));
       // tensor parallelism: sum the row-parallel o / down partial products
-      if (kind == 2 || kind == 4) TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(m->B * m->d), false, m->stream));
+      if (kind == 2 || kind == 4)
+        TB_TRY(tb::allreduce(m->comm, m->h, (size_t)(m->B * m->d), false, m->stream, m->err_word));
     }
   TB_TRY(decode_kernel(m, 5, 0, pdl));
-  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, m->stream));
+  TB_TRY(tb::allreduce(m->comm, m->keys, (size_t)m->B, true, m->stream, m->err_word));
   TB_TRY(tb::finish_step(m->keys, m->tokens, m->history, m->step, m->pos, (int)m->B, m->hist_cap, m->stream, pdl));
   return TB_SUCCESS;
 }
@@ -1044,6 +1045,7 @@ extern "C" tb_status_t tb_model_tokens(tb_model* m, int64_t* out_host, int64_t c
 static tb_status_t check_waits(tb_model* m) {
   int v = 0, zero = 0;
   TB_CUDA(cudaMemcpy(&v, m->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (tb::take_wait_timeouts() > 0) v = 1;  // the per-op kernels' bounded waits
   if (v) {
     TB_CUDA(cudaMemcpy(m->err_word, &zero, sizeof(int), cudaMemcpyHostToDevice));
     return TB_ERROR_TIMEOUT;

@@ -209,7 +209,11 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
 
 // comm.cu: in-place NCCL allreduce on `st` (fp32 sum, or uint64 max for the
 // packed greedy keys); a no-op without a communicator or with one rank.
-tb_status_t allreduce(tb_comm* c, void* buf, size_t count, bool u64_max, cudaStream_t st);
+// In-place sum (fp32) or max (uint64) over the communicator's ranks: the
+// peer-memory kernel up to the exchange capacity, NCCL past it.  Expired
+// device waits count in *err (the global wait-timeout word when null).
+tb_status_t allreduce(tb_comm* c, void* buf, size_t count, bool u64_max, cudaStream_t st, int* err = nullptr);
+bool peer_allreduce_active(const tb_comm* c);
 int comm_rank(const tb_comm* c);
 int comm_size(const tb_comm* c);
 

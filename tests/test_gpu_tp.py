@@ -65,3 +65,29 @@ def test_tp2_loads_its_shard_of_a_checkpoint(oracle, tb, cuda, tmp_path):
     mp.start_processes(tp_worker.run, args=(2, _free_port(), cfg, batch, 5, prompt, 24, out, path), nprocs=2,
                        join=True, start_method="spawn")
     np.testing.assert_array_equal(np.load(out), want)
+
+
+def test_tp2_peer_allreduce(tb, cuda, tmp_path):
+    """The allreduce kernel over peer memory: exact on integer values, within
+    fp32 rounding of the float64 sum on random values, the same bits on both
+    ranks, across ragged sizes, both parities and the NCCL path past 4 MB."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    import tp_worker
+
+    out = str(tmp_path / "ar.npy")
+    mp.start_processes(tp_worker.run_allreduce, args=(2, _free_port(), out), nprocs=2, join=True,
+                       start_method="spawn")
+    r0, r1 = np.load(out, allow_pickle=True)
+    assert r0["peer"] and r1["peer"]
+    for k in r0:
+        if k == "peer" or k.endswith("want"):
+            continue
+        np.testing.assert_array_equal(r0[k], r1[k])  # identical bits on every rank
+        if k.endswith("_int"):
+            np.testing.assert_array_equal(r0[k], r0[k[:-4] + "_intwant"])
+        else:
+            np.testing.assert_allclose(r0[k], r0[k[:-5] + "_want"], rtol=1e-6, atol=1e-6)
