@@ -186,8 +186,8 @@ __device__ __forceinline__ Stream stream_of(const MkArgs& a, int p, const AttnSp
     s.ntiles = a.d / 8;
     s.kind = kKindPlain;
   } else if (k == 3) {
-    s.base = a.wg + (size_t)l * a.F * a.d;
-    s.base2 = a.wu + (size_t)l * a.F * a.d;
+    s.base = a.wg + (size_t)l * 2 * a.F * a.d;  // a layer's gate rows, then its up rows
+    s.base2 = a.wu + (size_t)l * 2 * a.F * a.d;
     s.row_bytes = a.d;
     s.ntiles = a.F / 4;
     s.kind = kKindGateUp;
@@ -456,7 +456,7 @@ __device__ __forceinline__ void prefetch_scales(float* ssc, const MkArgs& a, int
       const int per = a.D / 8, head = tile / per, i0 = (tile % per) * 4;
       src = a.sqkv + (size_t)l * (a.H + 2 * a.Hkv) * a.D + head * a.D + i0 + hf * (a.D / 2);
     } else if (kind == 2) {  // gate rows 4 t.., up rows 4 t..
-      src = (hf ? a.su : a.sg) + (size_t)l * a.F + tile * 4;
+      src = (hf ? a.su : a.sg) + (size_t)l * 2 * a.F + tile * 4;
     } else {  // o (1) / down (3): rows 8 t .. 8 t + 7
       src = (kind == 1 ? a.so : a.sd) + (size_t)l * a.d + tile * 8 + hf * 4;
     }

@@ -40,6 +40,7 @@ struct tb_model {
   void *kc = nullptr, *vc = nullptr;  // fp32, or bf16 with kv16
   bool kv16 = false;                   // bf16 KV cache (TB_MODEL_KV_BF16)
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *u = nullptr;
+  float* gu = nullptr;  // decode: [B, 2F] gate and up products of one launch
   float *qbuf = nullptr, *partial = nullptr, *logits = nullptr, *last = nullptr;
   unsigned long long* keys = nullptr;
   int64_t *tokens = nullptr, *ids = nullptr, *history = nullptr, *pos = nullptr, *step = nullptr;
@@ -125,8 +126,9 @@ void lin_ptr(tb_model* m, int layer, int mat, int8_t** q, float** s) {
       *s = m->sqkv + (size_t)layer * m->NQKV + hq + hkv;
       break;
     case 3: *q = m->wo + (size_t)layer * m->d * hq; *s = m->so + (size_t)layer * m->d; break;
-    case 4: *q = m->wgate + (size_t)layer * m->F * m->d; *s = m->sgate + (size_t)layer * m->F; break;
-    case 5: *q = m->wup + (size_t)layer * m->F * m->d; *s = m->sup + (size_t)layer * m->F; break;
+    // gate and up rows of a layer are adjacent (one [2F, d] matrix, gate first)
+    case 4: *q = m->wgate + (size_t)layer * 2 * m->F * m->d; *s = m->sgate + (size_t)layer * 2 * m->F; break;
+    case 5: *q = m->wup + (size_t)layer * 2 * m->F * m->d; *s = m->sup + (size_t)layer * 2 * m->F; break;
     default: *q = m->wdown + (size_t)layer * m->d * m->F; *s = m->sdown + (size_t)layer * m->d; break;
   }
 }
@@ -351,10 +353,10 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
         return tb::gemm_tc_run(m->h, m->tcdig, m->tcs, wo, so, resid, B, d, HD, kTcPlanes, st);
       }
       if (kind == 3) {
+        // gate and up rows are one [2F, d] matrix: one GEMM, then SwiGLU
         TB_TRY(tb::gemm_tc_digits(m->tcdig, m->tcs, m->h, B, d, kTcPlanes, m->mlp_norm + l * m->d, m->c.eps, st));
-        TB_TRY(tb::gemm_tc_run(m->g, m->tcdig, m->tcs, wg, sg, nullptr, B, F, d, kTcPlanes, st));
-        TB_TRY(tb::gemm_tc_run(m->u, m->tcdig, m->tcs, wu, su, nullptr, B, F, d, kTcPlanes, st));
-        return tb::silu_mul(m->g, m->g, m->u, m->B * m->F, st);
+        TB_TRY(tb::gemm_tc_run(m->gu, m->tcdig, m->tcs, wg, sg, nullptr, B, 2 * F, d, kTcPlanes, st));
+        return tb::silu_mul_rows(m->g, m->gu, m->B, m->F, st);
       }
     }
     if (m->gv && kind != 1) {
@@ -370,12 +372,10 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
       }
       if (kind == 2) return tb::gemv_tc(m->h, m->attn, wo, so, resid, B, d, HD, m->gv_zero, false, m->gv_scratch, st);
       if (kind == 3) {
-        TB_TRY(tb::gemv_tc(m->g, m->h, wg, sg, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
+        // gate and up rows are one [2F, d] matrix: one GEMV launch, then SwiGLU
+        TB_TRY(tb::gemv_tc(m->gu, m->h, wg, sg, nullptr, B, 2 * F, d, m->gv_zero, false, m->gv_scratch, st,
                            m->mlp_norm + l * m->d, m->c.eps));
-        // the same normed x: the gate call's digit rows serve the up projection
-        TB_TRY(tb::gemv_tc(m->u, m->h, wu, su, nullptr, B, F, d, m->gv_zero, false, m->gv_scratch, st,
-                           m->mlp_norm + l * m->d, m->c.eps, 0, true));
-        return tb::silu_mul(m->g, m->g, m->u, m->B * m->F, st);
+        return tb::silu_mul_rows(m->g, m->gu, m->B, m->F, st);
       }
       if (kind == 4) return tb::gemv_tc(m->h, m->g, wd, sd, resid, B, d, F, m->gv_zero, false, m->gv_scratch, st);
     }
@@ -611,7 +611,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     // (a bf16 cache takes this path at batch 1 too: its RoPE / append kernel
     // writes either cache type)
     m->gv = (m->B > 1 || m->kv16) && m->B <= tb::kGemvTcMaxM && tb::gemv_tc_ok(al, m->B, m->NQKV, m->d) &&
-            tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, m->F, m->d) &&
+            tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, 2 * m->F, m->d) &&
             tb::gemv_tc_ok(al, m->B, m->d, m->F);
   }
   // the captured decode step: the attention kernel's head shapes, and either
@@ -645,10 +645,14 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->sqkv, L * m->NQKV));
   A(dalloc(m, &m->wo, L * m->d * m->H * m->D));
   A(dalloc(m, &m->so, L * m->d));
-  A(dalloc(m, &m->wgate, L * m->F * m->d));
-  A(dalloc(m, &m->sgate, L * m->F));
-  A(dalloc(m, &m->wup, L * m->F * m->d));
-  A(dalloc(m, &m->sup, L * m->F));
+  // per layer the gate rows, then the up rows: one [2F, d] matrix, so a
+  // single GEMV launch computes both
+  A(dalloc(m, &m->wgate, L * 2 * m->F * m->d));
+  A(dalloc(m, &m->sgate, L * 2 * m->F));
+  if (s == TB_SUCCESS) {
+    m->wup = m->wgate + m->F * m->d;
+    m->sup = m->sgate + m->F;
+  }
   A(dalloc(m, &m->wdown, L * m->d * m->F));
   A(dalloc(m, &m->sdown, L * m->d));
   A(dalloc(m, &m->attn_norm, L * m->d));
@@ -674,6 +678,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   const size_t gw = R * (m->F > m->H * m->D ? m->F : m->H * m->D);
   A(dalloc(m, &m->g, gw));
   A(dalloc(m, &m->u, R * m->F));
+  if (m->gv) A(dalloc(m, &m->gu, (size_t)m->B * 2 * m->F));
   A(dalloc(m, &m->qbuf, (size_t)m->B * m->H * m->D));
   {
     // split partials of the decode attention: the per-step kernels' layout
@@ -702,7 +707,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   A(dalloc(m, &m->samp_u, (size_t)m->B));
   if (m->gv) {
     int64_t nmax = m->NQKV > m->d ? m->NQKV : m->d;
-    if (m->F > nmax) nmax = m->F;
+    if (2 * m->F > nmax) nmax = 2 * m->F;
     int64_t kmax = m->d > m->H * m->D ? m->d : m->H * m->D;
     if (m->F > kmax) kmax = m->F;
     unsigned char* z = nullptr;

@@ -20,12 +20,10 @@
 //
 // Warps: 0 = TMA producer, 1 = MMA issuer (4 x tcgen05.mma per 128-byte K
 // block into one of two TMEM accumulators), 2..5 = epilogue (one weight row
-// per thread: its TMEM lane).  For M <= 8 (kGvInlineM) four more warps turn
-// x into the digit tiles of each stage directly in shared memory (row maxima
-// first, then 128 columns per stage), so one kernel does the whole product;
-// for larger M a digit kernel writes the digit rows and the producer loads
-// them with TMA.  The producer starts the weight stream before the
-// programmatic-launch wait: weights never depend on the preceding kernel.
+// per thread: its TMEM lane).  A digit kernel writes the digit rows (with the
+// RMSNorm when the caller fuses one) and the producer loads them with TMA.
+// The producer starts the weight stream before the programmatic-launch wait:
+// weights never depend on the preceding kernel.
 #include <string.h>
 
 #include <mutex>
@@ -42,11 +40,9 @@ constexpr int kGvRows = 128;               // weight rows per tile (MMA M)
 constexpr int kGvSub = 128;                // K bytes of one 128-byte-swizzled sub-tile
 constexpr int kGvWSub = kGvRows * kGvSub;  // 16 KB: 128 weight rows x 128 bytes
 constexpr int kGvTmemCols = 512;           // two accumulators of up to 256 columns (ND <= 192)
-constexpr int kGvInlineM = 8;              // M up to which the kernel makes its own digits
 
 struct GvArgs {
   float* out;
-  const float* x;       // inline digits: the activations
   const float* srow;    // TMA digits: row scales written by the digit kernel
   const float* scale;
   const float* resid;
@@ -67,12 +63,6 @@ __device__ __forceinline__ int range_begin(long long b, long long total, long lo
 }
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
-__device__ __forceinline__ void cvt_sync() { asm volatile("bar.sync 3, 128;" ::: "memory"); }
-
-// byte offset of (row r, byte c) in a K-major tile with the 128-byte swizzle
-__device__ __forceinline__ int sw128_offset(int r, int c) {
-  return (r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 4) ^ (r & 7)) << 4) | (c & 15));
-}
 
 // GKB 128-byte K sub-tiles per stage (one 3-D TMA box of 128 rows x GKB x 128
 // bytes for the weights: longer runs per row, fewer copies).
@@ -84,8 +74,8 @@ __device__ __forceinline__ int sw128_offset(int r, int c) {
 // into fp32 rows in shared memory.  A split tile's fp32 partial rows go to the
 // CTA's own workspace slots; the last CTA to count in adds them in CTA order,
 // so the sum does not depend on arrival order.
-template <bool INL, int GKB, bool GRP>
-__global__ void __launch_bounds__(INL ? 320 : 192, 1)
+template <int GKB, bool GRP>
+__global__ void __launch_bounds__(192, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GvArgs a) {
   constexpr int kGvBK = kGvSub * GKB;     // K bytes per stage
   constexpr int kGvWTile = kGvWSub * GKB;  // weight bytes per stage
@@ -97,11 +87,8 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
-  uint64_t* sready = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sready + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* srow_s = reinterpret_cast<float*>(tmem_slot + 2);  // [kGvInlineM]
-  float* cred = srow_s + kGvInlineM;                         // [4][kGvInlineM]
   float* accs = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes + 512);  // GRP: [ND][128]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long T = a.total, G = gridDim.x;
@@ -110,17 +97,16 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
-      mbarrier_init(&full[s], INL ? 2 : 1);  // + the arrival of the converter warp of the stage
+      mbarrier_init(&full[s], 1);
       mbarrier_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbarrier_init(&tfull[b], 1);
       mbarrier_init(&tempty[b], 4);  // one arrival per epilogue warp
     }
-    mbarrier_init(sready, 4);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-    if (!INL) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
   }
   if (warp == 0) tmem_alloc(tmem_slot, kGvTmemCols);
   tc_fence_before();
@@ -137,10 +123,10 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
       const int pre = n < S ? n : S;
       for (int i = 0; i < pre; i++) {
         const int it = b0 + i;
-        mbarrier_expect_tx(&full[i], (uint32_t)(INL ? kGvWTile : stage_bytes));
+        mbarrier_expect_tx(&full[i], (uint32_t)stage_bytes);
         tma_load_3d(smem + (size_t)i * stage_bytes, &tmW, 0, (it / KB) * kGvRows, (it % KB) * GKB, &full[i]);
       }
-      if (!INL) {
+      {
         pdl_wait();
         for (int i = 0; i < pre; i++)
           for (int g = 0; g < GKB; g++)
@@ -152,10 +138,9 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
         const int it = b0 + i, kb = it % KB;
         mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), a.err);
         unsigned char* st = smem + (size_t)s * stage_bytes;
-        mbarrier_expect_tx(&full[s], (uint32_t)(INL ? kGvWTile : stage_bytes));
+        mbarrier_expect_tx(&full[s], (uint32_t)stage_bytes);
         tma_load_3d(st, &tmW, 0, (it / KB) * kGvRows, kb * GKB, &full[s]);
-        if (!INL)
-          for (int g = 0; g < GKB; g++)
+        for (int g = 0; g < GKB; g++)
             tma_load_2d(st + kGvWTile + g * ND * kGvSub, &tmX, kb * kGvBK + g * kGvSub, 0, &full[s]);
       }
     }
@@ -229,8 +214,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
     // epilogue: thread = weight row (tile row 32 q + lane = its TMEM lane)
     const int q = warp & 3;
     const int rowt = q * 32 + lane;
-    if (INL) mbarrier_wait(sready, 0u, a.err);
-    const float* srow = INL ? srow_s : a.srow;
+    const float* srow = a.srow;
     if (GRP) {
       // fp32 sums per accumulator column (digit row p M + m) of this thread's
       // weight row; distinct columns, so a 16-column chunk is read, updated
@@ -249,7 +233,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 #pragma unroll
         for (int mm = 0; mm < 8; mm++) {
           const int m = m0 + mm < M ? m0 + mm : M - 1;
-          sr[mm] = INL ? srow[m] : __ldcg(srow + m);
+          sr[mm] = __ldcg(srow + m);
           rs[mm] = a.resid ? __ldcg(a.resid + (size_t)m * a.N + n) : 0.f;
         }
 #pragma unroll
@@ -368,7 +352,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
           pin1(c1);
           pin1(c2);
           if (live) {
-            const float y = (INL ? srow[m] : __ldcg(srow + m)) *
+            const float y = (__ldcg(srow + m)) *
                             ((float)(int)c0 + (float)(int)c1 * (1.0f / 128.0f) + (float)(int)c2 * (1.0f / 16384.0f));
             float o = y * sc;
             if (a.resid) o += __ldcg(a.resid + (size_t)m * a.N + n);
@@ -423,7 +407,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 #pragma unroll
             for (int mm = 0; mm < 8; mm++) {
               const int m = m0 + mm < M ? m0 + mm : M - 1;
-              sr[mm] = INL ? srow[m] : __ldcg(srow + m);
+              sr[mm] = __ldcg(srow + m);
               rs[mm] = (a.resid && live) ? __ldcg(a.resid + (size_t)m * a.N + n) : 0.f;
             }
 #pragma unroll
@@ -445,122 +429,6 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
       it = seg_end;
     }
     }
-  } else if (INL) {
-    // converters (warps 6..9): row scales, then the digit tiles; four stages
-    // are converted at once, one per warp (lane = 4-column group)
-    const int ct = threadIdx.x - 192;  // 0..127
-    const int cw = ct >> 5;
-    {
-      // zero every stage's digit tile once: rows >= 3M stay zero
-      const int xbytes = ND * kGvBK;  // GKB sub-tiles of ND rows x 128 bytes
-      for (int off = ct * 16; off < S * xbytes; off += 128 * 16)
-        *reinterpret_cast<uint4*>(smem + (size_t)(off / xbytes) * stage_bytes + kGvWTile + off % xbytes) =
-            make_uint4(0u, 0u, 0u, 0u);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    pdl_wait();  // x may come from the preceding kernel
-    const int nv = a.K >> 2;
-    float mx[kGvInlineM];
-#pragma unroll
-    for (int m = 0; m < kGvInlineM; m++) mx[m] = 0.f;
-    for (int m = 0; m < M; m++) {
-      const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)m * a.K);
-      float am = 0.f;
-      for (int v0 = ct; v0 < nv; v0 += 128 * 8) {
-        float4 t[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          t[u] = (v0 + u * 128 < nv) ? __ldcg(xr + v0 + u * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          am = fmaxf(am, fmaxf(fmaxf(fabsf(t[u].x), fabsf(t[u].y)), fmaxf(fabsf(t[u].z), fabsf(t[u].w))));
-      }
-#pragma unroll
-      for (int mm = 0; mm < kGvInlineM; mm++)
-        if (mm == m) mx[mm] = am;
-    }
-#pragma unroll
-    for (int m = 0; m < kGvInlineM; m++) {
-      const float w = warp_max(mx[m]);
-      if (lane == 0) cred[cw * kGvInlineM + m] = w;
-    }
-    cvt_sync();  // also orders every converter's zeroing before any tile is released
-    float inv[kGvInlineM];
-#pragma unroll
-    for (int m = 0; m < kGvInlineM; m++) {
-      float am = 0.f;
-#pragma unroll
-      for (int w = 0; w < 4; w++) am = fmaxf(am, cred[w * kGvInlineM + m]);
-      const float sc = (am > 0.f && isfinite(am)) ? am / 127.0f : 1.0f;
-      inv[m] = 1.0f / sc;
-      if (ct == 0 && m < M) srow_s[m] = sc;
-    }
-    __syncwarp();
-    if (lane == 0) mbarrier_arrive(sready);
-    const int n = b1 - b0;
-    // Warp cw owns the stage slots s = cw (mod 4), so the uses of a slot are
-    // made in order by one warp and each wait on a slot's `empty` barrier is
-    // for the phase right after the last one this warp saw complete (a wait
-    // two phases ahead would alias on the parity).  Its stages are taken two
-    // at a time: all x loads first, then the tiles.
-    int i = -1;
-    auto next_mine = [&](int from) {
-      for (int j = from; j < n; j++)
-        if ((j % S) % 4 == cw) return j;
-      return n;
-    };
-    i = next_mine(0);
-    while (i < n) {
-      const int i2 = next_mine(i + 1);
-      const int ii_[2] = {i, i2};
-      float4 xv[2][kGvInlineM][GKB];
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int ii = ii_[h];
-        const int kb = (b0 + ii) % KB;
-#pragma unroll
-        for (int m = 0; m < kGvInlineM; m++)
-          for (int g = 0; g < GKB; g++)
-            xv[h][m][g] = (ii < n && m < M)
-                              ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.K + kb * kGvBK + g * kGvSub) + lane)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int ii = ii_[h];
-        if (ii >= n) break;
-        const int s = ii % S, use = ii / S;
-        if (use > 0) mbarrier_wait(&empty[s], (uint32_t)((use - 1) & 1), a.err);
-        unsigned char* xt = smem + (size_t)s * stage_bytes + kGvWTile;
-#pragma unroll
-        for (int m = 0; m < kGvInlineM; m++) {
-          if (m >= M) break;
-          for (int g = 0; g < GKB; g++) {
-          const float vals[4] = {xv[h][m][g].x, xv[h][m][g].y, xv[h][m][g].z, xv[h][m][g].w};
-          uint32_t pk[3] = {0u, 0u, 0u};
-#pragma unroll
-          for (int t = 0; t < 4; t++) {
-            const float u = fminf(fmaxf(vals[t] * inv[m], -127.0f), 127.0f);
-            const float e0 = rintf(u);
-            const float r1 = (u - e0) * 128.0f;
-            const float e1 = rintf(r1);
-            const float e2 = rintf((r1 - e1) * 128.0f);
-            pk[0] |= ((uint32_t)__float2int_rn(e0) & 0xffu) << (8 * t);
-            pk[1] |= ((uint32_t)__float2int_rn(e1) & 0xffu) << (8 * t);
-            pk[2] |= ((uint32_t)__float2int_rn(e2) & 0xffu) << (8 * t);
-          }
-#pragma unroll
-          for (int p = 0; p < 3; p++)
-            *reinterpret_cast<uint32_t*>(xt + g * ND * kGvSub + sw128_offset(p * M + m, 4 * lane)) = pk[p];
-          }
-        }
-        // the tensor core reads the tile through the async proxy
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbarrier_arrive(&full[s]);
-      }
-      i = i2 < n ? next_mine(i2 + 1) : n;
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -569,7 +437,7 @@ __global__ void __launch_bounds__(INL ? 320 : 192, 1)
 
 // Workspace: a zero-maintained part (per-tile counters and split-tile sums:
 // zero before a launch, zero again after it) and a scratch part for the
-// digit rows and row scales (unused when the kernel makes its own digits).
+// digit rows and row scales.
 struct GvLayout {
   size_t count, acc, zeroed, dig, srow, part, scratch;
 };
@@ -590,12 +458,12 @@ GvLayout gv_layout(int64_t M, int64_t N, int64_t K, int64_t group = 0) {
   return L;
 }
 
-template <bool INL, int GKB, bool GRP>
+template <int GKB, bool GRP>
 tb_status_t set_gv_smem() {
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
-    err = cudaFuncSetAttribute(gemv_tc_kernel<INL, GKB, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    err = cudaFuncSetAttribute(gemv_tc_kernel<GKB, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(gemv_tc)");
   return TB_SUCCESS;
@@ -615,20 +483,14 @@ bool gemv_tc_ok(const void* q, int64_t M, int64_t N, int64_t K, int64_t group) {
 
 namespace {
 template <bool GRP>
-tb_status_t launch_gv(const cudaLaunchConfig_t& cfg, bool inl, int G, const CUtensorMap& tw, const CUtensorMap& tx,
+tb_status_t launch_gv(const cudaLaunchConfig_t& cfg, int G, const CUtensorMap& tw, const CUtensorMap& tx,
                       const GvArgs& a) {
-  if (inl && G == 2) {
-    TB_TRY((set_gv_smem<true, 2, GRP>()));
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 2, GRP>, tw, tx, a));
-  } else if (inl) {
-    TB_TRY((set_gv_smem<true, 1, GRP>()));
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<true, 1, GRP>, tw, tx, a));
-  } else if (G == 2) {
-    TB_TRY((set_gv_smem<false, 2, GRP>()));
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 2, GRP>, tw, tx, a));
+  if (G == 2) {
+    TB_TRY((set_gv_smem<2, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<2, GRP>, tw, tx, a));
   } else {
-    TB_TRY((set_gv_smem<false, 1, GRP>()));
-    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<false, 1, GRP>, tw, tx, a));
+    TB_TRY((set_gv_smem<1, GRP>()));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<1, GRP>, tw, tx, a));
   }
   return TB_SUCCESS;
 }
@@ -640,9 +502,9 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   const GvLayout L = gv_layout(M, N, K, group);
   unsigned char* z = static_cast<unsigned char*>(zeroed);
   unsigned char* w = static_cast<unsigned char*>(scratch);
-  // digit tiles made in the kernel for small M without a norm; otherwise the
-  // digit kernel (which also applies the RMSNorm) writes them for TMA
-  const bool inl = M <= kGvInlineM && !norm_w;
+  // the digit kernel (which also applies the RMSNorm) writes the digit rows
+  // for TMA: measured faster at every M than converter warps inside this
+  // kernel (M = 8, N = 28672, K = 8192: 49.0 against 88.3 us)
   const int ND = ((3 * M + 15) / 16) * 16;
   const int acc_bytes = group > 0 ? ND * kGvRows * 4 : 0;  // per-group: fp32 column sums
   // two 128-byte sub-tiles per stage where K allows (halves the copies and
@@ -661,7 +523,6 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   int stages = (200 * 1024 - acc_bytes) / stage_bytes;  // as many weight boxes in flight as fit
   if (stages > 16) stages = 16;
   const size_t smem = (size_t)stages * stage_bytes + 1024 + 512 + acc_bytes;
-  if (inl && (uintptr_t)x % 16 != 0) return TB_ERROR_NOT_SUPPORTED;
 
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return TB_ERROR_NOT_SUPPORTED;
@@ -677,10 +538,10 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return TB_ERROR_NOT_SUPPORTED;
   }
-  int8_t* dig = inl ? nullptr : reinterpret_cast<int8_t*>(w + L.dig);
-  float* srow = inl ? nullptr : reinterpret_cast<float*>(w + L.srow);
+  int8_t* dig = reinterpret_cast<int8_t*>(w + L.dig);
+  float* srow = reinterpret_cast<float*>(w + L.srow);
   if (zero_first) TB_CUDA(cudaMemsetAsync(z, 0, L.zeroed, st));
-  if (!inl) {
+  {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(3 * M)};
     const cuuint64_t strides[1] = {(cuuint64_t)K};
     const cuuint32_t box[2] = {kGvSub, (cuuint32_t)ND};
@@ -694,7 +555,6 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
 
   GvArgs a{};
   a.out = out;
-  a.x = x;
   a.srow = srow;
   a.scale = scale;
   a.resid = resid;
@@ -713,7 +573,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   a.err = wait_timeout_word();
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(inl ? 320 : 192);
+  cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -721,7 +581,7 @@ tb_status_t gemv_tc(float* out, const float* x, const int8_t* q, const float* sc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return group > 0 ? launch_gv<true>(cfg, inl, G, tw, tx, a) : launch_gv<false>(cfg, inl, G, tw, tx, a);
+  return group > 0 ? launch_gv<true>(cfg, G, tw, tx, a) : launch_gv<false>(cfg, G, tw, tx, a);
 }
 
 }  // namespace tb

@@ -241,6 +241,8 @@ tb_status_t kv_append_rope(void* kc, void* vc, const float* k, const float* v, c
 tb_status_t rope_rows(float* x, const float* cos_t, const float* sin_t, int64_t B, int64_t S, int64_t Hx, int64_t D,
                       int64_t pos, int64_t ld, cudaStream_t st);
 tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, cudaStream_t st);
+// out[m, j] = silu(gu[m, j]) * gu[m, F + j] for B rows of 2F values
+tb_status_t silu_mul_rows(float* out, const float* gu, int64_t B, int64_t F, cudaStream_t st);
 // Decode step, B rows of qkv [B][(H + 2 Hkv) D]: RoPE on the q and k heads at
 // the device position *pos; q heads to q [B][H][D], k and v heads to the
 // caches [B][Hkv][max_seq][D] at *pos (v unrotated; fp32, or bf16 with kv_bf16).

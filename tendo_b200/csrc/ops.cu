@@ -155,6 +155,14 @@ __global__ void silu_mul_kernel(float* out, const float* gate, const float* up, 
     out[i] = __fmul_rn(silu_f(gate[i]), up[i]);
 }
 
+// out[m, j] = silu(gu[m, j]) * gu[m, F + j]: rows of [gate | up] products.
+__global__ void silu_mul_rows_kernel(float* out, const float* gu, int64_t B, int64_t F) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < B * F; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / F, j = i - m * F;
+    out[i] = __fmul_rn(silu_f(gu[m * 2 * F + j]), gu[m * 2 * F + F + j]);
+  }
+}
+
 __global__ void add_kernel(float* out, const float* a, const float* b, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = __fadd_rn(a[i], b[i]);
@@ -303,6 +311,12 @@ tb_status_t silu_mul(float* out, const float* gate, const float* up, int64_t n, 
   if (n == 0) return TB_SUCCESS;
   silu_mul_kernel<<<grid_1d(n, 256), 256, 0, st>>>(out, gate, up, n);
   return check_launch("silu_mul_kernel");
+}
+
+tb_status_t silu_mul_rows(float* out, const float* gu, int64_t B, int64_t F, cudaStream_t st) {
+  if (B * F == 0) return TB_SUCCESS;
+  silu_mul_rows_kernel<<<grid_1d(B * F, 256), 256, 0, st>>>(out, gu, B, F);
+  return check_launch("silu_mul_rows_kernel");
 }
 
 tb_status_t argmax_rows(int64_t* out, const float* x, int64_t rows, int64_t n, cudaStream_t st) {
