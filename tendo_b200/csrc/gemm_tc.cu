@@ -25,6 +25,8 @@
 // Every wait is bounded (counted in the library's timeout word).
 #include <cuda.h>  // CUtensorMap and the tensor-map encoder's types (resolved through the runtime)
 
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -34,6 +36,8 @@
 
 namespace tb {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 128;  // kTcBK in bytes = int8 elements
 constexpr int kTcTile = kTcBM * kTcBK;                 // 16 KB: one operand tile
@@ -51,24 +55,39 @@ struct TcCfg {
 // ---------------------------------------------------------------------------
 // digit planes
 // ---------------------------------------------------------------------------
-template <int NP>
+// One row per thread-block cluster of C CTAs (grid C x M); CTA r of the
+// cluster holds K / (4 C) float4 of the row in registers (VPT per thread),
+// the row's sum of squares and max |x| are combined over the cluster through
+// distributed shared memory in rank order (the same bits in every CTA), and
+// each CTA writes the digits of its own slice.
+template <int NP, int VPT>
 __global__ void __launch_bounds__(256) tc_digits_kernel(int8_t* __restrict__ dig, float* __restrict__ srow,
                                                         const float* __restrict__ x, int M, int K,
                                                         const float* __restrict__ norm_w, float eps) {
   __shared__ float red[2][8];
+  __shared__ float part[2];
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks(), r = (int)cl.block_rank();
   pdl_launch_dependents();  // the GEMV that consumes the digits may start streaming weights
   pdl_wait();               // x may come from the preceding kernel
-  const int m = blockIdx.x;
+  const int m = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * K);
-  const float4* wr = reinterpret_cast<const float4*>(norm_w);
-  const int nv = K >> 2;
+  const int nvc = (K >> 2) / C, v0 = r * nvc;  // this CTA's float4 of the row
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * K) + v0;
+  const float4* wr = norm_w ? reinterpret_cast<const float4*>(norm_w) + v0 : nullptr;
+  float4 t[VPT];
   float ss = 0.f, mx = 0.f;
-  for (int v = threadIdx.x; v < nv; v += 256) {
-    const float4 t = xr[v];
-    ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
-    const float4 w = norm_w ? wr[v] : make_float4(1.f, 1.f, 1.f, 1.f);
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t.x * w.x), fabsf(t.y * w.y)), fmaxf(fabsf(t.z * w.z), fabsf(t.w * w.w))));
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int v = threadIdx.x + i * 256;
+    t[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (v < nvc) {
+      t[i] = xr[v];
+      ss += t[i].x * t[i].x + t[i].y * t[i].y + t[i].z * t[i].z + t[i].w * t[i].w;
+      const float4 w = wr ? wr[v] : make_float4(1.f, 1.f, 1.f, 1.f);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(t[i].x * w.x), fabsf(t[i].y * w.y)),
+                           fmaxf(fabsf(t[i].z * w.z), fabsf(t[i].w * w.w))));
+    }
   }
   ss = warp_sum(ss);
   mx = warp_max(mx);
@@ -77,30 +96,45 @@ __global__ void __launch_bounds__(256) tc_digits_kernel(int8_t* __restrict__ dig
     red[1][warp] = mx;
   }
   __syncthreads();
-  float tot = 0.f, a = 0.f;
+  if (threadIdx.x == 0) {
+    float s0 = 0.f, a0 = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; w++) {
-    tot += red[0][w];
-    a = fmaxf(a, red[1][w]);
+    for (int w = 0; w < 8; w++) {
+      s0 += red[0][w];
+      a0 = fmaxf(a0, red[1][w]);
+    }
+    part[0] = s0;
+    part[1] = a0;
   }
+  cl.sync();
+  float tot = 0.f, a = 0.f;
+  for (int q = 0; q < C; q++) {
+    const float* pq = cl.map_shared_rank(part, q);
+    tot += pq[0];
+    a = fmaxf(a, pq[1]);
+  }
+  cl.sync();  // no CTA leaves while another still reads its partial sums
   // RMSNorm as cpu/backend.go:606-652: rms = sqrt(sumSq / d + eps), out = (x / rms) * w
   const float rms = norm_w ? __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)) : 1.0f;
   if (norm_w) a = a / rms * 1.0001f;  // covers the rounding of (x / rms) * w against (x * w) / rms
-  const float s = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
-  const float inv = 1.0f / s;
-  if (threadIdx.x == 0) srow[m] = s;
-  uint32_t* d0 = reinterpret_cast<uint32_t*>(dig + (size_t)m * K);
+  const float sc = (a > 0.f && isfinite(a)) ? a / 127.0f : 1.0f;
+  const float inv = 1.0f / sc;
+  if (threadIdx.x == 0 && r == 0) srow[m] = sc;
+  uint32_t* d0 = reinterpret_cast<uint32_t*>(dig + (size_t)m * K) + v0;
   const size_t plane = (size_t)M * K / 4;  // uint32 per plane
-  for (int v = threadIdx.x; v < nv; v += 256) {
-    float4 t = xr[v];
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int v = threadIdx.x + i * 256;
+    if (v >= nvc) continue;
+    float4 u4 = t[i];
     if (norm_w) {
       const float4 w = wr[v];
-      t.x = __fmul_rn(__fdiv_rn(t.x, rms), w.x);
-      t.y = __fmul_rn(__fdiv_rn(t.y, rms), w.y);
-      t.z = __fmul_rn(__fdiv_rn(t.z, rms), w.z);
-      t.w = __fmul_rn(__fdiv_rn(t.w, rms), w.w);
+      u4.x = __fmul_rn(__fdiv_rn(u4.x, rms), w.x);
+      u4.y = __fmul_rn(__fdiv_rn(u4.y, rms), w.y);
+      u4.z = __fmul_rn(__fdiv_rn(u4.z, rms), w.z);
+      u4.w = __fmul_rn(__fdiv_rn(u4.w, rms), w.w);
     }
-    const float vals[4] = {t.x, t.y, t.z, t.w};
+    const float vals[4] = {u4.x, u4.y, u4.z, u4.w};
     uint32_t p[3] = {0u, 0u, 0u};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -512,11 +546,43 @@ tb_status_t gemm_tc_digits(int8_t* dig, float* srow, const float* x, int M, int 
   if (M <= 0) return TB_SUCCESS;
   if (K % 4 != 0 || (uintptr_t)x % 16 != 0 || (norm_w && (uintptr_t)norm_w % 16 != 0))
     return TB_ERROR_NOT_SUPPORTED;
-  if (planes == 3)
-    tc_digits_kernel<3><<<M, 256, 0, st>>>(dig, srow, x, M, K, norm_w, eps);
-  else
-    tc_digits_kernel<2><<<M, 256, 0, st>>>(dig, srow, x, M, K, norm_w, eps);
-  return check_launch("tc_digits_kernel");
+  // a cluster of C CTAs per row, each holding K / (4 C) float4 in registers
+  int C = 8;
+  while (C > 1 && ((K / 4) % C != 0 || (K / 4) / C < 64)) C >>= 1;
+  const int nvc = (K / 4) / C;
+  const int vpt = (nvc + 255) / 256;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)C, (unsigned)M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e;
+#define TB_DIGITS(NP_, VPT_) e = cudaLaunchKernelEx(&cfg, tc_digits_kernel<NP_, VPT_>, dig, srow, x, M, K, norm_w, eps)
+  if (vpt > 16) return TB_ERROR_NOT_SUPPORTED;
+  if (planes == 3) {
+    if (vpt <= 1) TB_DIGITS(3, 1);
+    else if (vpt <= 2) TB_DIGITS(3, 2);
+    else if (vpt <= 4) TB_DIGITS(3, 4);
+    else if (vpt <= 8) TB_DIGITS(3, 8);
+    else TB_DIGITS(3, 16);
+  } else {
+    if (vpt <= 1) TB_DIGITS(2, 1);
+    else if (vpt <= 2) TB_DIGITS(2, 2);
+    else if (vpt <= 4) TB_DIGITS(2, 4);
+    else if (vpt <= 8) TB_DIGITS(2, 8);
+    else TB_DIGITS(2, 16);
+  }
+#undef TB_DIGITS
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_digits_kernel)");
+  return TB_SUCCESS;
 }
 
 tb_status_t gemm_tc_run(float* out, const int8_t* dig, const float* srow, const int8_t* q, const float* scale,
