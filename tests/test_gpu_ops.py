@@ -89,7 +89,9 @@ def test_synth_quantized_matches_oracle_model_weights(oracle, be, cuda):
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (1, 11008, 4096), (1, 4096, 11008), (2, 1408, 512),
                                    (3, 512, 1408), (8, 4096, 4096), (9, 640, 512), (32, 4096, 4096),
                                    (5, 33, 48), (1, 7, 100), (4, 1003, 4096), (5, 77, 128), (1, 8, 64),
-                                   (5, 4096, 4096), (1, 32000, 4096), (1, 8192, 28672), (3, 2000, 11008)])
+                                   (5, 4096, 4096), (1, 32000, 4096), (1, 8192, 28672), (3, 2000, 11008),
+                                   (6, 4096, 4096), (8, 11008, 4096), (10, 1003, 4096), (10, 22016, 4096),
+                                   (7, 12288, 4096)])
 def test_dequant_matmul_gemv(oracle, be, cuda, M, N, K):
     rng = np.random.default_rng(M * 7 + N + K)
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
