@@ -546,9 +546,11 @@ tb_status_t gemm_tc_digits(int8_t* dig, float* srow, const float* x, int M, int 
   if (M <= 0) return TB_SUCCESS;
   if (K % 4 != 0 || (uintptr_t)x % 16 != 0 || (norm_w && (uintptr_t)norm_w % 16 != 0))
     return TB_ERROR_NOT_SUPPORTED;
-  // a cluster of C CTAs per row, each holding K / (4 C) float4 in registers
+  // a cluster of C CTAs per row, each holding K / (4 C) float4 in registers:
+  // 8 for the few rows of a decode step, down to 1 once the rows alone give
+  // about two CTAs per SM (the prefill's hundreds of rows)
   int C = 8;
-  while (C > 1 && ((K / 4) % C != 0 || (K / 4) / C < 64)) C >>= 1;
+  while (C > 1 && ((K / 4) % C != 0 || (K / 4) / C < 64 || (int64_t)M * C / 2 >= 2 * sm_count())) C >>= 1;
   const int nvc = (K / 4) / C;
   const int vpt = (nvc + 255) / 256;
   cudaLaunchConfig_t cfg = {};
