@@ -2,6 +2,7 @@
 
     python -m tendo_b200.microbench [--M 1 8 32 128 2048] [--N 4096 11008] [--K 4096] [--iters 20] [--group G]
     python -m tendo_b200.microbench --decode-layers 8 [--tokens 4]
+    python -m tendo_b200.microbench --kind attention [--width 70b] [--batch 16] [--position 2048]
 
 W [N, K] is drawn N(0, 0.02) (seed 42) and int8-quantized per output channel
 on the device (per group of G input columns with --group G: scales [N, K/G]);
@@ -17,6 +18,13 @@ to L layers (d 4096, 32x128 heads, F 11008, vocab 32000, KV capacity 1024):
 a 512-token prompt, then `--tokens` decode tokens, one persistent-kernel
 launch each.  It is the small case for profiling that kernel (about 2.5 GB
 on the device at L = 8).
+
+--kind K times one kernel kind of the batched decode step (qkv, attention, o,
+gateup, down, lm_head; tb_model_time_kernel: graph-timed, per layer) on one
+layer of the 7B or 70B width (70B: d 8192, 64 query / 8 kv heads of 128,
+F 28672, KV capacity 4096) at `--batch` sequences whose cache holds
+`--position` rows.  One layer of the 70B width with its cache is about 3 GB
+on the device: the small case for profiling those kernels.
 """
 from __future__ import annotations
 
@@ -97,6 +105,24 @@ def decode_small(layers, tokens):
     qm.close()
 
 
+KINDS = ["qkv", "attention", "o", "gateup", "down", "lm_head"]
+
+
+def time_kind(kind, width, batch, position, iters):
+    if width == "70b":
+        cfg = dict(vocab=32000, dim=8192, layers=1, heads=64, kv_heads=8, hidden=28672, max_seq=4096,
+                   rope_base=500000.0, eps=1e-5)
+    else:
+        cfg = dict(vocab=32000, dim=4096, layers=1, heads=32, kv_heads=32, hidden=11008, max_seq=2048,
+                   rope_base=10000.0, eps=1e-6)
+    qm = tb.QuantizedModel(cfg, batch=batch, device=0)
+    qm.init_synthetic(0)
+    qm.set_position(position)
+    us = qm.time_kernel(KINDS.index(kind), iters)
+    print(json.dumps({"kind": kind, "width": width, "batch": batch, "position": position, "us": us}), flush=True)
+    qm.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--decode-layers", type=int, default=0)
@@ -107,8 +133,14 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--mode", type=int, default=tb.TB_GEMM_I8X3)
     ap.add_argument("--group", type=int, default=0)
+    ap.add_argument("--kind", choices=KINDS, default=None)
+    ap.add_argument("--width", choices=["7b", "70b"], default="70b")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--position", type=int, default=2048)
     a = ap.parse_args()
-    if a.decode_layers > 0:
+    if a.kind:
+        time_kind(a.kind, a.width, a.batch, a.position, a.iters)
+    elif a.decode_layers > 0:
         decode_small(a.decode_layers, a.tokens)
     else:
         run(a.M, a.N, a.K, a.iters, a.mode, a.group)
