@@ -103,6 +103,40 @@ def test_dequant_matmul_gemv(oracle, be, cuda, M, N, K):
     np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-3 * np.abs(want).max())
 
 
+@pytest.mark.parametrize("M", [1, 8, 32, 128])
+@pytest.mark.parametrize("K", [4096, 11008])
+def test_dequant_matmul_digit_split_bound_with_outliers(oracle, be, cuda, M, K):
+    """The three-digit split of x on rows with outliers.  Each row of x is
+    N(0, 1) with 0.1% of its entries at +-100x the median |x| (the last row
+    instead has a single spike), so the row scale s = max|x| / 127 is set by
+    the outliers and the ordinary entries keep only the digits' resolution
+    (2^-15 s per element).  The product is bounded against a float64 product
+    of the same int8 weights: |y - y_ref| <= 4 * 2^-15 * s * scale_n *
+    sum_k |q_nk| per element (the digit rounding plus the fp32 conversion of
+    the exact s32 sums), whatever path M takes (ring GEMV, tcgen05 GEMV or
+    GEMM)."""
+    N = 256
+    rng = np.random.default_rng(M * 31 + K)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    med = float(np.median(np.abs(x)))
+    for m in range(M):
+        if m == M - 1:
+            idx = rng.integers(0, K, size=1)
+        else:
+            idx = rng.choice(K, size=max(1, K // 1000), replace=False)
+        x[m, idx] = (100.0 * med * rng.choice([-1.0, 1.0], size=idx.size)).astype(np.float32)
+    _, q, scale = oracle.quantize(w, 0)
+    q = np.asarray(q, dtype=np.int8)
+    scale = np.asarray(scale, dtype=np.float32)
+    got = _np(be.DequantizeMatmul(_t(x, cuda), _t(q, cuda), _t(scale, cuda), 0)).astype(np.float64)
+    ref = (x.astype(np.float64) @ q.astype(np.float64).T) * scale.astype(np.float64)[None, :]
+    s = np.abs(x).max(axis=1).astype(np.float64) / 127.0
+    bound = 4.0 * 2.0 ** -15 * s[:, None] * (np.abs(q).astype(np.float64).sum(axis=1) * scale)[None, :]
+    err = np.abs(got - ref)
+    assert np.all(err <= bound), f"max err / bound = {(err / bound).max():.3f}"
+
+
 @pytest.mark.parametrize("M,group", [(1, 128), (4, 64), (40, 128)])
 def test_dequant_matmul_grouped(oracle, be, cuda, M, group):
     rng = np.random.default_rng(group + M)
