@@ -368,9 +368,23 @@ TB_API tb_status_t tb_model_create_tp(tb_model** out, const tb_model_config* cfg
 /* tb_model_create / tb_model_create_tp (comm may be null) with options. */
 TB_API tb_status_t tb_model_create_ex(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm,
                                       uint32_t flags);
+/* The model with every Linear quantized per group of group_size input
+ * columns (QuantizeModel(m, groupSize), models/llama/quantized.go:52-73;
+ * nn/quantize.go:126-187): scales [rows][K / group_size] in
+ * tb_model_set_linear / tb_model_get_linear and in the synthetic weights.
+ * group_size 0 is tb_model_create_ex.  Every Linear's input width (on a
+ * tensor-parallel rank, its share of Wo and Wdown) must be a multiple of
+ * group_size (TB_ERROR_NOT_SUPPORTED otherwise).  Decode runs the tcgen05
+ * GEMV with per-group scales (group_size a multiple of 128, up to 64
+ * sequences; other sizes run the per-step DequantizeMatmul); prefill runs
+ * the grouped DequantizeMatmul; the batch-1 persistent kernel and the fused
+ * per-channel kernels are not used. */
+TB_API tb_status_t tb_model_create_grouped(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm,
+                                           uint32_t flags, int64_t group_size);
 TB_API tb_status_t tb_model_destroy(tb_model* m);
 /* Synthetic weights: N(0, 0.02) from (seed, stream = layer * 8 + matrix),
- * quantized per channel on the device; gains 1.0; embedding and lm_head fp32. */
+ * quantized per channel (per group for tb_model_create_grouped) on the
+ * device; gains 1.0; embedding and lm_head fp32. */
 TB_API tb_status_t tb_model_init_synthetic(tb_model* m, uint64_t seed);
 /* Loads one quantized Linear (mat 0..6 = q, k, v, o, gate, up, down) from
  * HOST arrays q[N, K] int8 and scale[N]; which = 0 embedding [V, d],

@@ -323,7 +323,9 @@ struct or_model {
   int64_t n_out[7];
   int64_t n_in[7];
   int8_t* q[7];     /* per matrix: [layers][N][K] */
-  float* scale[7];  /* [layers][N] */
+  float* scale[7];  /* [layers][N][K / group] (group 0: [layers][N]) */
+  int64_t group;    /* 0: per output channel */
+  int64_t ng[7];    /* scales per row */
   float* attn_norm; /* [layers][d] */
   float* mlp_norm;
   float* final_norm;
@@ -342,10 +344,17 @@ static void* xcalloc(size_t n) {
 }
 
 or_model* or_model_create(const or_config* cfg, int batch, uint64_t seed, int generate) {
+  return or_model_create_grouped(cfg, batch, seed, generate, 0);
+}
+
+/* QuantizeModel(m, groupSize) (models/llama/quantized.go:52-73): every
+ * Linear quantized per group of `group` input columns (0: per channel). */
+or_model* or_model_create_grouped(const or_config* cfg, int batch, uint64_t seed, int generate, int64_t group) {
   or_model* m = (or_model*)xcalloc(sizeof(or_model));
   if (!m) return NULL;
   m->c = *cfg;
   m->B = batch;
+  m->group = group;
   int64_t d = cfg->dim, D = cfg->dim / cfg->heads;
   int64_t hq = (int64_t)cfg->heads * D, hkv = (int64_t)cfg->kv_heads * D, F = cfg->hidden;
   int64_t no[7] = {hq, hkv, hkv, d, F, F, d};
@@ -355,8 +364,10 @@ or_model* or_model_create(const or_config* cfg, int batch, uint64_t seed, int ge
   for (int i = 0; i < 7; i++) {
     m->n_out[i] = no[i];
     m->n_in[i] = ni[i];
+    m->ng[i] = group > 0 ? ni[i] / group : 1;
+    if (group > 0 && ni[i] % group != 0) ok = 0;
     m->q[i] = (int8_t*)malloc((size_t)L * no[i] * ni[i]);
-    m->scale[i] = (float*)malloc(sizeof(float) * (size_t)L * no[i]);
+    m->scale[i] = (float*)malloc(sizeof(float) * (size_t)L * no[i] * m->ng[i]);
     ok = ok && m->q[i] && m->scale[i];
   }
   m->attn_norm = (float*)malloc(sizeof(float) * (size_t)L * d);
@@ -389,7 +400,10 @@ or_model* or_model_create(const or_config* cfg, int batch, uint64_t seed, int ge
 #pragma omp for schedule(static)
           for (int64_t n = 0; n < N; n++) {
             for (int64_t k = 0; k < K; k++) row[k] = ts_normal_f32(key, (uint64_t)(n * K + k), 0.02);
-            quantize_span(row, K, NULL, m->q[i] + ((int64_t)l * N + n) * K, m->scale[i] + (int64_t)l * N + n);
+            const int64_t ng = m->ng[i], g = K / ng;
+            for (int64_t j = 0; j < ng; j++)
+              quantize_span(row + j * g, g, NULL, m->q[i] + ((int64_t)l * N + n) * K + j * g,
+                            m->scale[i] + ((int64_t)l * N + n) * ng + j);
           }
           free(row);
         }
@@ -427,7 +441,9 @@ void or_model_free(or_model* m) {
 int8_t* or_model_q(or_model* m, int layer, int mat) {
   return m->q[mat] + (int64_t)layer * m->n_out[mat] * m->n_in[mat];
 }
-float* or_model_scale(or_model* m, int layer, int mat) { return m->scale[mat] + (int64_t)layer * m->n_out[mat]; }
+float* or_model_scale(or_model* m, int layer, int mat) {
+  return m->scale[mat] + (int64_t)layer * m->n_out[mat] * m->ng[mat];
+}
 float* or_model_norm(or_model* m, int layer, int which) {
   if (layer < 0) return m->final_norm;
   return (which ? m->mlp_norm : m->attn_norm) + (int64_t)layer * m->c.dim;
@@ -479,9 +495,9 @@ static void attention_layer(or_model* m, int l, const float* xn, int64_t S, floa
   const or_config* c = &m->c;
   int64_t B = m->B, d = c->dim, H = c->heads, Hkv = c->kv_heads, D = d / H;
   int64_t P = m->pos, Sk = P + S, Ms = c->max_seq;
-  or_dequant_matmul(xn, or_model_q(m, l, 0), or_model_scale(m, l, 0), B * S, H * D, d, 0, scratch_q);
-  or_dequant_matmul(xn, or_model_q(m, l, 1), or_model_scale(m, l, 1), B * S, Hkv * D, d, 0, scratch_k);
-  or_dequant_matmul(xn, or_model_q(m, l, 2), or_model_scale(m, l, 2), B * S, Hkv * D, d, 0, scratch_v);
+  or_dequant_matmul(xn, or_model_q(m, l, 0), or_model_scale(m, l, 0), B * S, H * D, d, m->group, scratch_q);
+  or_dequant_matmul(xn, or_model_q(m, l, 1), or_model_scale(m, l, 1), B * S, Hkv * D, d, m->group, scratch_k);
+  or_dequant_matmul(xn, or_model_q(m, l, 2), or_model_scale(m, l, 2), B * S, Hkv * D, d, m->group, scratch_v);
   /* permute [B,S,H,D] -> [B,H,S,D] */
   float* qh = (float*)malloc(sizeof(float) * (size_t)(B * H * S * D));
   float* kh = (float*)malloc(sizeof(float) * (size_t)(B * Hkv * S * D));
@@ -540,7 +556,7 @@ static void attention_layer(or_model* m, int l, const float* xn, int64_t S, floa
     free(sc);
     free(pr);
   }
-  or_dequant_matmul(attn, or_model_q(m, l, 3), or_model_scale(m, l, 3), B * S, d, H * D, 0, out);
+  or_dequant_matmul(attn, or_model_q(m, l, 3), or_model_scale(m, l, 3), B * S, d, H * D, m->group, out);
   free(qh);
   free(kh);
 }
@@ -573,11 +589,11 @@ int or_model_forward(or_model* m, const int64_t* tokens, int64_t S, float* logit
     for (int64_t i = 0; i < rows * d; i++) h[i] = h[i] + t1[i];
     or_rmsnorm(h, or_model_norm(m, l, 1), rows, d, c->eps, xn);
     /* forwardQuantizedMLP, :385-417: down(silu(gate(x)) * up(x)) */
-    or_dequant_matmul(xn, or_model_q(m, l, 4), or_model_scale(m, l, 4), rows, F, d, 0, g);
+    or_dequant_matmul(xn, or_model_q(m, l, 4), or_model_scale(m, l, 4), rows, F, d, m->group, g);
     or_silu(g, rows * F, g);
-    or_dequant_matmul(xn, or_model_q(m, l, 5), or_model_scale(m, l, 5), rows, F, d, 0, u);
+    or_dequant_matmul(xn, or_model_q(m, l, 5), or_model_scale(m, l, 5), rows, F, d, m->group, u);
     for (int64_t i = 0; i < rows * F; i++) g[i] = g[i] * u[i];
-    or_dequant_matmul(g, or_model_q(m, l, 6), or_model_scale(m, l, 6), rows, d, F, 0, t1);
+    or_dequant_matmul(g, or_model_q(m, l, 6), or_model_scale(m, l, 6), rows, d, F, m->group, t1);
     for (int64_t i = 0; i < rows * d; i++) h[i] = h[i] + t1[i];
     if (hidden) memcpy(hidden + (int64_t)(l + 1) * rows * d, h, sizeof(float) * (size_t)(rows * d));
   }

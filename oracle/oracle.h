@@ -95,6 +95,10 @@ typedef struct or_model or_model;
  * gains are 1.0, embedding and lm_head stay fp32.  With generate == 0 the
  * arrays are left zero for the caller to fill. */
 or_model* or_model_create(const or_config* cfg, int batch, uint64_t seed, int generate);
+/* The same model with every Linear quantized per group of `group` input
+ * columns (QuantizeModel(m, groupSize), models/llama/quantized.go:52-73);
+ * scales [N][K / group]; group 0 is per channel. */
+or_model* or_model_create_grouped(const or_config* cfg, int batch, uint64_t seed, int generate, int64_t group);
 void or_model_free(or_model* m);
 
 /* Pointers into the model's arrays (mat: 0..6 = q,k,v,o,gate,up,down). */

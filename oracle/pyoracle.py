@@ -72,6 +72,9 @@ def lib():
         L.or_synth_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _i64, _f32p]
         L.or_model_create.argtypes = [ctypes.POINTER(Config), ctypes.c_int, ctypes.c_uint64, ctypes.c_int]
         L.or_model_create.restype = ctypes.c_void_p
+        L.or_model_create_grouped.argtypes = [ctypes.POINTER(Config), ctypes.c_int, ctypes.c_uint64, ctypes.c_int,
+                                              _i64]
+        L.or_model_create_grouped.restype = ctypes.c_void_p
         L.or_model_free.argtypes = [ctypes.c_void_p]
         L.or_model_q.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.or_model_q.restype = _i8p
@@ -231,11 +234,13 @@ STREAM_W = 0x7FFF0005
 
 
 class Model:
-    """Quantized Llama oracle (models/llama/quantized.go) for B lockstep sequences."""
+    """Quantized Llama oracle (models/llama/quantized.go) for B lockstep sequences;
+    with ``group`` > 0 every Linear is quantized per group of that many input
+    columns (QuantizeModel(m, groupSize), models/llama/quantized.go:52-73)."""
 
     MATS = ("q", "k", "v", "o", "gate", "up", "down")
 
-    def __init__(self, cfg: dict, batch: int = 1, seed: int = 0, generate: bool = True):
+    def __init__(self, cfg: dict, batch: int = 1, seed: int = 0, generate: bool = True, group: int = 0):
         self.cfg = dict(cfg)
         c = Config(
             cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"],
@@ -243,7 +248,8 @@ class Model:
         )
         self._c = c
         self.B = batch
-        self.h = lib().or_model_create(ctypes.byref(c), batch, seed, 1 if generate else 0)
+        self.group = group
+        self.h = lib().or_model_create_grouped(ctypes.byref(c), batch, seed, 1 if generate else 0, group)
         if not self.h:
             raise MemoryError("or_model_create failed")
 
@@ -269,8 +275,9 @@ class Model:
         return np.ctypeslib.as_array(lib().or_model_q(self.h, layer, mat), shape=(N, K))
 
     def scale(self, layer: int, mat: int) -> np.ndarray:
-        N, _ = self.shape(mat)
-        return np.ctypeslib.as_array(lib().or_model_scale(self.h, layer, mat), shape=(N,))
+        N, K = self.shape(mat)
+        shape = (N, K // self.group) if self.group else (N,)
+        return np.ctypeslib.as_array(lib().or_model_scale(self.h, layer, mat), shape=shape)
 
     def embed(self) -> np.ndarray:
         c = self.cfg

@@ -81,6 +81,7 @@ SIGNATURES = [
     ("tb_model_create", _st, [_vp, _vp, ctypes.c_int]),
     ("tb_model_create_tp", _st, [_vp, _vp, ctypes.c_int, _vp]),
     ("tb_model_create_ex", _st, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_uint32]),
+    ("tb_model_create_grouped", _st, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_uint32, _i64]),
     ("tb_sample_f32", _st, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float, _vp]),
     ("tb_model_generate_sample", _st, [_vp, _vp, _i64, _i64, _i64, ctypes.c_float, _i64, ctypes.c_float,
                                        ctypes.c_uint64, _vp]),
@@ -629,19 +630,25 @@ class QuantizedModel:
     """QuantizedModel (models/llama/quantized.go) on one GPU, B sequences in
     lockstep; with ``comm``, this rank's tensor-parallel share of it.
     ``kv_bf16``: the KV cache in bf16 (TB_MODEL_KV_BF16), half the cache bytes,
-    values rounded to nearest even as they are appended."""
+    values rounded to nearest even as they are appended.  ``group``: every
+    Linear quantized per group of that many input columns (QuantizeModel(m,
+    groupSize)); scales [rows, K / group] in set_linear / get_linear."""
 
     def __init__(self, cfg: dict, batch: int = 1, device: int = 0, comm: "Comm | None" = None,
-                 kv_bf16: bool = False):
+                 kv_bf16: bool = False, group: int = 0):
         self.cfg = dict(cfg)
         self.B = batch
         self.device = device
         self.comm = comm
         self.kv_bf16 = kv_bf16
+        self.group = group
         c = ModelConfig(cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"],
                         cfg["max_seq"], cfg["rope_base"], cfg["eps"], batch)
         h = ctypes.c_void_p()
-        if kv_bf16:
+        if group:
+            check(lib.tb_model_create_grouped(ctypes.byref(h), ctypes.byref(c), device, comm.h if comm else None,
+                                              TB_MODEL_KV_BF16 if kv_bf16 else 0, group))
+        elif kv_bf16:
             check(lib.tb_model_create_ex(ctypes.byref(h), ctypes.byref(c), device, comm.h if comm else None,
                                          TB_MODEL_KV_BF16))
         elif comm is None:
@@ -671,13 +678,16 @@ class QuantizedModel:
 
         q = np.ascontiguousarray(q, dtype=np.int8)
         scale = np.ascontiguousarray(scale, dtype=np.float32)
+        want = q.shape[0] * (q.shape[1] // self.group if self.group else 1)
+        if q.ndim != 2 or scale.size != want:
+            raise ShapeError(f"set_linear: scales of a {q.shape} Linear have {want} values, got {scale.size}")
         check(lib.tb_model_set_linear(self.h, layer, mat, q.ctypes.data, scale.ctypes.data))
 
     def get_linear(self, layer: int, mat: int, shape):
         import numpy as np
 
         q = np.empty(shape, np.int8)
-        s = np.empty(shape[0], np.float32)
+        s = np.empty((shape[0], shape[1] // self.group) if self.group else shape[0], np.float32)
         check(lib.tb_model_get_linear(self.h, layer, mat, q.ctypes.data, s.ctypes.data))
         return q, s
 

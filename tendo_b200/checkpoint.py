@@ -138,14 +138,16 @@ def export_model(qm, path: str) -> None:
     tensors["model.norm.weight"] = qm.get_tensor(2, 0, (cfg["dim"],))
     tensors["lm_head.weight"] = qm.get_tensor(1, 0, (cfg["vocab"], cfg["dim"]))
     meta = {k: cfg[k] for k in ("vocab", "dim", "layers", "heads", "kv_heads", "hidden")}
-    meta["format"] = "tendo-int8-per-channel"
+    g = getattr(qm, "group", 0)
+    meta["format"] = f"tendo-int8-per-group-{g}" if g else "tendo-int8-per-channel"
     write(path, tensors, meta)
 
 
 def load_model(qm, path: str) -> None:
     """Uploads a pre-quantized checkpoint into a QuantizedModel (its shard,
-    for a tensor-parallel one).  Shapes, dtypes and per-channel scales are
-    checked against the model's configuration."""
+    for a tensor-parallel one).  Shapes, dtypes and the scales (per channel,
+    or per group for a model made with ``group``) are checked against the
+    model's configuration."""
     st = SafeTensors(path)
     cfg = qm.cfg
     comm = getattr(qm, "comm", None)
@@ -164,11 +166,16 @@ def load_model(qm, path: str) -> None:
         for mat in range(7):
             N, K = shapes[mat]
             base = _linear_name(layer, mat)
+            g = getattr(qm, "group", 0)
             q = need(base + ".weight", "I8", (N, K))
-            s = need(base + ".weight_scale", "F32", (N,))
+            s = need(base + ".weight_scale", "F32", (N, K // g) if g else (N,))
             if LINEARS[mat][1]:  # column-parallel: this rank's output rows
                 rows = slice(r * N // n, (r + 1) * N // n)
                 qm.set_linear(layer, mat, q[rows], s[rows])
+            elif g:  # row-parallel, per group: this rank's input columns and their groups
+                cols = slice(r * K // n, (r + 1) * K // n)
+                groups = slice(r * (K // g) // n, (r + 1) * (K // g) // n)
+                qm.set_linear(layer, mat, q[:, cols], np.ascontiguousarray(s[:, groups]))
             else:  # row-parallel: this rank's input columns, every row's scale
                 cols = slice(r * K // n, (r + 1) * K // n)
                 qm.set_linear(layer, mat, q[:, cols], s)

@@ -41,6 +41,7 @@ struct tb_model {
   bool kv16 = false;                   // bf16 KV cache (TB_MODEL_KV_BF16)
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *u = nullptr;
   float* gu = nullptr;  // decode: [B, 2F] gate and up products of one launch
+  int64_t group = 0;    // scales per group of this many input columns (0: per output channel)
   float *qbuf = nullptr, *partial = nullptr, *logits = nullptr, *last = nullptr;
   unsigned long long* keys = nullptr;
   int64_t *tokens = nullptr, *ids = nullptr, *history = nullptr, *pos = nullptr, *step = nullptr;
@@ -112,24 +113,28 @@ size_t lin_cols(const tb_model* m, int mat) {
   return (size_t)c[mat];
 }
 
-// Pointers of one Linear inside the layer buffers.
+// Scales per row of one Linear: K / group, or 1 per output channel.
+size_t lin_ng(const tb_model* m, int mat) { return m->group ? lin_cols(m, mat) / (size_t)m->group : 1; }
+
+// Pointers of one Linear inside the layer buffers (scales [rows][lin_ng]).
 void lin_ptr(tb_model* m, int layer, int mat, int8_t** q, float** s) {
   const int64_t hq = m->H * m->D, hkv = m->Hkv * m->D;
+  const size_t gd = m->group ? (size_t)(m->d / m->group) : 1, gh = lin_ng(m, 3), gf = lin_ng(m, 6);
   switch (mat) {
-    case 0: *q = m->wqkv + (size_t)layer * m->NQKV * m->d; *s = m->sqkv + (size_t)layer * m->NQKV; break;
+    case 0: *q = m->wqkv + (size_t)layer * m->NQKV * m->d; *s = m->sqkv + (size_t)layer * m->NQKV * gd; break;
     case 1:
       *q = m->wqkv + ((size_t)layer * m->NQKV + hq) * m->d;
-      *s = m->sqkv + (size_t)layer * m->NQKV + hq;
+      *s = m->sqkv + ((size_t)layer * m->NQKV + hq) * gd;
       break;
     case 2:
       *q = m->wqkv + ((size_t)layer * m->NQKV + hq + hkv) * m->d;
-      *s = m->sqkv + (size_t)layer * m->NQKV + hq + hkv;
+      *s = m->sqkv + ((size_t)layer * m->NQKV + hq + hkv) * gd;
       break;
-    case 3: *q = m->wo + (size_t)layer * m->d * hq; *s = m->so + (size_t)layer * m->d; break;
+    case 3: *q = m->wo + (size_t)layer * m->d * hq; *s = m->so + (size_t)layer * m->d * gh; break;
     // gate and up rows of a layer are adjacent (one [2F, d] matrix, gate first)
-    case 4: *q = m->wgate + (size_t)layer * 2 * m->F * m->d; *s = m->sgate + (size_t)layer * 2 * m->F; break;
-    case 5: *q = m->wup + (size_t)layer * 2 * m->F * m->d; *s = m->sup + (size_t)layer * 2 * m->F; break;
-    default: *q = m->wdown + (size_t)layer * m->d * m->F; *s = m->sdown + (size_t)layer * m->d; break;
+    case 4: *q = m->wgate + (size_t)layer * 2 * m->F * m->d; *s = m->sgate + (size_t)layer * 2 * m->F * gd; break;
+    case 5: *q = m->wup + (size_t)layer * 2 * m->F * m->d; *s = m->sup + (size_t)layer * 2 * m->F * gd; break;
+    default: *q = m->wdown + (size_t)layer * m->d * m->F; *s = m->sdown + (size_t)layer * m->d * gf; break;
   }
 }
 
@@ -153,7 +158,8 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
   const int64_t P = m->host_pos;
   const float scale = 1.0f / (float)sqrt((double)m->D);
   // rows > 32: projections on the tcgen05 GEMM (digit rows of the activations)
-  const bool tc = rows > 32 && tb::gemm_tc_ok(m->wqkv, rows, m->NQKV, m->d) &&
+  // per-group scales: every projection through the grouped DequantizeMatmul
+  const bool tc = rows > 32 && !m->group && tb::gemm_tc_ok(m->wqkv, rows, m->NQKV, m->d) &&
                   tb::gemm_tc_ok(m->wo, rows, m->d, m->H * m->D) && tb::gemm_tc_ok(m->wdown, rows, m->d, m->F);
   for (int64_t l = 0; l < m->L; l++) {
     int8_t *wq, *wo, *wg, *wu, *wd;
@@ -173,7 +179,7 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
                              st));
     } else {
       TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->attn_norm + l * m->d, rows, m->d, m->c.eps, st));
-      TB_TRY(tb_dequant_matmul_i8f32(m->qkv, m->xn, wq, sq, rows, m->NQKV, m->d, 0, (tb_stream_t)st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->qkv, m->xn, wq, sq, rows, m->NQKV, m->d, m->group, (tb_stream_t)st));
     }
     TB_TRY(tb::rope_rows(m->qkv, m->cos_t, m->sin_t, m->B, S, m->H, m->D, P, m->NQKV, st));
     TB_TRY(tb::kv_append_rope(kcl, vcl, m->qkv + m->H * m->D, m->qkv + (m->H + m->Hkv) * m->D, m->cos_t, m->sin_t,
@@ -206,8 +212,8 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
     // o projection + residual; row-parallel under tensor parallelism: each
     // rank's partial product, the residual on rank 0 only, summed over ranks
     const float* resid = m->tp_rank == 0 ? m->h : nullptr;
-    if (rows <= 32) {
-      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, 0, (tb_stream_t)st));
+    if (rows <= 32 || m->group) {
+      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->attn, wo, so, rows, m->d, m->H * m->D, m->group, (tb_stream_t)st));
       TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st, m->err_word));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
@@ -227,12 +233,12 @@ tb_status_t forward_layers(tb_model* m, int64_t S) {
       TB_TRY(tb::gemm_tc_run(m->u, m->tcdig, m->tcs, wu, su, nullptr, (int)rows, (int)m->F, (int)m->d, kTcPlanes, st));
     } else {
       TB_TRY(tb::rmsnorm(m->xn, nullptr, m->h, nullptr, m->mlp_norm + l * m->d, rows, m->d, m->c.eps, st));
-      TB_TRY(tb_dequant_matmul_i8f32(m->g, m->xn, wg, sg, rows, m->F, m->d, 0, (tb_stream_t)st));
-      TB_TRY(tb_dequant_matmul_i8f32(m->u, m->xn, wu, su, rows, m->F, m->d, 0, (tb_stream_t)st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->g, m->xn, wg, sg, rows, m->F, m->d, m->group, (tb_stream_t)st));
+      TB_TRY(tb_dequant_matmul_i8f32(m->u, m->xn, wu, su, rows, m->F, m->d, m->group, (tb_stream_t)st));
     }
     TB_TRY(tb::silu_mul(m->g, m->g, m->u, rows * m->F, st));
-    if (rows <= 32) {
-      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, 0, (tb_stream_t)st));
+    if (rows <= 32 || m->group) {
+      TB_TRY(tb_dequant_matmul_i8f32(m->xn, m->g, wd, sd, rows, m->d, m->F, m->group, (tb_stream_t)st));
       TB_TRY(tb::allreduce(m->comm, m->xn, (size_t)(rows * m->d), false, st, m->err_word));
       TB_TRY(tb_add_f32(m->h, m->h, m->xn, rows * m->d, (tb_stream_t)st));
     } else if (tc) {
@@ -335,7 +341,7 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
     qa.D = (int)m->D;
     qa.max_seq = (int)m->Ms;
     const float* resid = m->tp_rank == 0 ? m->h : nullptr;
-    if (m->gv && (kind == 0 || kind == 2 || kind == 3) && m->B > kDecodeGemmRows) {
+    if (m->gv && (kind == 0 || kind == 2 || kind == 3) && m->B > kDecodeGemmRows && !m->group) {
       // 33..64 sequences: the prefill GEMM (a 128-row tile of the sequences'
       // digit rows against 128 weight rows) reads each weight tile once and
       // needs no split-K reduction; the digit rows (with the RMSNorm) once
@@ -366,18 +372,22 @@ tb_status_t decode_kernel(tb_model* m, int kind, int64_t l, bool pdl) {
       const int B = (int)m->B, d = (int)m->d, HD = (int)(m->H * m->D), F = (int)m->F;
       if (kind == 0) {
         TB_TRY(tb::gemv_tc(m->qkv, m->h, wq, sq, nullptr, B, (int)m->NQKV, d, m->gv_zero, false, m->gv_scratch, st,
-                           m->attn_norm + l * m->d, m->c.eps));
+                           m->attn_norm + l * m->d, m->c.eps, (int)m->group));
         return tb::qkv_rope_append(m->qbuf, kcl, vcl, m->qkv, m->cos_t, m->sin_t, m->pos, m->B, m->H, m->Hkv, m->D,
                                    m->Ms, st, m->kv16);
       }
-      if (kind == 2) return tb::gemv_tc(m->h, m->attn, wo, so, resid, B, d, HD, m->gv_zero, false, m->gv_scratch, st);
+      if (kind == 2)
+        return tb::gemv_tc(m->h, m->attn, wo, so, resid, B, d, HD, m->gv_zero, false, m->gv_scratch, st, nullptr, 0.f,
+                           (int)m->group);
       if (kind == 3) {
         // gate and up rows are one [2F, d] matrix: one GEMV launch, then SwiGLU
         TB_TRY(tb::gemv_tc(m->gu, m->h, wg, sg, nullptr, B, 2 * F, d, m->gv_zero, false, m->gv_scratch, st,
-                           m->mlp_norm + l * m->d, m->c.eps));
+                           m->mlp_norm + l * m->d, m->c.eps, (int)m->group));
         return tb::silu_mul_rows(m->g, m->gu, m->B, m->F, st);
       }
-      if (kind == 4) return tb::gemv_tc(m->h, m->g, wd, sd, resid, B, d, F, m->gv_zero, false, m->gv_scratch, st);
+      if (kind == 4)
+        return tb::gemv_tc(m->h, m->g, wd, sd, resid, B, d, F, m->gv_zero, false, m->gv_scratch, st, nullptr, 0.f,
+                           (int)m->group);
     }
     if (kind == 0) {
       // the fused kernels take up to 8 sequences: larger batches run in groups
@@ -564,8 +574,9 @@ tb_status_t build_graph(tb_model* m) {
 
 namespace {
 
-tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm, uint32_t flags) {
-  TB_REQUIRE(out && cfg);
+tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm, uint32_t flags,
+                         int64_t group = 0) {
+  TB_REQUIRE(out && cfg && group >= 0);
   TB_REQUIRE((flags & ~(uint32_t)TB_MODEL_KV_BF16) == 0);
   *out = nullptr;
   TB_REQUIRE(cfg->vocab > 0 && cfg->dim > 0 && cfg->layers > 0 && cfg->heads > 0 && cfg->kv_heads > 0);
@@ -581,6 +592,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->device = device;
   m->comm = comm;
   m->kv16 = (flags & TB_MODEL_KV_BF16) != 0;
+  m->group = group;
   m->tp = tp;
   m->tp_rank = rank;
   m->Hg = cfg->heads;
@@ -598,6 +610,12 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   m->Ms = cfg->max_seq;
   m->B = cfg->max_batch;
   m->NQKV = (m->H + 2 * m->Hkv) * m->D;
+  // per-group scales: every Linear's input width (this rank's share of the
+  // row-parallel ones) a whole number of groups
+  if (group && (m->d % group || (m->H * m->D) % group || m->F % group)) {
+    delete m;
+    return TB_ERROR_NOT_SUPPORTED;
+  }
   m->hist_cap = m->Ms;
   m->chunk_s = 4096 / m->B > 0 ? 4096 / m->B : 1;
   if (m->chunk_s > m->Ms) m->chunk_s = m->Ms;
@@ -610,9 +628,9 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     const int64_t HD = m->H * m->D;
     // (a bf16 cache takes this path at batch 1 too: its RoPE / append kernel
     // writes either cache type)
-    m->gv = (m->B > 1 || m->kv16) && m->B <= tb::kGemvTcMaxM && tb::gemv_tc_ok(al, m->B, m->NQKV, m->d) &&
-            tb::gemv_tc_ok(al, m->B, m->d, HD) && tb::gemv_tc_ok(al, m->B, 2 * m->F, m->d) &&
-            tb::gemv_tc_ok(al, m->B, m->d, m->F);
+    m->gv = (m->B > 1 || m->kv16 || m->group) && m->B <= tb::kGemvTcMaxM &&
+            tb::gemv_tc_ok(al, m->B, m->NQKV, m->d, m->group) && tb::gemv_tc_ok(al, m->B, m->d, HD, m->group) &&
+            tb::gemv_tc_ok(al, m->B, 2 * m->F, m->d, m->group) && tb::gemv_tc_ok(al, m->B, m->d, m->F, m->group);
   }
   // the captured decode step: the attention kernel's head shapes, and either
   // the tcgen05 GEMV projections (2..64 sequences) or the fused CUDA-core /
@@ -626,13 +644,13 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
   if (m->lm_rows && m->B > 4 * m->lm_rows) m->lm_rows = 0;
   m->fused = m->d % 16 == 0 && (m->H * m->D) % 16 == 0 && m->F % 16 == 0 && (m->D == 64 || m->D == 128) &&
              (m->H / m->Hkv == 1 || m->H / m->Hkv == 2 || m->H / m->Hkv == 4 || m->H / m->Hkv == 8) &&
-             (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024 && !m->kv16));
+             (m->gv ? m->B <= 64 : (m->B <= 16 && fused_smem <= 200 * 1024 && !m->kv16 && !m->group));
   const char* nopdl = getenv("TENDO_B200_NO_PDL");
   m->pdl = !(nopdl && *nopdl == '1');
   m->nsplit = tb::attn_decode_splits((int)m->B, (int)m->H, (int)m->Hkv, (int)m->D, m->Ms, m->kv16);
   {
     const char* e = getenv("TENDO_B200_MEGAKERNEL");
-    m->mk = !(e && e[0] == '0') && tp == 1 && !m->kv16 &&
+    m->mk = !(e && e[0] == '0') && tp == 1 && !m->kv16 && m->group == 0 &&
             tb::megakernel_supported((int)m->d, (int)m->H, (int)m->Hkv, (int)m->D, (int)m->F, (int)m->V, (int)m->B);
     m->mk_nsplit = tb::megakernel_splits((int)m->Hkv);
   }
@@ -641,20 +659,21 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     if (s == TB_SUCCESS) s = r;
   };
   const size_t L = m->L;
+  const size_t gd = m->group ? (size_t)(m->d / m->group) : 1;
   A(dalloc(m, &m->wqkv, L * m->NQKV * m->d));
-  A(dalloc(m, &m->sqkv, L * m->NQKV));
+  A(dalloc(m, &m->sqkv, L * m->NQKV * gd));
   A(dalloc(m, &m->wo, L * m->d * m->H * m->D));
-  A(dalloc(m, &m->so, L * m->d));
+  A(dalloc(m, &m->so, L * m->d * lin_ng(m, 3)));
   // per layer the gate rows, then the up rows: one [2F, d] matrix, so a
   // single GEMV launch computes both
   A(dalloc(m, &m->wgate, L * 2 * m->F * m->d));
-  A(dalloc(m, &m->sgate, L * 2 * m->F));
+  A(dalloc(m, &m->sgate, L * 2 * m->F * gd));
   if (s == TB_SUCCESS) {
     m->wup = m->wgate + m->F * m->d;
-    m->sup = m->sgate + m->F;
+    m->sup = m->sgate + m->F * gd;
   }
   A(dalloc(m, &m->wdown, L * m->d * m->F));
-  A(dalloc(m, &m->sdown, L * m->d));
+  A(dalloc(m, &m->sdown, L * m->d * lin_ng(m, 6)));
   A(dalloc(m, &m->attn_norm, L * m->d));
   A(dalloc(m, &m->mlp_norm, L * m->d));
   A(dalloc(m, &m->final_norm, (size_t)m->d));
@@ -713,7 +732,7 @@ tb_status_t create_model(tb_model** out, const tb_model_config* cfg, int device,
     unsigned char* z = nullptr;
     unsigned char* sc = nullptr;
     A(dalloc(m, &z, tb::gemv_tc_zeroed_bytes(m->B, nmax, kmax)));
-    A(dalloc(m, &sc, tb::gemv_tc_scratch_bytes(m->B, nmax, kmax)));
+    A(dalloc(m, &sc, tb::gemv_tc_scratch_bytes(m->B, nmax, kmax, m->group)));
     m->gv_zero = z;
     m->gv_scratch = sc;
     if (z) {
@@ -778,6 +797,12 @@ extern "C" tb_status_t tb_model_create_ex(tb_model** out, const tb_model_config*
   return create_model(out, cfg, device, comm, flags);
 }
 
+extern "C" tb_status_t tb_model_create_grouped(tb_model** out, const tb_model_config* cfg, int device, tb_comm* comm,
+                                               uint32_t flags, int64_t group_size) {
+  TB_INJECT("tb_model_create");
+  return create_model(out, cfg, device, comm, flags, group_size);
+}
+
 extern "C" tb_status_t tb_model_destroy(tb_model* m) {
   if (!m) return TB_SUCCESS;
   DeviceGuard guard(m->device);
@@ -816,8 +841,12 @@ extern "C" tb_status_t tb_model_init_synthetic(tb_model* m, uint64_t seed) {
         case 5: row0 = r * m->F; break;
         default: col0 = r * m->F; K = m->Fg; break;
       }
-      TB_TRY(tb::synth_quant_shard(q, s, rows, K, row0, col0, cols, seed, (uint64_t)l * TS_MATS + (uint64_t)mat, 0.02,
-                                   m->stream));
+      if (m->group)
+        TB_TRY(tb::synth_quant_shard_grp(q, s, rows, K, row0, col0, cols, m->group, seed,
+                                         (uint64_t)l * TS_MATS + (uint64_t)mat, 0.02, m->stream));
+      else
+        TB_TRY(tb::synth_quant_shard(q, s, rows, K, row0, col0, cols, seed, (uint64_t)l * TS_MATS + (uint64_t)mat,
+                                     0.02, m->stream));
     }
   }
   TB_TRY(tb_synth_normal_f32(m->embed, m->Vg, m->d, seed, 0x7fff0001ull, 0.02, st));
@@ -838,7 +867,7 @@ extern "C" tb_status_t tb_model_set_linear(tb_model* m, int layer, int mat, cons
   float* s;
   lin_ptr(m, layer, mat, &q, &s);
   TB_CUDA(cudaMemcpy(q, q_host, lin_rows(m, mat) * lin_cols(m, mat), cudaMemcpyHostToDevice));
-  TB_CUDA(cudaMemcpy(s, scale_host, lin_rows(m, mat) * sizeof(float), cudaMemcpyHostToDevice));
+  TB_CUDA(cudaMemcpy(s, scale_host, lin_rows(m, mat) * lin_ng(m, mat) * sizeof(float), cudaMemcpyHostToDevice));
   return TB_SUCCESS;
 }
 
@@ -850,7 +879,8 @@ extern "C" tb_status_t tb_model_get_linear(tb_model* m, int layer, int mat, int8
   lin_ptr(m, layer, mat, &q, &s);
   TB_CUDA(cudaStreamSynchronize(m->stream));
   if (q_host) TB_CUDA(cudaMemcpy(q_host, q, lin_rows(m, mat) * lin_cols(m, mat), cudaMemcpyDeviceToHost));
-  if (scale_host) TB_CUDA(cudaMemcpy(scale_host, s, lin_rows(m, mat) * sizeof(float), cudaMemcpyDeviceToHost));
+  if (scale_host)
+    TB_CUDA(cudaMemcpy(scale_host, s, lin_rows(m, mat) * lin_ng(m, mat) * sizeof(float), cudaMemcpyDeviceToHost));
   return TB_SUCCESS;
 }
 

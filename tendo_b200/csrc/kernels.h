@@ -226,6 +226,10 @@ tb_status_t gemm_f32_nt(float* out, const float* a, const float* b, int M, int N
 // row0.. of a K-column matrix (scales over the full row), columns col0..col0+cols.
 tb_status_t synth_quant_shard(int8_t* q, float* scale, int64_t rows, int64_t K, int64_t row0, int64_t col0,
                               int64_t cols, uint64_t seed, uint64_t stream_id, double std_, cudaStream_t st);
+// The same draw quantized per group of `group` kept columns: scale [rows][cols / group].
+tb_status_t synth_quant_shard_grp(int8_t* q, float* scale, int64_t rows, int64_t K, int64_t row0, int64_t col0,
+                                  int64_t cols, int64_t group, uint64_t seed, uint64_t stream_id, double std_,
+                                  cudaStream_t st);
 tb_status_t synth_normal_rows(float* w, int64_t rows, int64_t K, int64_t row0, uint64_t seed, uint64_t stream_id,
                               double std_, cudaStream_t st);
 

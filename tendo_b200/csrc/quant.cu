@@ -110,6 +110,27 @@ __global__ void __launch_bounds__(kQuantThreads) synth_quant_shard_kernel(int8_t
     q[n * cols + i] = quant_one(ts_normal_f32(key, base + col0 + i, std_), s);
 }
 
+// The per-group form: block (n, j) quantizes kept group j (columns
+// col0 + j g .. col0 + j g + g - 1 of global row row0 + n) with its own scale
+// (nn/quantize.go:126-187); col0 is a multiple of g, so a shard keeps whole
+// groups of the unsharded draw.
+__global__ void __launch_bounds__(kQuantThreads) synth_quant_shard_grp_kernel(int8_t* __restrict__ q,
+                                                                              float* __restrict__ scale, int64_t K,
+                                                                              int64_t row0, int64_t col0,
+                                                                              int64_t cols, int64_t g, uint64_t key,
+                                                                              double std_) {
+  __shared__ float red[kQuantThreads / 32];
+  const int64_t n = blockIdx.x, j = blockIdx.y;
+  const uint64_t base = (uint64_t)((row0 + n) * K + col0 + j * g);
+  float m = 0.0f;
+  for (int64_t i = threadIdx.x; i < g; i += kQuantThreads) m = fmaxf(m, fabsf(ts_normal_f32(key, base + i, std_)));
+  m = block_max_256(m, red);
+  const float s = scale_of(m);
+  if (threadIdx.x == 0) scale[n * (cols / g) + j] = s;
+  for (int64_t i = threadIdx.x; i < g; i += kQuantThreads)
+    q[n * cols + j * g + i] = quant_one(ts_normal_f32(key, base + i, std_), s);
+}
+
 __global__ void synth_normal_offset_kernel(float* __restrict__ w, int64_t total, uint64_t first, uint64_t key,
                                            double std_) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
@@ -191,6 +212,16 @@ tb_status_t synth_quant_shard(int8_t* q, float* scale, int64_t rows, int64_t K, 
   synth_quant_shard_kernel<<<(unsigned)rows, kQuantThreads, 0, st>>>(q, scale, K, row0, col0, cols,
                                                                       ts_key(seed, stream_id), std_);
   return check_launch("synth_quant_shard_kernel");
+}
+
+tb_status_t synth_quant_shard_grp(int8_t* q, float* scale, int64_t rows, int64_t K, int64_t row0, int64_t col0,
+                                  int64_t cols, int64_t group, uint64_t seed, uint64_t stream_id, double std_,
+                                  cudaStream_t st) {
+  if (rows == 0) return TB_SUCCESS;
+  if (group <= 0 || cols % group != 0 || col0 % group != 0 || cols / group > 65535) return TB_ERROR_INVALID_ARGUMENT;
+  synth_quant_shard_grp_kernel<<<dim3((unsigned)rows, (unsigned)(cols / group)), kQuantThreads, 0, st>>>(
+      q, scale, K, row0, col0, cols, group, ts_key(seed, stream_id), std_);
+  return check_launch("synth_quant_shard_grp_kernel");
 }
 
 tb_status_t synth_normal_rows(float* w, int64_t rows, int64_t K, int64_t row0, uint64_t seed, uint64_t stream_id,

@@ -164,3 +164,33 @@ def test_sampled_generation_matches_oracle(oracle, tb, cuda, batch, T, K, P):
     np.testing.assert_array_equal(got, want)
     m.close()
     ref_w.close()
+
+
+@pytest.mark.parametrize("cfg,batch,group", [("GQA", 1, 128), ("GQA", 3, 128), ("GQA64", 1, 128),
+                                             ("GQA64", 12, 256), ("GQA64", 40, 128)])
+def test_grouped_model_greedy(oracle, tb, cuda, cfg, batch, group):
+    """A model quantized per group (QuantizeModel(m, groupSize)): head_dim 32
+    decodes through the per-step grouped DequantizeMatmul, head_dim 64 through
+    the captured step's tcgen05 GEMV with per-group scales (batch 1 included);
+    the 40-sequence prompt takes the grouped tensor-core GEMM.  Tokens equal
+    the grouped oracle's; the synthetic weights and their scales equal the
+    oracle's quantization of the same draws."""
+    c = GQA if cfg == "GQA" else GQA64
+    m = tb.QuantizedModel(c, batch=batch, device=0, group=group)
+    m.init_synthetic(5)
+    ref = oracle.Model(c, batch, seed=5, group=group)
+    for mat in (0, 3, 6):
+        q, s = m.get_linear(1, mat, ref.shape(mat))
+        np.testing.assert_array_equal(q, ref.q(1, mat))
+        np.testing.assert_array_equal(s, ref.scale(1, mat))
+    prompt = np.stack([oracle.synth_tokens(7 + b, 40, c["vocab"]) for b in range(batch)])
+    want, margins = ref.generate_greedy(prompt, 16)
+    got = m.generate_greedy(prompt, 16)
+    np.testing.assert_array_equal(got, want)
+    m.close()
+
+
+def test_grouped_model_rejects_ragged_groups(tb, cuda):
+    """Every Linear's input width must be a whole number of groups."""
+    with pytest.raises(tb.TendoB200Error):
+        tb.QuantizedModel(GQA64, batch=1, device=0, group=384)

@@ -275,3 +275,22 @@ def test_sampler_restatement_known_answers(oracle):
     assert s([0.0, math.log(4.0)], temperature=2.0, r=0.34) == 1
     # r at the very top of [0, 1) still lands on a token
     assert s([5.0, 1.0, 0.0], r=0.9999999) == 2
+
+
+def test_grouped_model_quantizes_the_same_draws_per_group(oracle):
+    """QuantizeModel(m, groupSize): each Linear of the grouped oracle model is
+    nn/quantize.go's per-group quantization of the same synthetic draw as the
+    per-channel model (stream layer * 8 + matrix), and the projection uses the
+    per-group dequantization."""
+    m = oracle.Model(SMALL, 1, seed=3, group=32)
+    for layer, mat in ((0, 0), (1, 3), (1, 6)):
+        N, K = m.shape(mat)
+        w = oracle.synth_normal(3, layer * 8 + mat, N * K, 0.02).reshape(N, K)
+        _, q, s = oracle.quantize(w, 32)
+        np.testing.assert_array_equal(m.q(layer, mat), q)
+        np.testing.assert_array_equal(m.scale(layer, mat), s)
+    toks = np.array([[3, 4, 5, 6]], np.int64)
+    full, _, _ = m.forward(toks)
+    assert np.all(np.isfinite(full))
+    with pytest.raises(MemoryError):
+        oracle.Model(SMALL, 1, seed=3, group=48)  # 64 is not a whole number of groups of 48
