@@ -23,8 +23,9 @@ on the device at L = 8).
 gateup, down, lm_head; tb_model_time_kernel: graph-timed, per layer) on one
 layer of the 7B or 70B width (70B: d 8192, 64 query / 8 kv heads of 128,
 F 28672, KV capacity 4096) at `--batch` sequences whose cache holds
-`--position` rows.  One layer of the 70B width with its cache is about 3 GB
-on the device: the small case for profiling those kernels.
+`--position` rows (with `--group G`, a model quantized per group of G).  One
+layer of the 70B width with its cache is about 3 GB on the device: the small
+case for profiling those kernels.
 """
 from __future__ import annotations
 
@@ -108,18 +109,19 @@ def decode_small(layers, tokens):
 KINDS = ["qkv", "attention", "o", "gateup", "down", "lm_head"]
 
 
-def time_kind(kind, width, batch, position, iters):
+def time_kind(kind, width, batch, position, iters, group=0):
     if width == "70b":
         cfg = dict(vocab=32000, dim=8192, layers=1, heads=64, kv_heads=8, hidden=28672, max_seq=4096,
                    rope_base=500000.0, eps=1e-5)
     else:
         cfg = dict(vocab=32000, dim=4096, layers=1, heads=32, kv_heads=32, hidden=11008, max_seq=2048,
                    rope_base=10000.0, eps=1e-6)
-    qm = tb.QuantizedModel(cfg, batch=batch, device=0)
+    qm = tb.QuantizedModel(cfg, batch=batch, device=0, group=group)
     qm.init_synthetic(0)
     qm.set_position(position)
     us = qm.time_kernel(KINDS.index(kind), iters)
-    print(json.dumps({"kind": kind, "width": width, "batch": batch, "position": position, "us": us}), flush=True)
+    print(json.dumps({"kind": kind, "width": width, "batch": batch, "position": position, "group": group, "us": us}),
+          flush=True)
     qm.close()
 
 
@@ -139,7 +141,7 @@ def main():
     ap.add_argument("--position", type=int, default=2048)
     a = ap.parse_args()
     if a.kind:
-        time_kind(a.kind, a.width, a.batch, a.position, a.iters)
+        time_kind(a.kind, a.width, a.batch, a.position, a.iters, a.group)
     elif a.decode_layers > 0:
         decode_small(a.decode_layers, a.tokens)
     else:
