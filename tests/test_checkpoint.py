@@ -103,14 +103,14 @@ class _FakeModel:
 CFG = dict(vocab=64, dim=32, layers=2, heads=4, kv_heads=2, hidden=48)
 
 
-def _checkpoint(path):
+def _checkpoint(path, group=0):
     rng = np.random.default_rng(1)
     t = {}
     for layer in range(CFG["layers"]):
         for mat, (N, K) in enumerate(ck._shapes(CFG)):
             name = ck._linear_name(layer, mat)
             t[name + ".weight"] = rng.integers(-127, 128, (N, K), dtype=np.int8)
-            t[name + ".weight_scale"] = rng.random(N, dtype=np.float32)
+            t[name + ".weight_scale"] = rng.random((N, K // group) if group else N, dtype=np.float32)
         t[f"model.layers.{layer}.input_layernorm.weight"] = rng.random(CFG["dim"], dtype=np.float32)
         t[f"model.layers.{layer}.post_attention_layernorm.weight"] = rng.random(CFG["dim"], dtype=np.float32)
     t["model.embed_tokens.weight"] = rng.random((CFG["vocab"], CFG["dim"]), dtype=np.float32)
@@ -149,5 +149,35 @@ def test_shape_mismatch_is_rejected(tmp_path):
     p = str(tmp_path / "m.safetensors")
     _checkpoint(p)
     m = _FakeModel(dict(CFG, hidden=64), None)
+    with pytest.raises(ck.CheckpointError):
+        ck.load_model(m, p)
+
+
+@pytest.mark.parametrize("nranks", [1, 2])
+def test_grouped_checkpoint_shards(tmp_path, nranks):
+    """Per-group scales [N, K / group]: a column-parallel rank takes its rows'
+    scales, a row-parallel rank its input columns and the groups over them."""
+    group = 8
+    p = str(tmp_path / "g.safetensors")
+    t = _checkpoint(p, group)
+    for r in range(nranks):
+        m = _FakeModel(CFG, _Comm(r, nranks) if nranks > 1 else None)
+        m.group = group
+        ck.load_model(m, p)
+        for layer in range(CFG["layers"]):
+            for mat, (N, K) in enumerate(ck._shapes(CFG)):
+                q, s = m.lin[(layer, mat)]
+                full_q = t[ck._linear_name(layer, mat) + ".weight"]
+                full_s = t[ck._linear_name(layer, mat) + ".weight_scale"]
+                if ck.LINEARS[mat][1]:
+                    rows = slice(r * N // nranks, (r + 1) * N // nranks)
+                    np.testing.assert_array_equal(q, full_q[rows])
+                    np.testing.assert_array_equal(s, full_s[rows])
+                else:
+                    cols = slice(r * K // nranks, (r + 1) * K // nranks)
+                    groups = slice(r * (K // group) // nranks, (r + 1) * (K // group) // nranks)
+                    np.testing.assert_array_equal(q, full_q[:, cols])
+                    np.testing.assert_array_equal(s, full_s[:, groups])
+    m = _FakeModel(CFG, None)  # a per-channel model rejects per-group scales
     with pytest.raises(ck.CheckpointError):
         ck.load_model(m, p)
