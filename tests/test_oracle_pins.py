@@ -294,3 +294,30 @@ def test_grouped_model_quantizes_the_same_draws_per_group(oracle):
     assert np.all(np.isfinite(full))
     with pytest.raises(MemoryError):
         oracle.Model(SMALL, 1, seed=3, group=48)  # 64 is not a whole number of groups of 48
+
+
+def test_reference_sampling_known_answers(oracle):
+    """models/sampling_test.go: TestGreedy (:66-107), TestFindKthLargest
+    (:185-223) through the top-k mask, TestSortIndicesByValue (:225-238)
+    through the top-p cut, TestSampler_Sample_Deterministic (:240-262)."""
+    rs = [i / 64.0 for i in range(64)] + [1.0 - 2.0 ** -24]
+    # Greedy: first index of the maximum
+    for logits, want in (([5.0, 2.0, 1.0, 0.5], 0), ([1.0, 2.0, 3.0, 10.0], 3), ([1.0, 5.0, 2.0], 1),
+                         ([-1.0, -0.5, -2.0], 1), ([1.0], 0)):
+        assert oracle.argmax(np.array(logits, np.float32)) == want
+    # findKthLargest: k = 1 keeps 9.0 only, k = 3 keeps {4, 5, 9}, k >= len keeps every value
+    vals = [3.0, 1.0, 4.0, 1.0, 5.0, 9.0]
+    assert {oracle.sample(vals, top_k=1, r=r) for r in rs} == {5}
+    assert {oracle.sample(vals, top_k=3, r=r) for r in rs} == {2, 4, 5}
+    short = [3.0, 1.0, 4.0]
+    assert [oracle.sample(short, top_k=10, r=r) for r in rs] == [oracle.sample(short, r=r) for r in rs]
+    # sortIndicesByValue: descending order 1, 3, 4, 2, 0; a top-p cut after the
+    # third keeps exactly indices {1, 3, 4}, after the first only {1}
+    v = np.array([1.0, 5.0, 2.0, 4.0, 3.0], np.float32)
+    p = np.exp(v - v.max()) / np.exp(v - v.max()).sum()
+    order = [1, 3, 4, 2, 0]
+    cut3 = float(p[order[:3]].sum()) - 1e-4
+    assert {oracle.sample(v, top_p=cut3, r=r) for r in rs} == {1, 3, 4}
+    assert {oracle.sample(v, top_p=1e-4, r=r) for r in rs} == {1}
+    # temperature 0.001: always the largest logit
+    assert {oracle.sample([1.0, 5.0, 2.0, 3.0], temperature=0.001, r=r) for r in rs} == {1}
