@@ -329,9 +329,10 @@ TB_API tb_status_t tb_sample_f32(int64_t* tokens, const float* logits, const flo
  * thread) per GPU: NCCL, loaded at run time (libnccl.so.2).  Rank 0 makes the
  * unique id, the caller distributes its bytes to every rank (any channel),
  * and each rank creates its communicator with it (collective: every rank
- * calls it).  Creation also maps every rank's 4 MB peer-exchange region into
- * every other rank (CUDA IPC; up to 8 ranks on one node); allreduces of up to
- * 4 MB then run as one kernel over peer memory, larger ones through NCCL.  If
+ * calls it).  Creation also maps every rank's peer-exchange region (8 MB per
+ * rank of the group) into every other rank (CUDA IPC; up to 8 ranks on one
+ * node); allreduces of up to 2 MB then run as one kernel over peer memory,
+ * larger ones through NCCL.  If
  * any rank cannot map a peer, or TENDO_B200_ALLREDUCE=nccl is set, every
  * rank uses NCCL throughout.  The tb_comm_init / tb_allreduce_sum_f32 pair
  * planned for the reference's cgo layer. */
